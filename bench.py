@@ -1,0 +1,448 @@
+"""Benchmark of the fused Qwen3 layer kernels (HBM GB/s and tokens/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
+
+A step is one pass of the layer's memory-bound kernels over one batch of
+token rows already resident in HBM.  Default workload `prefill4b`: the
+Qwen3-4B-shaped prefill layer, 4096 fp32 tokens per GPU, dim 2560, 32 q / 8 kv
+heads of 128, hidden 9728, positions 0..4095, theta 1e6:
+
+    rmsnorm_q8    x[4096][2560] -> Q8_0 codes + scales            (fused)
+    qk_norm_rope  q[4096][32][128], k[4096][8][128], in place
+    swiglu_q8     hb, hb2 [4096][9728] -> Q8_0 codes + scales     (fused)
+
+Inputs are seeded synthetic data with the workload's shapes and value rules
+(activations N(0,1) with a fixed 1% of channels x20; norm weights 1+N(0,0.1)).
+value = algorithmic bytes (every input read once + every output written once)
+of all ranks / max-over-ranks device time.  Under torchrun each rank runs its own
+batch on its own GPU (token rows are independent: weak scaling, no collective on
+the data path).  Between timed steps L2 is flushed by writing a 256 MiB buffer
+outside the timed events.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+GS = 64
+
+
+# ---------------------------------------------------------------------------- workloads
+class Workload:
+    name = ""
+    tokens = 0
+
+    def kernels(self):              # [(name, algorithmic bytes per launch)]
+        raise NotImplementedError
+
+    def total_bytes(self):
+        return sum(b for _, b in self.kernels())
+
+
+class Prefill4B(Workload):
+    """Qwen3-4B-shaped prefill layer kernels, fp32, T tokens."""
+    name = "prefill4b"
+
+    def __init__(self, tokens=4096, dim=2560, nh=32, nkv=8, hd=128, hidden=9728):
+        self.tokens, self.dim, self.nh, self.nkv, self.hd, self.hidden = tokens, dim, nh, nkv, hd, hidden
+
+    def kernels(self):
+        T, D, H = self.tokens, self.dim, self.hidden
+        rms = T * D * 4 + T * D + T * (D // GS) * 4 + D * 4
+        rope = 2 * T * (self.nh + self.nkv) * self.hd * 4 + T * 4 + 2 * self.hd * 4
+        swi = 2 * T * H * 4 + T * H + T * (H // GS) * 4
+        return [("rmsnorm_q8", rms), ("qk_norm_rope", rope), ("swiglu_q8", swi)]
+
+    def config(self):
+        return {"workload": "Qwen3-4B-shaped prefill layer kernels (rmsnorm_q8 + qk_norm_rope + swiglu_q8)",
+                "tokens_per_gpu": self.tokens, "dim": self.dim, "n_heads": self.nh, "n_kv_heads": self.nkv,
+                "head_dim": self.hd, "hidden": self.hidden, "positions": f"0..{self.tokens - 1}",
+                "rope_theta": 1e6, "input_dtype": "f32"}
+
+    # -- device data
+    def make(self, torch, dev, seed):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        T, D, H = self.tokens, self.dim, self.hidden
+
+        def act(rows, cols):
+            a = torch.randn(rows, cols, device=dev, generator=g)
+            k = max(1, round(cols * 0.01))
+            ch = torch.randperm(cols, device=dev, generator=g)[:k]
+            a[:, ch] *= 20.0
+            return a
+
+        d = {
+            "x": act(T, D),
+            "w": 1.0 + 0.1 * torch.randn(D, device=dev, generator=g),
+            "q": torch.randn(T, self.nh, self.hd, device=dev, generator=g),
+            "k": torch.randn(T, self.nkv, self.hd, device=dev, generator=g),
+            "pos": torch.arange(T, device=dev, dtype=torch.int32),
+            "qn": 1.0 + 0.1 * torch.randn(self.hd, device=dev, generator=g),
+            "kn": 1.0 + 0.1 * torch.randn(self.hd, device=dev, generator=g),
+            "hb": act(T, H),
+            "hb2": act(T, H),
+        }
+        d["xq"] = torch.empty(T, D, dtype=torch.int8, device=dev)
+        d["xs"] = torch.empty(T, D // GS, dtype=torch.float32, device=dev)
+        d["hq"] = torch.empty(T, H, dtype=torch.int8, device=dev)
+        d["hs"] = torch.empty(T, H // GS, dtype=torch.float32, device=dev)
+        return d
+
+    def launch(self, q3, d, stream, events=None):
+        """Enqueues the step; events = list of (start, end) pairs per kernel."""
+        ops = [
+            lambda: q3.rmsnorm_q8(d["x"], d["w"], q=d["xq"], s=d["xs"], stream=stream),
+            lambda: q3.qk_norm_rope(d["q"], d["k"], d["pos"], d["qn"], d["kn"], stream=stream),
+            lambda: q3.swiglu_q8(d["hb"], d["hb2"], q=d["hq"], s=d["hs"], stream=stream),
+        ]
+        for i, op in enumerate(ops):
+            if events is not None:
+                events[i][0].record(stream)
+            op()
+            if events is not None:
+                events[i][1].record(stream)
+        return len(ops)
+
+    # -- host (end-to-end) data: inputs copied in, outputs copied out each step
+    h2d_keys = ("x", "q", "k", "pos", "hb", "hb2")
+    d2h_keys = ("xq", "xs", "q", "k", "hq", "hs")
+
+    # -- CPU oracle on a token sample
+    def cpu_step(self, oracle, np, sample, threads, rng):
+        if not hasattr(self, "_cpu"):
+            D, H = self.dim, self.hidden
+            x = rng.standard_normal((sample, D), dtype=np.float32)
+            w = (1 + 0.1 * rng.standard_normal(D)).astype(np.float32)
+            q = rng.standard_normal((sample, self.nh, self.hd), dtype=np.float32)
+            k = rng.standard_normal((sample, self.nkv, self.hd), dtype=np.float32)
+            pos = np.arange(sample, dtype=np.int32)
+            qn = (1 + 0.1 * rng.standard_normal(self.hd)).astype(np.float32)
+            kn = (1 + 0.1 * rng.standard_normal(self.hd)).astype(np.float32)
+            hb = rng.standard_normal((sample, H), dtype=np.float32)
+            hb2 = rng.standard_normal((sample, H), dtype=np.float32)
+            self._cpu = (x, w, q, k, pos, qn, kn, hb, hb2)
+        x, w, q, k, pos, qn, kn, hb, hb2 = self._cpu
+        oracle.rows_rmsnorm_q8(x, w, threads=threads)
+        oracle.rows_qk_norm_rope(q, k, pos, qn, kn, threads=threads)
+        oracle.rows_swiglu_q8(hb, hb2, threads=threads)
+
+    def bytes_for_tokens(self, n):
+        return self.total_bytes() * n / self.tokens
+
+
+WORKLOADS = {"prefill4b": Prefill4B}
+
+
+# ---------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML every 10 ms."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+        0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index):
+        self.index, self.samples, self.reasons, self.max_mhz = index, [], set(), None
+        self._stop = threading.Event()
+        self._t = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML unavailable: report nothing rather than guess
+            self.err = str(e)
+
+    def _run(self):
+        nv = self.nv
+        while not self._stop.is_set():
+            try:
+                self.samples.append(nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM))
+                r = nv.nvmlDeviceGetCurrentClocksEventReasons(self.h) if hasattr(
+                    nv, "nvmlDeviceGetCurrentClocksEventReasons") else nv.nvmlDeviceGetCurrentClocksThrottleReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.01)
+
+    def start(self):
+        if self.ok:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+
+    def stop(self):
+        if self._t:
+            self._stop.set()
+            self._t.join()
+        if not self.ok or not self.samples:
+            return None
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples), "source": "nvml 10 ms"}
+
+
+# ---------------------------------------------------------------------------- helpers
+def measured_hbm_peak():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def profiled_traffic(workload, kernel):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, or None."""
+    p = os.path.join(ROOT, "profiles", "traffic.json")
+    try:
+        with open(p) as f:
+            return json.load(f)[workload][kernel]["dram_bytes_per_launch"]
+    except Exception:
+        return None
+
+
+def cpu_baseline(workload, seconds=10.0):
+    import numpy as np
+    from oracle.oracle import Oracle
+    o = Oracle()
+    threads = os.cpu_count() or 1
+    sample = 128
+    rng = np.random.default_rng(0)
+    workload.cpu_step(o, np, sample, threads, rng)          # warm up (allocations, page faults)
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        workload.cpu_step(o, np, sample, threads, rng)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    gbs = workload.bytes_for_tokens(sample) * n / el / 1e9
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
+            "sample": f"{n} passes over {sample} tokens of the same step ({el:.1f} s), oracle/q3_oracle.c "
+                      f"(the reference's CPU arithmetic), OpenMP over rows",
+            "tokens_per_s": round(sample * n / el, 1)}
+
+
+# ---------------------------------------------------------------------------- reference arm
+def run_reference(args, wl):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    import numpy as np
+    from oracle.oracle import Oracle, reference_path
+    o = Oracle()
+    threads = os.cpu_count() or 1
+    sample = 32
+    rng = np.random.default_rng(0)
+    kind = "port"
+    use_ref = os.path.exists(reference_path())
+    ref_rows = None
+    if use_ref:
+        try:
+            from oracle.oracle import ReferenceRows
+            ref_rows = ReferenceRows()
+            kind = "reference"
+        except Exception:
+            ref_rows = None
+
+    def step():
+        if ref_rows is not None:
+            ref_rows.step(wl, sample, threads)
+        else:
+            wl.cpu_step(o, np, sample, threads, rng)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    el = time.perf_counter() - t0
+    per_step = wl.bytes_for_tokens(sample)
+    val = per_step * args.steps / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": dict(wl.config(), sample_tokens_per_step=sample),
+        "tokens_per_s": round(sample * args.steps / el, 2),
+        "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": kind,
+                         "sample": f"{sample} tokens per step of the same workload on the host cores"},
+        "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+METRIC = "fused layer-kernel HBM GB/s & tokens/s at 1/2/4/8 B200; % of HBM roofline"
+
+
+# ---------------------------------------------------------------------------- our arm
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="prefill4b")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    wl = WORKLOADS[args.workload]()
+
+    if args.impl == "reference":
+        return run_reference(args, wl)
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+
+    from metalqwen3_b200.q3cu import Q3CU
+    q3 = Q3CU(local)
+    stream = torch.cuda.Stream(device=dev)
+    d = wl.make(torch, dev, seed=1234 + rank)
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    nk = len(wl.kernels())
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+
+    # warm-up
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            wl.launch(q3, d, stream)
+            flush.fill_(1)
+    stream.synchronize()
+    if q3.device_status(stream) != 0:
+        raise RuntimeError("device status set during warm-up")
+
+    clocks = ClockSampler(local)
+    clocks.start()
+    ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nk)] for _ in range(args.steps)]
+    barrier()
+    torch.cuda.synchronize(dev)
+    launches = 0
+    with torch.cuda.stream(stream):
+        for i in range(args.steps):
+            launches += wl.launch(q3, d, stream, events=ev[i])
+            flush.fill_(1)                      # outside the events: L2 cold for the next step
+    stream.synchronize()
+    torch.cuda.synchronize(dev)
+    barrier()
+    clk = clocks.stop()
+
+    per_kernel = [[ev[i][k][0].elapsed_time(ev[i][k][1]) for i in range(args.steps)] for k in range(nk)]
+    step_ms = [sum(per_kernel[k][i] for k in range(nk)) for i in range(args.steps)]
+    total_ms = sum(step_ms)
+    if world > 1:
+        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+    if q3.device_status(stream) != 0:
+        raise RuntimeError("device status set during the timed region")
+
+    # ---- end to end: host buffers, copies inside the timed region ----------
+    hin = {k: d[k].detach().to("cpu").pin_memory() for k in wl.h2d_keys}
+    hout = {k: torch.empty(d[k].shape, dtype=d[k].dtype).pin_memory() for k in wl.d2h_keys}
+    h2d = sum(t.numel() * t.element_size() for t in hin.values())
+    d2h = sum(t.numel() * t.element_size() for t in hout.values())
+
+    def e2e_step():
+        with torch.cuda.stream(stream):
+            for k, t in hin.items():
+                d[k].copy_(t, non_blocking=True)
+            wl.launch(q3, d, stream)
+            for k, t in hout.items():
+                t.copy_(d[k], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    stream.synchronize()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    stream.synchronize()
+    e2e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+        barrier()
+
+    # ---- report ---------------------------------------------------------------
+    if rank == 0:
+        step_bytes = wl.total_bytes()
+        ms_per_step = total_ms / args.steps
+        gbs = world * step_bytes * args.steps / (total_ms / 1e3) / 1e9
+        kern = {}
+        for k, (name, b) in enumerate(wl.kernels()):
+            avg = statistics.mean(per_kernel[k])
+            kern[name] = {"bytes": b, "avg_us": round(avg * 1e3, 3), "gbs": round(b / (avg / 1e3) / 1e9, 1)}
+        peak, peak_kind = measured_hbm_peak()
+        dom_name, dom_bytes = max(wl.kernels(), key=lambda kb: kb[1])
+        dom_avg_s = statistics.mean(per_kernel[[n for n, _ in wl.kernels()].index(dom_name)]) / 1e3
+        achieved = dom_bytes / dom_avg_s / 1e9
+        line = {
+            "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": dict(wl.config(), parallelism=f"token rows x{world} (weak)",
+                           l2="flushed between timed steps (256 MiB write outside the events); "
+                              "step working set 582 MB > 126 MB L2"),
+            "tokens_per_s": round(world * wl.tokens * args.steps / (total_ms / 1e3), 1),
+            "hbm_frac": round(gbs / world / peak, 4),
+            "kernels": kern,
+            "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": peak,
+                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                         else "fallback 6650 GB/s", "unit": "GB/s", "frac": round(achieved / peak, 4),
+                         "traffic": profiled_traffic(wl.name, dom_name),
+                         "algorithmic_bytes_per_launch": dom_bytes},
+            "e2e": {"value": round(world * step_bytes * args.e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
+                    "path": "pinned host inputs -> cudaMemcpyAsync H2D -> q3cu C ABI kernels -> D2H, per step"},
+            "gpu_launches": launches,
+            "clocks": clk,
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
+        print(json.dumps(line), flush=True)
+
+    q3.close()
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

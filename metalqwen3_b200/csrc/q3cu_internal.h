@@ -1,0 +1,43 @@
+// q3cu_internal.h -- launchers shared between the kernel files and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "q3cu.h"
+#include "q3cu_device.cuh"
+
+namespace q3 {
+
+// Raises a kernel's dynamic shared-memory limit once per (device, slot):
+// `slot` (< 32) names the kernel instantiation.
+cudaError_t ensure_smem_attr(const void *kernel, size_t bytes, int slot);
+
+// Every launcher enqueues on `stream`, allocates nothing and returns the
+// launch error.  `sms` is the device's multiprocessor count (grid sizing).
+cudaError_t launch_quantize_q8(const void *x, q3cu_dtype dt, int64_t elems, int8_t *q, float *s,
+                               cudaStream_t stream, int sms);
+cudaError_t launch_dequantize_q8(const int8_t *q, const float *s, int64_t n, float *x, cudaStream_t stream,
+                                 int sms);
+cudaError_t launch_embed_gather(const int8_t *tq, const float *ts, int vocab, int dim, const int32_t *ids,
+                                int64_t n, float *out, int8_t *oq, float *os, uint32_t *status,
+                                cudaStream_t stream, int sms);
+
+cudaError_t launch_rmsnorm(const void *x, q3cu_dtype dt, const float *w, int64_t rows, int dim, float eps,
+                           void *out, int8_t *q, float *s, uint32_t *status, cudaStream_t stream, int sms);
+
+cudaError_t launch_rmsnorm_padded(const float *x, const float *w, int size, int padded, float *out, uint32_t *status,
+                                  cudaStream_t stream, int sms);
+
+struct InvFreq { float v[64]; };
+cudaError_t launch_qk_norm_rope(void *q, void *k, q3cu_dtype dt, const int32_t *pos, int64_t rows, int n_heads,
+                                int n_kv, const float *q_norm, const float *k_norm, const InvFreq &inv_freq,
+                                float eps, uint32_t *status, cudaStream_t stream, int sms);
+
+cudaError_t launch_swiglu(const void *hb, const void *hb2, q3cu_dtype dt, int64_t elems, void *out, int8_t *q,
+                          float *s, cudaStream_t stream, int sms);
+
+cudaError_t launch_softmax_rows(float *x, const int64_t *off, const int32_t *len, int64_t rows,
+                                cudaStream_t stream, int sms);
+
+}  // namespace q3

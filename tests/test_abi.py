@@ -1,0 +1,84 @@
+"""The C ABI library: loads, exports every entry point that include/q3cu.h
+declares, and validates arguments on the host (no kernel is launched here)."""
+import ctypes as C
+import os
+import struct
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from metalqwen3_b200.build import build_library, library_path
+    if not os.path.exists(library_path()):
+        build_library()
+    from metalqwen3_b200.q3cu import load_library
+    return load_library()
+
+
+def test_exports_every_declared_symbol(lib):
+    from metalqwen3_b200.q3cu import header_functions
+    names = header_functions()
+    assert len(names) >= 20
+    missing = [n for n in names if not hasattr(lib, n)]
+    assert not missing, f"declared in include/q3cu.h but not exported: {missing}"
+
+
+def test_cudacontext_symbols_exported():
+    import subprocess
+    from metalqwen3_b200.build import library_path
+    syms = subprocess.run(["nm", "-D", "-C", library_path()], capture_output=True, text=True).stdout
+    for m in ("CudaContext::executeRMSNorm", "CudaContext::executeSoftmax", "CudaContext::executeSwiGLU",
+              "CudaContext::executeRoPE", "CudaContext::executeQuantize", "CudaContext::executeEmbedding",
+              "CudaContext::initialize", "CudaContext::cleanup"):
+        assert m in syms, m
+
+
+def test_status_strings(lib):
+    for s in range(11):
+        assert lib.q3cu_status_string(s)
+    assert lib.q3cu_version() >= 100
+
+
+def test_null_context_is_rejected(lib):
+    # every op checks the context before touching CUDA
+    assert lib.q3cu_rmsnorm(None, None, 0, None, 1, 64, 1e-6, None, None) == 7
+    assert lib.q3cu_rmsnorm_q8(None, None, 0, None, 1, 64, 1e-6, None, None, None) == 7
+    assert lib.q3cu_swiglu_q8(None, None, None, 0, 1, 64, None, None, None) == 7
+    assert lib.q3cu_softmax_rows(None, None, None, None, 1, None) == 7
+    assert lib.q3cu_quantize_q8(None, None, 0, 1, 64, None, None, None) == 7
+    assert lib.q3cu_embed_gather(None, None, None, 1, 64, None, 1, None, None, None, None) == 7
+    assert lib.q3cu_execute_rmsnorm(None, None, None, None, 4) == 7
+    assert lib.q3cu_destroy(None) == 7
+    assert lib.q3cu_is_initialized(None) == 0
+    assert b"context" in lib.q3cu_last_error_string()
+
+
+def header(**kw):
+    f = dict(magic=0x616A6331, version=1, dim=1024, hidden=3072, n_layers=28, n_heads=16, n_kv=8, vocab=151936,
+             seq_len=64, head_dim=128, shared=1, gs=64)
+    f.update(kw)
+    return struct.pack("Iiiiiiiiiiii", f["magic"], f["version"], f["dim"], f["hidden"], f["n_layers"], f["n_heads"],
+                       f["n_kv"], f["vocab"], f["seq_len"], f["head_dim"], f["shared"], f["gs"]) + b"\0" * 208
+
+
+def test_check_header(lib):
+    cfg = (C.c_int32 * 12)()
+    h = header()
+    assert lib.q3cu_check_header(h, len(h), cfg) == 0
+    assert cfg[2] == 1024 and cfg[7] == 151936
+    for bad in (header(magic=0x12345678), header(version=2), header(gs=32), header(n_kv=3)):
+        assert lib.q3cu_check_header(bad, len(bad), None) == 10
+    assert lib.q3cu_check_header(h, 20, None) == 10
+    assert lib.q3cu_check_header(None, 0, None) == 1
+
+
+def test_init_without_gpu_reports_device_error(lib):
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("a GPU is present")
+    h = C.c_void_p()
+    assert lib.q3cu_init(0, C.byref(h)) == 9
+    assert not h.value

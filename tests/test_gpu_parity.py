@@ -1,0 +1,427 @@
+"""Parity of the CUDA kernels (through the C ABI) with the CPU oracle.
+
+Contract (from the reference, src/cpu/qwen3_original.c):
+  * Q8_0 codes / scales and the embedding dequant: bit-exact;
+  * RMSNorm (incl. the per-head QK-norm) and SwiGLU float outputs: bit-exact
+    for f32 (sequential sum of squares, libm-identical expf);
+  * RoPE and softmax: within RTOL = 1e-5, ATOL = 1e-6 (f32), 1e-2 relative for
+    bf16 inputs; softmax is also held to "no further from the oracle than the
+    oracle is from a binary64 softmax, plus the tolerance".
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 1e-5, 1e-6
+BF16_RTOL = 1e-2
+
+
+def dev(a):
+    import torch
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if a.dtype == np.uint16:
+        t = t.view(torch.bfloat16)
+    return t.cuda()
+
+
+def host(t):
+    import torch
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).cpu().numpy().view(np.uint16)
+    return t.cpu().numpy()
+
+
+def bits(a):
+    return np.ascontiguousarray(a).view(np.uint32 if a.dtype == np.float32 else np.uint8)
+
+
+def to_bf16(a, oracle):
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    r = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    return r
+
+
+def bf16_to_f32(u):
+    return (u.astype(np.uint32) << 16).view(np.float32)
+
+
+def activations(rng, rows, dim, outlier_frac=0.01, scale=20.0):
+    """N(0,1) with a fixed 1% channel set scaled x20 (the prefill workloads' rule)."""
+    x = rng.standard_normal((rows, dim), dtype=np.float32)
+    k = max(1, int(round(dim * outlier_frac)))
+    ch = np.random.default_rng(1234).choice(dim, size=k, replace=False)
+    x[:, ch] *= np.float32(scale)
+    return x
+
+
+def assert_q8_equal(qg, sg, qo, so):
+    qg, sg = host(qg), host(sg)
+    assert qg.shape == qo.shape and sg.shape == so.shape
+    nq = int((qg != qo).sum())
+    ns = int((sg.view(np.uint32) != so.view(np.uint32)).sum())
+    assert nq == 0 and ns == 0, f"{nq} code and {ns} scale mismatches"
+
+
+# --------------------------------------------------------------------------- quantize
+@pytest.mark.parametrize("rows,n", [(1, 64), (3, 128), (7, 2560), (33, 9728), (4096, 2560)])
+def test_quantize_f32(q3, oracle, rows, n):
+    rng = np.random.default_rng(rows * 7 + n)
+    x = activations(rng, rows, n)
+    qg, sg = q3.quantize_q8(dev(x))
+    qo, so = oracle.rows_quantize(x, threads=8)
+    assert_q8_equal(qg, sg, qo, so)
+
+
+def test_quantize_edge_groups(q3, oracle):
+    md = np.float32(1.4e-45)
+    x = np.zeros((1, 64 * 12), np.float32)
+    x[0, 64:128] = np.arange(64, dtype=np.float32) * md          # denormal group
+    x[0, 128:192] = 190 * md; x[0, 130] = -190 * md                 # codes wrap past 127
+    x[0, 192:256] = 63 * md                                        # scale underflows to 0
+    x[0, 256] = np.inf; x[0, 320] = np.nan; x[0, 384] = -np.inf; x[0, 385] = 1.0
+    x[0, 448:512] = -0.0
+    x[0, 512:576] = np.linspace(-127.0, 127.0, 64, dtype=np.float32)   # exact .5 quotients
+    x[0, 576:640] = (np.arange(64, dtype=np.float32) + 0.5)
+    x[0, 640:704] = np.float32(3.4e38) * np.sign(np.arange(64) - 31.5).astype(np.float32)
+    qg, sg = q3.quantize_q8(dev(x))
+    qo, so = oracle.rows_quantize(x)
+    assert_q8_equal(qg, sg, qo, so)
+
+
+@pytest.mark.parametrize("rows,n", [(5, 256), (256, 4096)])
+def test_quantize_bf16(q3, oracle, rows, n):
+    rng = np.random.default_rng(5)
+    xb = to_bf16(activations(rng, rows, n), oracle)
+    qg, sg = q3.quantize_q8(dev(xb))
+    qo, so = oracle.rows_quantize(xb)
+    assert_q8_equal(qg, sg, qo, so)
+
+
+def test_dequantize(q3, oracle):
+    rng = np.random.default_rng(3)
+    q = rng.integers(-127, 128, size=64 * 1000, dtype=np.int8)
+    s = np.abs(0.01 * rng.standard_normal(1000)).astype(np.float32)
+    g = host(q3.dequantize_q8(dev(q), dev(s)))
+    assert np.array_equal(bits(g), bits(oracle.dequantize(q, s)))
+
+
+# --------------------------------------------------------------------------- rmsnorm
+@pytest.mark.parametrize("rows,dim", [(1, 64), (3, 128), (7, 1024), (300, 2560), (5, 4096), (9, 5120), (2, 1028)])
+def test_rmsnorm_f32_bitexact(q3, oracle, rows, dim):
+    rng = np.random.default_rng(rows + dim)
+    x = activations(rng, rows, dim)
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    g = host(q3.rmsnorm(dev(x), dev(w)))
+    o = oracle.rows_rmsnorm(x, w, threads=8)
+    assert np.array_equal(bits(g), bits(o)), f"max abs diff {np.abs(g - o).max()}"
+
+
+def test_rmsnorm_in_place(q3, oracle):
+    rng = np.random.default_rng(11)
+    x = activations(rng, 17, 2560)
+    w = (1 + 0.1 * rng.standard_normal(2560)).astype(np.float32)
+    t = dev(x)
+    q3.rmsnorm(t, dev(w), out=t)
+    assert np.array_equal(bits(host(t)), bits(oracle.rows_rmsnorm(x, w)))
+
+
+@pytest.mark.parametrize("rows,dim", [(1, 1024), (37, 2560), (4096, 2560)])
+def test_rmsnorm_q8_f32(q3, oracle, rows, dim):
+    rng = np.random.default_rng(rows)
+    x = activations(rng, rows, dim)
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    qg, sg = q3.rmsnorm_q8(dev(x), dev(w))
+    qo, so = oracle.rows_rmsnorm_q8(x, w, threads=8)
+    assert_q8_equal(qg, sg, qo, so)
+
+
+@pytest.mark.parametrize("rows,dim", [(3, 512), (256, 4096), (2048, 5120)])
+def test_rmsnorm_bf16(q3, oracle, rows, dim):
+    rng = np.random.default_rng(dim)
+    xb = to_bf16(activations(rng, rows, dim), oracle)
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    qg, sg = q3.rmsnorm_q8(dev(xb), dev(w))
+    qo, so = oracle.rows_rmsnorm_q8(xb, w, threads=8)
+    assert_q8_equal(qg, sg, qo, so)
+    g = host(q3.rmsnorm(dev(xb), dev(w)))
+    o = oracle.rows_rmsnorm(xb, w, threads=8)
+    np.testing.assert_allclose(bf16_to_f32(g), bf16_to_f32(o), rtol=BF16_RTOL)
+    assert np.array_equal(g, o)      # the float result is exact, so is its bf16 rounding
+
+
+def test_rmsnorm_rejects_bad_shapes(q3):
+    import torch
+    from metalqwen3_b200.q3cu import Q3Error
+    x = torch.zeros((2, 100), device="cuda")
+    w = torch.ones(100, device="cuda")
+    with pytest.raises(Q3Error) as e:
+        q3.rmsnorm_q8(x, w)
+    assert e.value.status == 3                       # ERR_GROUP
+    x = torch.zeros((2, 130), device="cuda")
+    with pytest.raises(Q3Error) as e:
+        q3.rmsnorm(x, torch.ones(130, device="cuda"))
+    assert e.value.status == 2                       # ERR_ALIGN (row bytes not a multiple of 16)
+
+
+# --------------------------------------------------------------------------- qk-norm + rope
+@pytest.mark.parametrize("rows,nh,nkv,posmax", [(1, 16, 8, 37), (5, 32, 8, 4096), (4096, 32, 8, 4096), (64, 40, 8, 32768)])
+def test_qk_norm_rope_f32(q3, oracle, rows, nh, nkv, posmax):
+    rng = np.random.default_rng(rows + nh)
+    qh = rng.standard_normal((rows, nh, 128), dtype=np.float32)
+    kh = rng.standard_normal((rows, nkv, 128), dtype=np.float32)
+    pos = (np.arange(rows) % posmax).astype(np.int32) if rows >= posmax else rng.integers(0, posmax, rows).astype(np.int32)
+    if rows > 1:
+        pos[0], pos[-1] = 0, posmax - 1
+    qn = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    tq, tk = dev(qh), dev(kh)
+    q3.qk_norm_rope(tq, tk, dev(pos), dev(qn), dev(kn))
+    qo, ko = oracle.rows_qk_norm_rope(qh, kh, pos, qn, kn, threads=8)
+    np.testing.assert_allclose(host(tq), qo, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(host(tk), ko, rtol=RTOL, atol=ATOL)
+
+
+def test_qk_norm_only_is_bitexact_at_pos0(q3, oracle):
+    """At pos 0 the rotation is the identity (cos 0 = 1, sin 0 = 0), so the
+    output is the QK-RMSNorm alone, which must match bit for bit."""
+    rng = np.random.default_rng(2)
+    qh = rng.standard_normal((9, 32, 128), dtype=np.float32)
+    kh = rng.standard_normal((9, 8, 128), dtype=np.float32)
+    pos = np.zeros(9, np.int32)
+    qn = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    tq, tk = dev(qh), dev(kh)
+    q3.qk_norm_rope(tq, tk, dev(pos), dev(qn), dev(kn))
+    qo, ko = oracle.rows_qk_norm_rope(qh, kh, pos, qn, kn)
+    assert np.array_equal(bits(host(tq)), bits(qo)) and np.array_equal(bits(host(tk)), bits(ko))
+
+
+@pytest.mark.parametrize("rows,nh", [(7, 32), (256, 32)])
+def test_qk_norm_rope_bf16(q3, oracle, rows, nh):
+    rng = np.random.default_rng(rows)
+    qh = to_bf16(rng.standard_normal((rows, nh, 128), dtype=np.float32), oracle)
+    kh = to_bf16(rng.standard_normal((rows, 8, 128), dtype=np.float32), oracle)
+    pos = rng.integers(0, 32768, rows).astype(np.int32)
+    qn = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    tq, tk = dev(qh), dev(kh)
+    q3.qk_norm_rope(tq, tk, dev(pos), dev(qn), dev(kn))
+    qo, ko = oracle.rows_qk_norm_rope(qh, kh, pos, qn, kn)
+    np.testing.assert_allclose(bf16_to_f32(host(tq)), bf16_to_f32(qo), rtol=BF16_RTOL, atol=1e-2)
+    np.testing.assert_allclose(bf16_to_f32(host(tk)), bf16_to_f32(ko), rtol=BF16_RTOL, atol=1e-2)
+
+
+# --------------------------------------------------------------------------- swiglu
+@pytest.mark.parametrize("rows,hidden", [(1, 64), (3, 3072), (64, 9728), (4096, 9728)])
+def test_swiglu_q8_f32(q3, oracle, rows, hidden):
+    rng = np.random.default_rng(hidden + rows)
+    hb = activations(rng, rows, hidden)
+    hb2 = activations(rng, rows, hidden)
+    qg, sg = q3.swiglu_q8(dev(hb), dev(hb2))
+    qo, so = oracle.rows_swiglu_q8(hb, hb2, threads=8)
+    assert_q8_equal(qg, sg, qo, so)
+
+
+@pytest.mark.parametrize("rows,hidden", [(1, 4), (3, 3072), (64, 10240)])
+def test_swiglu_f32_bitexact(q3, oracle, rows, hidden):
+    rng = np.random.default_rng(hidden)
+    hb = (4 * rng.standard_normal((rows, hidden))).astype(np.float32)
+    hb2 = rng.standard_normal((rows, hidden)).astype(np.float32)
+    t = dev(hb)
+    q3.swiglu(t, dev(hb2))
+    assert np.array_equal(bits(host(t)), bits(oracle.rows_swiglu(hb, hb2, threads=8)))
+
+
+def test_swiglu_expf_sweep(q3, oracle):
+    """hb swept over 2^24 binary32 values spanning the whole exponent range
+    (incl. |hb| > 88, denormals, +-inf): SwiGLU outputs equal the oracle's bit
+    for bit, i.e. the device expf returns the host libm's bits there."""
+    u = (np.arange(1 << 24, dtype=np.uint64) * 256 + 17).astype(np.uint32)
+    hb = u.view(np.float32).copy()
+    hb[~np.isfinite(hb)] = 0.5
+    hb[:4] = [np.inf, -np.inf, np.float32(88.72283), np.float32(-103.97)]
+    hb = hb.reshape(-1, 4096)
+    hb2 = np.ones_like(hb)
+    t = dev(hb)
+    q3.swiglu(t, dev(hb2))
+    g, o = host(t), oracle.rows_swiglu(hb, hb2, threads=8)
+    same = (bits(g) == bits(o)) | (np.isnan(g) & np.isnan(o))
+    assert same.all(), f"{int((~same).sum())} mismatches"
+
+
+@pytest.mark.parametrize("rows,hidden", [(3, 512), (256, 12288)])
+def test_swiglu_q8_bf16(q3, oracle, rows, hidden):
+    rng = np.random.default_rng(hidden)
+    hb = to_bf16(activations(rng, rows, hidden), oracle)
+    hb2 = to_bf16(activations(rng, rows, hidden), oracle)
+    qg, sg = q3.swiglu_q8(dev(hb), dev(hb2))
+    qo, so = oracle.rows_swiglu_q8(hb, hb2, threads=8)
+    assert_q8_equal(qg, sg, qo, so)
+
+
+# --------------------------------------------------------------------------- softmax
+def softmax_f64(x, off, lens):
+    out = np.empty(x.size, np.float64)
+    for o_, n in zip(off, lens):
+        r = x[o_:o_ + n].astype(np.float64)
+        m = max(0.0, r.max()) if n else 0.0
+        e = np.exp(r - m)
+        out[o_:o_ + n] = e / e.sum()
+    return out
+
+
+def check_softmax(g, o, ref64, off, lens):
+    nan_o = np.isnan(o)
+    assert np.array_equal(np.isnan(g), nan_o)
+    g, o, r = g[~nan_o], o[~nan_o], ref64[~nan_o]
+    tol = ATOL + RTOL * np.abs(r)
+    assert (np.abs(g - r) <= tol).all(), "GPU softmax outside tolerance of the binary64 softmax"
+    assert (np.abs(g - o) <= np.abs(o - r) + tol).all(), "GPU softmax further from the oracle than allowed"
+
+
+@pytest.mark.parametrize("lens", [
+    [1, 2, 3, 38, 511, 512, 513, 1024, 1025, 2048, 2049, 4096, 4097, 16384, 32768],
+    list(range(1, 300, 7)),
+])
+def test_softmax_ragged(q3, oracle, lens):
+    rng = np.random.default_rng(len(lens))
+    lens = np.array(lens, np.int32)
+    gaps = rng.integers(0, 5, lens.size)                # unaligned row starts
+    off = np.concatenate([[0], np.cumsum(lens + gaps)[:-1]]).astype(np.int64) + 1
+    total = int(off[-1] + lens[-1] + 3)
+    x = (2.0 * rng.standard_normal(total)).astype(np.float32)
+    t = dev(x)
+    q3.softmax_rows(t, dev(off), dev(lens))
+    o = oracle.rows_softmax(x, off, lens)
+    g = host(t)
+    check_softmax(g, o, softmax_f64(x, off, lens), off, lens)
+    # bytes outside the rows are untouched
+    mask = np.ones(total, bool)
+    for a, n in zip(off, lens):
+        mask[a:a + n] = False
+    assert np.array_equal(bits(g[mask]), bits(x[mask]))
+
+
+def test_softmax_max_starts_at_zero(q3, oracle):
+    """All-negative rows: the reference's max is 0, not max(x); a row with
+    every score below -104 underflows to 0/0 = NaN in the reference."""
+    x = np.concatenate([np.full(100, -3.0, np.float32), np.full(50, -200.0, np.float32),
+                        np.linspace(-90, -80, 20, dtype=np.float32)])
+    lens = np.array([100, 50, 20], np.int32)
+    off = np.array([0, 100, 150], np.int64)
+    t = dev(x)
+    q3.softmax_rows(t, dev(off), dev(lens))
+    g, o = host(t), oracle.rows_softmax(x, off, lens)
+    assert np.isnan(o[100:150]).all() and np.isnan(g[100:150]).all()
+    np.testing.assert_allclose(g[:100], o[:100], rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(g[150:], o[150:], rtol=RTOL, atol=ATOL)
+
+
+def test_softmax_decode_batch(q3, oracle):
+    """256 tokens x 32 heads, row length pos+1 with pos uniform in 0..32767,
+    scores N(0, sigma=2): the batched-decode workload."""
+    rng = np.random.default_rng(0)
+    pos = rng.integers(0, 32768, 256)
+    lens = np.repeat(pos + 1, 32).astype(np.int32)
+    off = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+    x = (2.0 * rng.standard_normal(int(lens.sum()))).astype(np.float32)
+    t = dev(x)
+    q3.softmax_rows(t, dev(off), dev(lens))
+    o = oracle.rows_softmax(x, off, lens, threads=8)
+    sel = rng.choice(lens.size, 64, replace=False)     # binary64 reference on a row sample
+    g = host(t)
+    for r in sel:
+        a, n = off[r], lens[r]
+        check_softmax(g[a:a + n], o[a:a + n], softmax_f64(x[a:a + n], [0], [n]), [0], [n])
+    np.testing.assert_allclose(g, o, rtol=1e-4, atol=ATOL)
+
+
+# --------------------------------------------------------------------------- embedding
+@pytest.mark.parametrize("dim", [64, 1024, 4096, 4160])
+def test_embed_gather(q3, oracle, dim):
+    rng = np.random.default_rng(dim)
+    vocab = 3000
+    tq = rng.integers(-127, 128, size=(vocab, dim), dtype=np.int8)
+    ts = np.abs(0.01 * rng.standard_normal((vocab, dim // 64))).astype(np.float32)
+    ids = np.minimum(rng.zipf(1.1, 5000) - 1, vocab - 1).astype(np.int32)
+    out, oq, os_ = q3.embed_gather(dev(tq), dev(ts), dev(ids))
+    ro, rq, rs, bad = oracle.rows_embed(tq, ts, ids, threads=8)
+    assert bad == 0
+    assert np.array_equal(bits(host(out)), bits(ro))
+    assert_q8_equal(oq, os_, rq, rs)
+    f_only, _, _ = q3.embed_gather(dev(tq), dev(ts), dev(ids), want_q8=False)
+    assert np.array_equal(bits(host(f_only)), bits(ro))
+    _, q_only, s_only = q3.embed_gather(dev(tq), dev(ts), dev(ids), want_f32=False)
+    assert_q8_equal(q_only, s_only, rq, rs)
+
+
+def test_embed_bad_ids_flag_and_skip(q3, oracle):
+    import torch
+    rng = np.random.default_rng(9)
+    tq = rng.integers(-127, 128, size=(100, 256), dtype=np.int8)
+    ts = np.abs(0.01 * rng.standard_normal((100, 4))).astype(np.float32)
+    ids = np.array([0, 5, -1, 99, 100, 7, 1 << 30], np.int32)
+    assert q3.device_status() == 0
+    out = torch.full((7, 256), 7.0, device="cuda")
+    q3.embed_gather(dev(tq), dev(ts), dev(ids), want_q8=False, out=out)
+    flags = q3.device_status()
+    assert flags & 0x1
+    assert q3.device_status() == 0                    # reading clears the word
+    g = host(out)
+    ro, _, _, bad = oracle.rows_embed(tq, ts, ids)
+    assert bad == 3
+    for i, t in enumerate(ids):
+        if 0 <= t < 100:
+            assert np.array_equal(bits(g[i]), bits(ro[i]))
+        else:
+            assert (g[i] == 7.0).all()
+
+
+# --------------------------------------------------------------------------- drop-in (host pointers)
+def test_execute_dropin(q3, oracle):
+    rng = np.random.default_rng(42)
+    # MetalContext::executeRMSNorm, incl. a size that is not a multiple of 4
+    for size in (2560, 1023):
+        x = rng.uniform(-1, 1, size).astype(np.float32)
+        w = rng.uniform(-1, 1, size).astype(np.float32)
+        out = np.empty_like(x)
+        q3.execute_rmsnorm(out, x, w)
+        assert np.array_equal(bits(out), bits(oracle.rmsnorm(x, w)))
+    # executeSoftmax
+    x = rng.uniform(-1, 1, 4096).astype(np.float32)
+    y = x.copy()
+    q3.execute_softmax(y)
+    np.testing.assert_allclose(y, oracle.softmax(x), rtol=RTOL, atol=ATOL)
+    assert abs(float(y.astype(np.float64).sum()) - 1.0) <= 1e-5
+    # executeSwiGLU (size 10240 as in the reference's shader test, and a ragged one)
+    for n in (10240, 1001):
+        hb = rng.uniform(-1, 1, n).astype(np.float32)
+        hb2 = rng.uniform(-1, 1, n).astype(np.float32)
+        y = hb.copy()
+        q3.execute_swiglu(y, hb2)
+        assert np.array_equal(bits(y), bits(oracle.swiglu(hb, hb2)))
+    # executeRoPE: 20 q heads / 4 kv heads at pos 42 (the reference's shader test shape)
+    q = rng.uniform(-1, 1, 20 * 128).astype(np.float32)
+    k = rng.uniform(-1, 1, 4 * 128).astype(np.float32)
+    qn = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    kn = rng.uniform(0.5, 1.5, 128).astype(np.float32)
+    qg, kg = q.copy(), k.copy()
+    q3.execute_rope(qg, kg, 128, 42, 20, 4, qn, kn)
+    qo = np.concatenate([oracle.qk_norm_rope_head(q[h * 128:(h + 1) * 128], qn, 42) for h in range(20)])
+    ko = np.concatenate([oracle.qk_norm_rope_head(k[h * 128:(h + 1) * 128], kn, 42) for h in range(4)])
+    np.testing.assert_allclose(qg, qo, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(kg, ko, rtol=RTOL, atol=ATOL)
+    # executeQuantize, incl. a ragged tail the reference leaves untouched
+    x = rng.standard_normal(1000).astype(np.float32)
+    qq = np.full(1000, 99, np.int8)
+    ss = np.zeros(1000 // 64, np.float32)
+    q3.execute_quantize(qq, ss, x)
+    qo, so = oracle.quantize(x[:960])
+    assert np.array_equal(qq[:960], qo) and np.array_equal(bits(ss), bits(so)) and (qq[960:] == 99).all()
+    # executeEmbedding from a Q8_0 table
+    tq = rng.integers(-127, 128, size=(50, 1024), dtype=np.int8)
+    ts = np.abs(0.01 * rng.standard_normal((50, 16))).astype(np.float32)
+    out = np.empty(1024, np.float32)
+    q3.execute_embedding(out, tq, ts, 17, 1024)
+    assert np.array_equal(bits(out), bits(oracle.dequantize(tq[17], ts[17])))
