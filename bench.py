@@ -219,63 +219,53 @@ def profiled_traffic(workload, kernel):
 
 def cpu_baseline(workload, seconds=10.0):
     import numpy as np
-    from oracle.oracle import Oracle
-    o = Oracle()
+    impl, kind = cpu_impl()
     threads = os.cpu_count() or 1
     sample = 128
     rng = np.random.default_rng(0)
-    workload.cpu_step(o, np, sample, threads, rng)          # warm up (allocations, page faults)
+    workload.cpu_step(impl, np, sample, threads, rng)          # warm up (allocations, page faults)
     t0 = time.perf_counter()
     n = 0
     while True:
-        workload.cpu_step(o, np, sample, threads, rng)
+        workload.cpu_step(impl, np, sample, threads, rng)
         n += 1
         el = time.perf_counter() - t0
         if el >= seconds:
             break
     gbs = workload.bytes_for_tokens(sample) * n / el / 1e9
-    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": "port",
-            "sample": f"{n} passes over {sample} tokens of the same step ({el:.1f} s), oracle/q3_oracle.c "
-                      f"(the reference's CPU arithmetic), OpenMP over rows",
+    return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
+            "sample": f"{n} passes over {sample} tokens of the same step ({el:.1f} s), OpenMP over rows; "
+                      + CPU_NOTE[kind],
             "tokens_per_s": round(sample * n / el, 1)}
 
 
 # ---------------------------------------------------------------------------- reference arm
+def cpu_impl():
+    """The reference compiled from its sources (oracle/_ref) if present, else the port."""
+    try:
+        from oracle.oracle import ReferenceRows
+        return ReferenceRows(), "reference"
+    except Exception:
+        from oracle.oracle import Oracle
+        return Oracle(), "port"
+
+
 def run_reference(args, wl):
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return 0
     import numpy as np
-    from oracle.oracle import Oracle, reference_path
-    o = Oracle()
+    impl, kind = cpu_impl()
     threads = os.cpu_count() or 1
     sample = 32
     rng = np.random.default_rng(0)
-    kind = "port"
-    use_ref = os.path.exists(reference_path())
-    ref_rows = None
-    if use_ref:
-        try:
-            from oracle.oracle import ReferenceRows
-            ref_rows = ReferenceRows()
-            kind = "reference"
-        except Exception:
-            ref_rows = None
-
-    def step():
-        if ref_rows is not None:
-            ref_rows.step(wl, sample, threads)
-        else:
-            wl.cpu_step(o, np, sample, threads, rng)
-
     for _ in range(args.warmup):
-        step()
+        wl.cpu_step(impl, np, sample, threads, rng)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        step()
+        wl.cpu_step(impl, np, sample, threads, rng)
     el = time.perf_counter() - t0
-    per_step = wl.bytes_for_tokens(sample)
-    val = per_step * args.steps / el / 1e9
+    val = wl.bytes_for_tokens(sample) * args.steps / el / 1e9
     line = {
         "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
@@ -283,11 +273,19 @@ def run_reference(args, wl):
         "config": dict(wl.config(), sample_tokens_per_step=sample),
         "tokens_per_s": round(sample * args.steps / el, 2),
         "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": kind,
-                         "sample": f"{sample} tokens per step of the same workload on the host cores"},
+                         "sample": f"{sample} tokens per step of the same workload, {threads} host threads "
+                                   f"(OpenMP over rows); " + CPU_NOTE[kind]},
         "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+CPU_NOTE = {
+    "reference": "src/cpu/qwen3_original.c compiled unmodified (rmsnorm, quantize); its inline RoPE and "
+                 "SwiGLU loops restated in oracle/ref_rows.c",
+    "port": "oracle/q3_oracle.c, the restatement of src/cpu/qwen3_original.c",
+}
 
 
 METRIC = "fused layer-kernel HBM GB/s & tokens/s at 1/2/4/8 B200; % of HBM roofline"
@@ -301,12 +299,13 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="prefill4b")
+    ap.add_argument("--tokens", type=int, default=0, help="token rows per GPU (default: the workload's)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    wl = WORKLOADS[args.workload]()
+    wl = WORKLOADS[args.workload](tokens=args.tokens) if args.tokens else WORKLOADS[args.workload]()
 
     if args.impl == "reference":
         return run_reference(args, wl)

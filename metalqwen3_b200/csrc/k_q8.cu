@@ -49,16 +49,11 @@ __global__ void __launch_bounds__(256) quantize_q8_kernel(const T *__restrict__ 
 #pragma unroll
             for (int o = LPG / 2; o > 0; o >>= 1) m = amax_merge(m, __shfl_xor_sync(FULL, m, o));
             if (!ok[u]) continue;
-            float scale = q8_scale(m);
-            uint32_t w[V / 4];
-#pragma unroll
-            for (int i = 0; i < V / 4; ++i)
-                w[i] = q8_code(v[4 * i], scale) | (q8_code(v[4 * i + 1], scale) << 8) |
-                       (q8_code(v[4 * i + 2], scale) << 16) | (q8_code(v[4 * i + 3], scale) << 24);
+            const Q8Scale gs = q8_prepare(m);
             int8_t *qp = q + g * GS + (lane % LPG) * V;
-            if constexpr (V == 4) st_cs_u32(qp, w[0]);
-            else st_cs_v2(qp, make_uint2(w[0], w[1]));
-            if ((lane % LPG) == 0) st_cs_f32(s + g, scale);
+            if constexpr (V == 4) st_cs_u32(qp, q8_pack4(v, gs));
+            else st_cs_v2(qp, make_uint2(q8_pack4(v, gs), q8_pack4(v + 4, gs)));
+            if ((lane % LPG) == 0) st_cs_f32(s + g, gs.scale);
         }
     }
 }
@@ -146,14 +141,10 @@ __global__ void __launch_bounds__(256) embed_gather_kernel(const int8_t *__restr
                 m = amax_merge(m, __shfl_xor_sync(FULL, m, 1));
                 m = amax_merge(m, __shfl_xor_sync(FULL, m, 2));
                 if (act) {
-                    float scale = q8_scale(m);
-                    uint32_t cw[4];
-#pragma unroll
-                    for (int k = 0; k < 4; ++k)
-                        cw[k] = q8_code(v[4 * k], scale) | (q8_code(v[4 * k + 1], scale) << 8) |
-                                (q8_code(v[4 * k + 2], scale) << 16) | (q8_code(v[4 * k + 3], scale) << 24);
-                    st_cs_v4(oq + i * dim + e, make_uint4(cw[0], cw[1], cw[2], cw[3]));
-                    if ((lane & 3) == 0) st_cs_f32(os + i * (dim / GS) + e / GS, scale);
+                    const Q8Scale gs = q8_prepare(m);
+                    st_cs_v4(oq + i * dim + e,
+                             make_uint4(q8_pack4(v, gs), q8_pack4(v + 4, gs), q8_pack4(v + 8, gs), q8_pack4(v + 12, gs)));
+                    if ((lane & 3) == 0) st_cs_f32(os + i * (dim / GS) + e / GS, gs.scale);
                 }
             }
         }

@@ -119,44 +119,67 @@ __global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(const T *x, const 
     if (s_fail) return;
 
     // ---- phase 2: normalise, scale, store or quantize ----------------------
-    const int iters = (dim + 32 * V - 1) / (32 * V);
-    for (int r = warp; r < rv; r += RMS_THREADS / 32) {
-        const float ss = s_ss[r];
-        const int64_t rowoff = (r0 + r) * int64_t(dim);
-        for (int it = 0; it < iters; ++it) {
-            const int e = (it * 32 + lane) * V;
-            const bool act = e < dim;
-            float o[V];
+    // Thread t owns the column vectors f = t + 128*j of every row of the block,
+    // so it loads each weight vector once and reuses it for the R rows; a warp
+    // covers 32 consecutive vectors, so a Q8_0 group (LPG vectors) never
+    // straddles warps.  JB column sweeps x R rows (8 loads) are issued before any
+    // is consumed: the rows come back from L2 and the loads in flight hide its
+    // latency.
+    constexpr int JB = R >= 8 ? 1 : 8 / R;
+    const int NV = dim / V;
+    const int NJ = (NV + RMS_THREADS - 1) / RMS_THREADS;
+    float ssr[R];
+#pragma unroll
+    for (int r = 0; r < R; ++r) ssr[r] = r < rv ? s_ss[r] : 0.0f;
+    for (int j0 = 0; j0 < NJ; j0 += JB) {
+        uint4 xr[JB][R];
+#pragma unroll
+        for (int jj = 0; jj < JB; ++jj) {
+            const int f = tid + RMS_THREADS * (j0 + jj);
+#pragma unroll
+            for (int r = 0; r < R; ++r)
+                if (j0 + jj < NJ && f < NV && r < rv)
+                    xr[jj][r] = ld_v4(x + (r0 + r) * int64_t(dim) + int64_t(f) * V);   // coherent: out may alias x
+        }
+#pragma unroll
+        for (int jj = 0; jj < JB; ++jj) {
+            if (j0 + jj >= NJ) break;                                // uniform across the CTA
+            const int f = tid + RMS_THREADS * (j0 + jj);
+            const bool act = f < NV;
+            float wv[V];
             if (act) {
-                float xv[V], wv[V];
-                Vec<T>::widen(ld_v4(x + rowoff + e), xv);   // coherent: out may alias x
-                Vec<float>::widen(ld_nc_v4(w + e), wv);
-                if constexpr (V == 8) Vec<float>::widen(ld_nc_v4(w + e + 4), wv + 4);
-#pragma unroll
-                for (int i = 0; i < V; ++i) o[i] = __fmul_rn(wv[i], __fmul_rn(ss, xv[i]));
-            } else {
-#pragma unroll
-                for (int i = 0; i < V; ++i) o[i] = 0.0f;
+                Vec<float>::widen(ld_nc_v4(w + f * V), wv);
+                if constexpr (V == 8) Vec<float>::widen(ld_nc_v4(w + f * V + 4), wv + 4);
             }
-            if constexpr (Q8) {
-                float m = 0.0f;
 #pragma unroll
-                for (int i = 0; i < V; ++i) m = amax_fold(m, o[i]);
-#pragma unroll
-                for (int k = LPG / 2; k > 0; k >>= 1) m = amax_merge(m, __shfl_xor_sync(FULL, m, k));
+            for (int r = 0; r < R; ++r) {
+                if (r >= rv) break;                                  // uniform across the CTA
+                const int64_t e = (r0 + r) * int64_t(dim) + int64_t(f) * V;
+                float o[V];
                 if (act) {
-                    const float scale = q8_scale(m);
-                    uint32_t cw[V / 4];
+                    float xv[V];
+                    Vec<T>::widen(xr[jj][r], xv);
 #pragma unroll
-                    for (int i = 0; i < V / 4; ++i)
-                        cw[i] = q8_code(o[4 * i], scale) | (q8_code(o[4 * i + 1], scale) << 8) |
-                                (q8_code(o[4 * i + 2], scale) << 16) | (q8_code(o[4 * i + 3], scale) << 24);
-                    if constexpr (V == 4) st_cs_u32(q + rowoff + e, cw[0]);
-                    else st_cs_v2(q + rowoff + e, make_uint2(cw[0], cw[1]));
-                    if ((lane % LPG) == 0) st_cs_f32(s + (rowoff + e) / GS, scale);
+                    for (int i = 0; i < V; ++i) o[i] = __fmul_rn(wv[i], __fmul_rn(ssr[r], xv[i]));
+                } else {
+#pragma unroll
+                    for (int i = 0; i < V; ++i) o[i] = 0.0f;
                 }
-            } else {
-                if (act) st_cs_v4(out + rowoff + e, Vec<T>::narrow(o));
+                if constexpr (Q8) {
+                    float m = 0.0f;
+#pragma unroll
+                    for (int i = 0; i < V; ++i) m = amax_fold(m, o[i]);
+#pragma unroll
+                    for (int kk = LPG / 2; kk > 0; kk >>= 1) m = amax_merge(m, __shfl_xor_sync(FULL, m, kk));
+                    if (act) {
+                        const Q8Scale gs = q8_prepare(m);
+                        if constexpr (V == 4) st_cs_u32(q + e, q8_pack4(o, gs));
+                        else st_cs_v2(q + e, make_uint2(q8_pack4(o, gs), q8_pack4(o + 4, gs)));
+                        if ((lane % LPG) == 0) st_cs_f32(s + e / GS, gs.scale);
+                    }
+                } else {
+                    if (act) st_cs_v4(out + e, Vec<T>::narrow(o));
+                }
             }
         }
     }

@@ -9,13 +9,13 @@
 //                   v[j] = x*c - y*s;  v[j+hd/2] = x*s + y*c
 //
 // q [T][n_heads][128] and k [T][n_kv][128] are flat lists of 128-element head
-// rows.  A warp owns a tile of 32 consecutive head rows of one tensor:
+// rows.  A warp owns a tile of 16 consecutive head rows of one tensor:
 //   * lane i bulk-copies head row i into a padded shared-memory slot (TMA,
 //     one mbarrier per buffer; two buffers per warp so the next tile streams
 //     in while this one is processed);
 //   * lane i runs row i's sum of squares in index order (the reference's
 //     rounding sequence, so the normalised values are bit-exact);
-//   * then the warp walks the 32 rows: lane l rotates the pairs (2l, 2l+64)
+//   * then the warp walks the 16 rows: lane l rotates the pairs (2l, 2l+64)
 //     and (2l+1, 2l+65), reading the row from shared memory and writing it
 //     back to HBM with coalesced stores.
 // freq_j comes from the host (the C library's powf, the reference's own
@@ -26,8 +26,8 @@
 namespace q3 {
 
 constexpr int HD = 128;
-constexpr int ROPE_WARPS = 4;
-constexpr int ROPE_TILE = 32;
+constexpr int ROPE_WARPS = 12;                   // 12 warps x 2 tiles of 16 rows: 203 KB (f32), 104 KB (bf16)
+constexpr int ROPE_TILE = 16;
 
 template <typename T>
 __device__ __forceinline__ void load_pair(const uint8_t *rowp, int j, float &a, float &b) {
@@ -130,18 +130,19 @@ __global__ void __launch_bounds__(ROPE_WARPS * 32) qk_norm_rope_kernel(
 
         const float2 wlo = *reinterpret_cast<const float2 *>(nw + 2 * lane);
         const float2 whi = *reinterpret_cast<const float2 *>(nw + 64 + 2 * lane);
-        int64_t cur_tok = -1;
+        // token of each head row, tracked incrementally (one division per tile)
+        int64_t tok = row0 / heads;
+        int hin = int(row0 - tok * heads);
         float c0 = 0.f, s0 = 0.f, c1 = 0.f, s1 = 0.f;
         for (int i = 0; i < nvalid; ++i) {
             const float ss = __shfl_sync(FULL, ssl, i);
             const int64_t hr = row0 + i;
-            const int64_t tok = hr / heads;
-            if (tok != cur_tok) {                          // warp-uniform
-                cur_tok = tok;
+            if (i == 0 || hin == 0) {                      // warp-uniform: a new token
                 const float p = float(__ldg(pos + tok));
                 sincosf(__fmul_rn(p, f0), &s0, &c0);
                 sincosf(__fmul_rn(p, f1), &s1, &c1);
             }
+            if (++hin == heads) { hin = 0; ++tok; }
             const uint8_t *rp = tb + size_t(i) * ROWB;
             float x0, x1, y0, y1;
             load_pair<T>(rp, 2 * lane, x0, x1);
@@ -173,7 +174,7 @@ static cudaError_t launch_rope_t(T *q, T *k, const int32_t *pos, int64_t rows, i
     if (e != cudaSuccess) return e;
     const int64_t qr = rows * nh, kr = rows * nkv;
     const int64_t tiles = (qr + ROPE_TILE - 1) / ROPE_TILE + (kr + ROPE_TILE - 1) / ROPE_TILE;
-    const int per_sm = (sizeof(T) == 4) ? 1 : 3;                // CTAs that fit an SM's shared memory
+    const int per_sm = (sizeof(T) == 4) ? 1 : 2;                // CTAs that fit an SM's shared memory
     int64_t blocks = (tiles + ROPE_WARPS - 1) / ROPE_WARPS;
     const int64_t cap = int64_t(sms) * per_sm;
     if (blocks > cap) blocks = cap;

@@ -77,7 +77,7 @@ __global__ void __launch_bounds__(NW * 32) softmax_reg_kernel(float *x, const in
                                                               int lo, int hi) {
     constexpr int NT = NW * 32;
     constexpr int NB = SMX_PER_THREAD / 4;    // float4 slots per thread
-    __shared__ uint64_t s_tab[32];
+    __shared__ ExpTab s_tab;
     __shared__ float sh_f[NW];
     __shared__ double sh_d[NW];
     load_exp_table(s_tab);
@@ -111,14 +111,14 @@ __global__ void __launch_bounds__(NW * 32) softmax_reg_kernel(float *x, const in
 #pragma unroll
         for (int j = 0; j < NB; ++j) {
             if (t + j * NT < sp.nb) {
-                v[j].x = q3_expf_tab(__fsub_rn(v[j].x, m), s_tab);
-                v[j].y = q3_expf_tab(__fsub_rn(v[j].y, m), s_tab);
-                v[j].z = q3_expf_tab(__fsub_rn(v[j].z, m), s_tab);
-                v[j].w = q3_expf_tab(__fsub_rn(v[j].w, m), s_tab);
+                v[j].x = expf_host(__fsub_rn(v[j].x, m), s_tab);
+                v[j].y = expf_host(__fsub_rn(v[j].y, m), s_tab);
+                v[j].z = expf_host(__fsub_rn(v[j].z, m), s_tab);
+                v[j].w = expf_host(__fsub_rn(v[j].w, m), s_tab);
                 sum += double(v[j].x) + double(v[j].y) + double(v[j].z) + double(v[j].w);
             }
         }
-        if (si >= 0) { xs = q3_expf_tab(__fsub_rn(xs, m), s_tab); sum += double(xs); }
+        if (si >= 0) { xs = expf_host(__fsub_rn(xs, m), s_tab); sum += double(xs); }
         sum = block_sum<NW>(sum, sh_d);
         const float inv = float(1.0 / sum);
 
@@ -141,7 +141,7 @@ __global__ void __launch_bounds__(SMX_LONG_THREADS) softmax_long_kernel(float *x
                                                                         int64_t rows, int lo) {
     constexpr int NW = SMX_LONG_THREADS / 32;
     constexpr int NT = SMX_LONG_THREADS;
-    __shared__ uint64_t s_tab[32];
+    __shared__ ExpTab s_tab;
     __shared__ float sh_f[NW];
     __shared__ double sh_d[NW];
     load_exp_table(s_tab);
@@ -172,15 +172,15 @@ __global__ void __launch_bounds__(SMX_LONG_THREADS) softmax_long_kernel(float *x
 #pragma unroll 4
         for (int bi = t; bi < sp.nb; bi += NT) {
             float4 v = u4_as_f4(ld_v4(body + bi));
-            v.x = q3_expf_tab(__fsub_rn(v.x, m), s_tab);
-            v.y = q3_expf_tab(__fsub_rn(v.y, m), s_tab);
-            v.z = q3_expf_tab(__fsub_rn(v.z, m), s_tab);
-            v.w = q3_expf_tab(__fsub_rn(v.w, m), s_tab);
+            v.x = expf_host(__fsub_rn(v.x, m), s_tab);
+            v.y = expf_host(__fsub_rn(v.y, m), s_tab);
+            v.z = expf_host(__fsub_rn(v.z, m), s_tab);
+            v.w = expf_host(__fsub_rn(v.w, m), s_tab);
             sum += double(v.x) + double(v.y) + double(v.z) + double(v.w);
             *reinterpret_cast<uint4 *>(body + bi) = f4_as_u4(v);
         }
         if (si >= 0) {
-            const float e = q3_expf_tab(__fsub_rn(row[si], m), s_tab);
+            const float e = expf_host(__fsub_rn(row[si], m), s_tab);
             row[si] = e;
             sum += double(e);
         }

@@ -114,4 +114,55 @@ Q3_HD float q3_expf_tab(float x, const uint64_t *tab) {
     return (float)y;
 }
 
+/* ---------------------------------------------------------------------------
+ * q3_expf_fast: the same function with the table read as separate high/low
+ * 32-bit words (on the device: no shared-memory bank conflicts between lanes),
+ * k/N added to the high word's exponent field, and the 64-bit integer add
+ * avoided.  tests/test_expf.py checks it against the host expf on all 2^32
+ * inputs as well.
+ * ------------------------------------------------------------------------- */
+#if defined(__CUDACC__)
+Q3_HD double q3_hilo(uint32_t hi, uint32_t lo) {
+#if defined(__CUDA_ARCH__)
+    return __hiloint2double((int)hi, (int)lo);
+#else
+    return q3_u2d(((uint64_t)hi << 32) | lo);
+#endif
+}
+Q3_HD uint32_t q3_dlo(double d) {
+#if defined(__CUDA_ARCH__)
+    return (uint32_t)__double2loint(d);
+#else
+    return (uint32_t)q3_d2u(d);
+#endif
+}
+#else
+Q3_HD double q3_hilo(uint32_t hi, uint32_t lo) { return q3_u2d(((uint64_t)hi << 32) | lo); }
+Q3_HD uint32_t q3_dlo(double d) { return (uint32_t)q3_d2u(d); }
+#endif
+
+Q3_HD float q3_expf_fast(float x, const uint32_t *tab_hi, const uint32_t *tab_lo) {
+    uint32_t ux = q3_f2u(x);
+    uint32_t abstop = (ux >> 20) & 0x7ffu;
+    if (abstop >= 0x42bu) {                        /* |x| >= 88 or x is NaN/inf */
+        if (ux == 0xff800000u) return 0.0f;
+        if (abstop >= 0x7f8u) return x + x;
+        if (x > 0x1.62e42ep6f) return (float)(Q3_EXP_SHIFT * Q3_EXP_SHIFT * Q3_EXP_SHIFT);
+        if (x < -0x1.9fe368p6f) return 0.0f;
+    }
+    double xd = (double)x;
+    double kd = Q3_FMA(Q3_EXP_INVLN2N, xd, Q3_EXP_SHIFT);
+    uint32_t ki = q3_dlo(kd);
+    kd -= Q3_EXP_SHIFT;
+    double r = Q3_FMA(Q3_EXP_INVLN2N, xd, -kd);
+    uint32_t j = ki & 31u;
+    double s = q3_hilo(tab_hi[j] + (ki << 15), tab_lo[j]);   /* (ki << 47) reaches the high word only */
+    double z = Q3_FMA(Q3_EXP_C0, r, Q3_EXP_C1);
+    double r2 = r * r;
+    double y = Q3_FMA(Q3_EXP_C2, r, 1.0);
+    y = Q3_FMA(z, r2, y);
+    y = y * s;
+    return (float)y;
+}
+
 #endif /* Q3_EXPF_H */

@@ -131,6 +131,71 @@ __device__ __forceinline__ uint32_t q8_code(float v, float scale) {
 
 __device__ __forceinline__ float q8_scale(float wmax) { return __fdiv_rn(wmax, 127.0f); }
 
+__device__ __forceinline__ float rcp_approx(float x) {
+    float r;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));   // max error 1 ulp
+    return r;
+}
+
+// Correctly rounded 1/d for d >= 1 by Newton-Raphson from the 1-ulp seed
+// followed by Markstein's correction step (Markstein, IBM J. Res. Dev. 34(1),
+// 1990): e = 1 - d*y and y + y*e with fused multiply-adds.  Equal to the IEEE
+// reciprocal (__frcp_rn) for every binary32 d in [1, 2^120), which
+// tests/test_device_math.py checks exhaustively on the GPU; larger d, inf and
+// NaN use __frcp_rn.
+// Rare paths are kept out of line so the compiler branches around them
+// instead of predicating them into every element's instruction stream.
+static __device__ __noinline__ float rcp_rn_slow(float d) { return __frcp_rn(d); }
+
+__device__ __forceinline__ float rcp_rn_ge1(float d) {
+    if (!(d < 0x1p120f)) return rcp_rn_slow(d);
+    const float y0 = rcp_approx(d);
+    const float y1 = __fmaf_rn(y0, __fmaf_rn(-d, y0, 1.0f), y0);
+    return __fmaf_rn(y1, __fmaf_rn(-d, y1, 1.0f), y1);
+}
+
+// Per-group state for the fast code path.
+//  * scale = RN(wmax/127): one multiply by RN(1/127) = 0x1.020408p-7 and one
+//    FMA-based correction (Markstein); equal to the IEEE quotient for every
+//    wmax in [2^-100, 2^100] (exhaustive check in tests/test_device_math.py).
+//    Groups outside [2^-90, 2^100] (zero, tiny, huge, inf) use the division.
+//  * codes: q8_code needs one IEEE division per element, but the code depends
+//    on that quotient only through round-half-away.  So multiply by an
+//    approximate reciprocal (rcp.approx, within 1 ulp) and fall back to the
+//    exact division when the product lies within 2^-14 of a tie k + 1/2.  For
+//    |v| <= wmax, |v*inv - v/scale| <= 127.0001 * (2^-23 + 2^-24) < 2.3e-5 and
+//    the IEEE quotient is within half an ulp (< 3.9e-6) of v/scale, so outside
+//    the window both round to the same integer.
+struct Q8Scale {
+    float scale, inv;
+    bool exact;
+};
+static __device__ __noinline__ float q8_scale_slow(float wmax) { return q8_scale(wmax); }
+static __device__ __noinline__ uint32_t q8_code_slow(float v, float scale) { return q8_code(v, scale); }
+
+__device__ __forceinline__ Q8Scale q8_prepare(float wmax) {
+    Q8Scale g;
+    const float c = 0x1.020408p-7f;
+    const float s0 = __fmul_rn(wmax, c);
+    g.scale = __fmaf_rn(__fmaf_rn(-s0, 127.0f, wmax), c, s0);
+    g.exact = !(wmax >= 0x1p-90f && wmax <= 0x1p+100f);
+    if (g.exact) g.scale = q8_scale_slow(wmax);
+    g.inv = g.exact ? 0.0f : rcp_approx(g.scale);
+    return g;
+}
+__device__ __forceinline__ uint32_t q8_code_g(float v, const Q8Scale &g) {
+    const float qa = __fmul_rn(v, g.inv);
+    const float t = __fadd_rn(qa, 12582912.0f);          // 1.5*2^23: round to nearest integer (|qa| < 2^22)
+    const float d = fabsf(__fsub_rn(qa, __fsub_rn(t, 12582912.0f)));   // exact distance to it
+    if (g.exact || !(d <= 0.49993896484375f))            // exact group, near a tie, or NaN
+        return q8_code_slow(v, g.scale);
+    return uint32_t(__float_as_int(t) - 0x4B400000) & 0xffu;
+}
+// Four codes packed little-endian into one word.
+__device__ __forceinline__ uint32_t q8_pack4(const float *o, const Q8Scale &g) {
+    return q8_code_g(o[0], g) | (q8_code_g(o[1], g) << 8) | (q8_code_g(o[2], g) << 16) | (q8_code_g(o[3], g) << 24);
+}
+
 // ---------------------------------------------------------------------------
 // expf with the host libm's bits (q3_expf.h); the table lives in shared memory
 // ---------------------------------------------------------------------------
@@ -139,6 +204,18 @@ static __constant__ uint64_t c_exp_tab[32] = Q3_EXP2_TAB32_INIT;
 __device__ __forceinline__ void load_exp_table(uint64_t *s_tab) {
     if (threadIdx.x < 32) s_tab[threadIdx.x] = c_exp_tab[threadIdx.x];
 }
+// High and low 32-bit words in separate arrays, for q3_expf_fast.
+struct ExpTab {
+    uint32_t hi[32], lo[32];
+};
+__device__ __forceinline__ void load_exp_table(ExpTab &t) {
+    if (threadIdx.x < 32) {
+        const uint64_t v = c_exp_tab[threadIdx.x];
+        t.hi[threadIdx.x] = uint32_t(v >> 32);
+        t.lo[threadIdx.x] = uint32_t(v);
+    }
+}
+__device__ __forceinline__ float expf_host(float x, const ExpTab &t) { return q3_expf_fast(x, t.hi, t.lo); }
 
 // ---------------------------------------------------------------------------
 // TMA bulk copies (cp.async.bulk, no tensor map, no multicast) and mbarriers

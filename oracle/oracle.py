@@ -302,6 +302,70 @@ class Reference:
         self.lib.qwen3_transformer_free(t)
 
 
+class ReferenceRows:
+    """Row-batched, OpenMP driver of the compiled reference (oracle/ref_rows.c).
+
+    Same method names and signatures as the f32 paths of ``Oracle`` so callers
+    can time either; only f32 inputs.
+    """
+
+    def __init__(self, path: str | None = None):
+        path = path or os.path.join(HERE, "_ref", "libref_rows.so")
+        if not os.path.exists(path):
+            raise FileNotFoundError(path)
+        self.lib = C.CDLL(path)
+        vp, i32, i64 = C.c_void_p, C.c_int, C.c_int64
+        for name, args in (
+            ("ref_rows_rmsnorm_q8", [vp, vp, i64, i32, vp, vp, i32]),
+            ("ref_rows_qk_norm_rope", [vp, vp, vp, i64, i32, i32, i32, vp, vp, i32]),
+            ("ref_rows_swiglu_q8", [vp, vp, i64, i32, vp, vp, i32]),
+            ("ref_rows_softmax", [vp, vp, vp, i64, i32]),
+            ("ref_rows_embed", [vp, vp, i32, i32, vp, i64, vp, vp, vp, i32]),
+        ):
+            fn = getattr(self.lib, name)
+            fn.restype = None
+            fn.argtypes = args
+
+    def rows_rmsnorm_q8(self, x, w, threads=1):
+        rows, dim = x.shape
+        q = np.empty((rows, dim), np.int8)
+        s = np.empty((rows, dim // GS), np.float32)
+        self.lib.ref_rows_rmsnorm_q8(_p(x), _p(w), rows, dim, _p(q), _p(s), threads)
+        return q, s
+
+    def rows_qk_norm_rope(self, q, k, pos, q_norm, k_norm, theta=1e6, threads=1):
+        assert theta == 1e6, "the reference hard-codes theta = 1e6"
+        rows, nh, hd = q.shape
+        qo, ko = np.array(q, copy=True), np.array(k, copy=True)
+        self.lib.ref_rows_qk_norm_rope(_p(qo), _p(ko), _p(np.ascontiguousarray(pos, np.int32)), rows, nh,
+                                       k.shape[1], hd, _p(q_norm), _p(k_norm), threads)
+        return qo, ko
+
+    def rows_swiglu_q8(self, hb, hb2, threads=1):
+        rows, n = hb.shape
+        q = np.empty((rows, n), np.int8)
+        s = np.empty((rows, n // GS), np.float32)
+        self.lib.ref_rows_swiglu_q8(_p(hb), _p(hb2), rows, n, _p(q), _p(s), threads)
+        return q, s
+
+    def rows_softmax(self, x, off, lens, threads=1):
+        out = np.array(x, np.float32, copy=True)
+        off = np.ascontiguousarray(off, np.int64)
+        lens = np.ascontiguousarray(lens, np.int32)
+        self.lib.ref_rows_softmax(_p(out), _p(off), _p(lens), off.size, threads)
+        return out
+
+    def rows_embed(self, tq, ts, ids, want_q8=True, threads=1):
+        vocab, dim = tq.shape
+        ids = np.ascontiguousarray(ids, np.int32)
+        n = ids.size
+        out = np.zeros((n, dim), np.float32)
+        oq = np.zeros((n, dim), np.int8) if want_q8 else None
+        os_ = np.zeros((n, dim // GS), np.float32) if want_q8 else None
+        self.lib.ref_rows_embed(_p(tq), _p(ts), vocab, dim, _p(ids), n, _p(out), _p(oq), _p(os_), threads)
+        return out, oq, os_
+
+
 class OracleModel:
     """The restated decode step (q3o_forward) over an in-memory checkpoint image."""
 

@@ -1,0 +1,65 @@
+"""Checks of the fast arithmetic used by the Q8_0 epilogues and SwiGLU.
+
+* Q8_0 scale RN(wmax/127) by a Markstein correction step == IEEE division
+  for every binary32 wmax in [2^-100, 2^100]  (CPU, exhaustive, fmaf);
+* on the GPU (tests/native/check_device_math.cu, built with nvcc):
+  the Markstein reciprocal == __frcp_rn for every binary32 d >= 1, and the
+  multiply-by-reciprocal code path == the IEEE-division path on 2^20 random
+  scales x values placed on and around every rounding tie.
+"""
+import os
+import subprocess
+import tempfile
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+CSRC = os.path.join(ROOT, "metalqwen3_b200", "csrc")
+
+DIV127 = r"""
+#include <stdio.h>
+#include <stdint.h>
+#include <string.h>
+#include <math.h>
+int main(void) {
+    const float c = 0x1.020408p-7f;
+    long long bad = 0;
+    #pragma omp parallel for reduction(+:bad) schedule(dynamic, 1 << 16)
+    for (long long i = 0x0d800000LL; i <= 0x71800000LL; i++) {          /* 2^-100 .. 2^100 */
+        uint32_t u = (uint32_t)i; float m; memcpy(&m, &u, 4);
+        float s0 = m * c;
+        float s = fmaf(fmaf(-s0, 127.0f, m), c, s0);
+        float ref = m / 127.0f;
+        uint32_t a, b; memcpy(&a, &s, 4); memcpy(&b, &ref, 4);
+        if (a != b) bad++;
+    }
+    printf("%lld\n", bad);
+    return 0;
+}
+"""
+
+
+def test_scale_div127_exhaustive():
+    with tempfile.TemporaryDirectory() as d:
+        src, exe = os.path.join(d, "a.c"), os.path.join(d, "a")
+        open(src, "w").write(DIV127)
+        subprocess.run(["gcc", "-O2", "-fopenmp", "-ffp-contract=off", src, "-o", exe, "-lm"], check=True)
+        bad = int(subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split()[0])
+    assert bad == 0
+
+
+@pytest.mark.gpu
+def test_fast_device_math_on_gpu():
+    import torch
+    if not torch.cuda.is_available():
+        pytest.skip("no GPU")
+    with tempfile.TemporaryDirectory() as d:
+        exe = os.path.join(d, "check")
+        subprocess.run(["nvcc", "-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-std=c++17", "--fmad=false",
+                        "-I", CSRC, "-I", os.path.join(ROOT, "include"),
+                        os.path.join(ROOT, "tests", "native", "check_device_math.cu"), "-o", exe], check=True)
+        out = subprocess.run([exe], check=True, capture_output=True, text=True, timeout=300).stdout.split()
+    bad_rcp, bad_scale, bad_code = map(int, out[:3])
+    assert bad_rcp == 0, f"{bad_rcp} binary32 d >= 1 where the Markstein reciprocal != __frcp_rn"
+    assert bad_scale == 0, f"{bad_scale} scales differ from the IEEE quotient"
+    assert bad_code == 0, f"{bad_code} codes differ between the fast and the exact path"

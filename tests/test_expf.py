@@ -21,16 +21,19 @@ HARNESS = r"""
 #include "q3_expf.h"
 static const uint64_t TAB[32] = Q3_EXP2_TAB32_INIT;
 int main(void) {
-    long long bad = 0, checked = 0;
+    uint32_t HI[32], LO[32];
+    for (int i = 0; i < 32; i++) { HI[i] = (uint32_t)(TAB[i] >> 32); LO[i] = (uint32_t)TAB[i]; }
+    long long bad = 0, checked = 0, bad_fast = 0;
     #pragma omp parallel for reduction(+:bad,checked) schedule(dynamic, 1 << 16)
     for (long long i = 0; i < (1LL << 32); i++) {
         uint32_t u = (uint32_t)i; float x; memcpy(&x, &u, 4);
-        float a = expf(x), b = q3_expf_tab(x, TAB);
-        uint32_t ua, ub; memcpy(&ua, &a, 4); memcpy(&ub, &b, 4);
+        float a = expf(x), b = q3_expf_tab(x, TAB), c = q3_expf_fast(x, HI, LO);
+        uint32_t ua, ub, uc; memcpy(&ua, &a, 4); memcpy(&ub, &b, 4); memcpy(&uc, &c, 4);
         checked++;
         if (ua != ub && !(isnan(a) && isnan(b))) bad++;
+        if (ua != uc && !(isnan(a) && isnan(c))) bad_fast++;
     }
-    printf("%lld %lld\n", checked, bad);
+    printf("%lld %lld %lld\n", checked, bad, bad_fast);
     return 0;
 }
 """
@@ -54,6 +57,7 @@ def test_expf_all_binary32_inputs():
         open(src, "w").write(HARNESS)
         subprocess.run(["gcc", "-O2", "-fopenmp", "-ffp-contract=off", "-I", CSRC, src, "-o", exe, "-lm"], check=True)
         out = subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split()
-    checked, bad = int(out[0]), int(out[1])
+    checked, bad, bad_fast = int(out[0]), int(out[1]), int(out[2])
     assert checked == 1 << 32
-    assert bad == 0, f"{bad} binary32 inputs where the device expf differs from the host expf"
+    assert bad == 0, f"{bad} binary32 inputs where q3_expf_tab differs from the host expf"
+    assert bad_fast == 0, f"{bad_fast} binary32 inputs where q3_expf_fast differs from the host expf"
