@@ -9,39 +9,74 @@
 //
 // The sum is a chain of dependent adds in index order; changing the order
 // changes the bits of ss and can move a Q8_0 scale or code.  So each row's sum
-// is computed by one lane, in order, and the kernel gets its parallelism from
-// many rows at once instead of from a tree reduction:
+// is run by one lane, in order, and parallelism comes from many rows at once:
+// one warp carries up to 32 row chains, one per lane (about 5 cycles per element
+// of latency; 28 chains keep pace with an SM's share of HBM for f32 rows).
 //
-//   phase 1  warp 0 streams the CTA's R rows through shared memory in 1 KB
-//            chunks with TMA bulk copies (cp.async.bulk + mbarrier, NS-stage
-//            ring, padded rows so the R reader lanes hit distinct banks);
-//            lane r folds row r's chunk into its running sum.
-//   phase 2  all four warps re-read the rows (L2-resident: the row was read a
-//            few microseconds earlier), apply w*(ss*x), and either store the
-//            float row or quantize each 64-group (absmax by xor-shuffle) and
-//            store int8 codes + one f32 scale per group.
-//
-// A CTA holds R <= 8 rows; many CTAs share an SM, so while some are in phase 1
-// others stream their phase-2 output.  HBM traffic per row is one read of x
-// plus the output; the chain costs ~4 cycles/element of latency, which the
-// ~13 resident CTAs per SM (R=4) hide behind the memory time.
+// Persistent CTA per SM over blocks of R <= 32 rows (the same number of rows
+// per SM): 16 compute warps and one producer warp.  All data moves through one ring of NS = 3 stages of
+// 32 rows x 2 KB in shared memory, filled by TMA bulk copies (cp.async.bulk,
+// one 2 KB copy per row per stage, an mbarrier per stage, rows padded so the
+// chain lanes read distinct banks), so two stages are in flight while the
+// chain consumes the third.  Per block:
+//   phase 1  the row chunks in order; chain-warp lane r folds row r's chunk into
+//            its running sum.  The first nch - NS chunks are released as soon
+//            as the chain has read them; the last NS stay in their stages.
+//   phase 2  all 16 warps normalise the resident chunks from shared memory,
+//            then the released chunks again (second copies, served from L2:
+//            they were streamed a few microseconds earlier), apply w*(ss*x)
+//            and store the float rows or quantize each 64-group (absmax by
+//            xor-shuffle) into int8 codes + f32 scales.
+// For a 2560-wide f32 row (5 chunks) only 2 of the 5 chunks are read twice.
+// The copies form one stream per CTA (first reads, then second reads, block
+// after block).  The producer warp issues item it into stage it % NS once the
+// consumers have released item it - NS (an "empty" mbarrier per stage), so
+// the ring runs across phases and blocks, and the ~1 us it takes to issue a
+// stage's 32 row copies is spent by a warp that has nothing else to do.
 #include "q3cu_internal.h"
 
 namespace q3 {
 
-constexpr int RMS_CHUNK_BYTES = 1024;
-constexpr int RMS_ROWB = RMS_CHUNK_BYTES + 16;   // padded smem row stride
-constexpr int RMS_NS = 4;                        // ring stages
-constexpr int RMS_THREADS = 128;
+constexpr int RMS_CWARPS = 16;                   // compute warps; warp RMS_CWARPS is the producer
+constexpr int RMS_CTHREADS = RMS_CWARPS * 32;
+constexpr int RMS_THREADS = RMS_CTHREADS + 32;
+constexpr int RMS_CHAIN = 1;                     // chain warp: not on the producer's SMSP (warp % 4)
+constexpr int RMS_MAXR = 32;                     // rows per block = lanes of the chain warp
+constexpr int RMS_CB = 2048;                     // bytes per row per stage
+constexpr int RMS_ROWB = RMS_CB + 16;            // padded smem row stride
+constexpr int RMS_NS = 3;                        // ring stages
+constexpr size_t RMS_SMEM = size_t(RMS_NS) * RMS_MAXR * RMS_ROWB;   // 198,144 bytes
 
 template <typename T>
 __device__ __forceinline__ float chain_sum(float acc, const uint8_t *p, int elems) {
-    // elems is a multiple of Vec<T>::N; 16-byte smem loads, adds in index order.
+    // 16-byte smem loads in batches of 8, the next batch loaded before the
+    // current one is folded in; squares by packed multiplies, adds in index order.
     constexpr int V = Vec<T>::N;
     const uint4 *p4 = reinterpret_cast<const uint4 *>(p);
-    const int nv = elems / V;
-#pragma unroll 8
-    for (int k = 0; k < nv; ++k) {
+    const int nv = elems / V, nb8 = nv / 8;
+    if (nb8 > 0) {
+        uint4 cur[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cur[j] = p4[j];
+        for (int b = 0; b < nb8; ++b) {
+            uint4 nxt[8];
+            const int kn = (b + 1 < nb8 ? b + 1 : b) * 8;          // the last batch reloads itself
+#pragma unroll
+            for (int j = 0; j < 8; ++j) nxt[j] = p4[kn + j];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) {
+                float v[V], sq[V];
+                Vec<T>::widen(cur[j], v);
+#pragma unroll
+                for (int i = 0; i < V; i += 2) up2(mul2(pk2(v[i], v[i + 1]), pk2(v[i], v[i + 1])), sq[i], sq[i + 1]);
+#pragma unroll
+                for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, sq[i]);     // in index order
+            }
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+        }
+    }
+    for (int k = nb8 * 8; k < nv; ++k) {
         float v[V];
         Vec<T>::widen(p4[k], v);
 #pragma unroll
@@ -50,158 +85,248 @@ __device__ __forceinline__ float chain_sum(float acc, const uint8_t *p, int elem
     return acc;
 }
 
-template <typename T, int R, bool Q8>
-__global__ void __launch_bounds__(RMS_THREADS) rmsnorm_kernel(const T *x, const float *__restrict__ w,
-                                                              int64_t rows, int dim, int n_div, float eps, T *out,
-                                                              int8_t *__restrict__ q, float *__restrict__ s,
-                                                              uint32_t *status) {
+template <typename T, bool Q8>
+__global__ void __launch_bounds__(RMS_THREADS, 1) rmsnorm_kernel(const T *x, const float *__restrict__ w, int64_t rows,
+                                                                 int dim, int n_div, float eps, int R, T *out,
+                                                                 int8_t *__restrict__ q, float *__restrict__ s,
+                                                                 uint32_t *status) {
     constexpr int ESZ = sizeof(T);
-    constexpr int CW = RMS_CHUNK_BYTES / ESZ;    // elements per chunk
     constexpr int V = Vec<T>::N;                 // elements per 16-byte vector
-    constexpr int LPG = GS / V;                  // lanes per Q8_0 group
-
-    __shared__ __align__(128) uint8_t stage[RMS_NS][R][RMS_ROWB];
-    __shared__ __align__(8) uint64_t bar[RMS_NS];
-    __shared__ float s_ss[R];
-    __shared__ int s_fail;
+    constexpr int NLPG = GS / V;                 // lanes per Q8_0 group
+    extern __shared__ __align__(128) uint8_t stage[];          // [RMS_NS][RMS_MAXR][RMS_ROWB]
+    __shared__ __align__(8) uint64_t bar[RMS_NS];             // full: the stage's copies landed
+    __shared__ __align__(8) uint64_t empty[RMS_NS];           // the stage's item was released
+    __shared__ float ss_sh[RMS_MAXR];
+    __shared__ int fail_sh;
 
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int64_t r0 = int64_t(blockIdx.x) * R;
-    const int rv = int(rows - r0 < R ? rows - r0 : R);
-    const int nch = (dim + CW - 1) / CW;
-    const uint8_t *xb = reinterpret_cast<const uint8_t *>(x) + r0 * int64_t(dim) * ESZ;
+    const int64_t nblocks = (rows + R - 1) / R;
+    const int nb = int((nblocks - 1 - blockIdx.x) / gridDim.x) + 1;   // blocks of this CTA (grid <= nblocks)
+    const int64_t row_bytes = int64_t(dim) * ESZ;
+    const int nch = int((row_bytes + RMS_CB - 1) / RMS_CB);
+    const int nre = nch > RMS_NS ? nch - RMS_NS : 0;    // chunks read twice; chunks nre.. stay resident
+    const int per_block = nch + nre;                    // stream items per block
+    const int total = nb * per_block;
 
     if (tid == 0) {
-        for (int i = 0; i < RMS_NS; ++i) mbar_init(&bar[i], 1);
+        for (int i = 0; i < RMS_NS; ++i) {
+            mbar_init(&bar[i], 1);
+            mbar_init(&empty[i], 1);
+        }
         mbar_init_fence();
-        s_fail = 0;
+        fail_sh = 0;
     }
     __syncthreads();
 
-    // ---- phase 1: ordered sum of squares, one lane per row ----------------
-    if (warp == 0) {
+    auto block_rows = [&](int k, int64_t &r0, int &rv) {
+        const int64_t b = blockIdx.x + int64_t(k) * gridDim.x;
+        r0 = b * R;
+        rv = int(rows - r0 < R ? rows - r0 : R);
+    };
+    auto chunk_bytes = [&](int c) {
+        const int64_t off = int64_t(c) * RMS_CB;
+        return int(row_bytes - off < RMS_CB ? row_bytes - off : RMS_CB);
+    };
+    // Item it: block it / per_block; j = it % per_block is the first read of
+    // chunk j (j < nch) or the second read of chunk j - nch.  Stage it % NS.
+    auto issue = [&](int it) {
+        const int k = it / per_block, j = it % per_block, c = j < nch ? j : j - nch, st = it % RMS_NS;
+        int64_t r0; int rv;
+        block_rows(k, r0, rv);
+        const uint32_t bytes = uint32_t(chunk_bytes(c));
+        if (lane == 0) mbar_arrive_expect_tx(&bar[st], bytes * uint32_t(rv));
+        __syncwarp();
+        if (lane < rv)
+            bulk_g2s(stage + (size_t(st) * RMS_MAXR + lane) * RMS_ROWB,
+                     reinterpret_cast<const uint8_t *>(x) + (r0 + lane) * row_bytes + int64_t(c) * RMS_CB, bytes,
+                     &bar[st]);
+    };
+    // ---- producer warp -----------------------------------------------------
+    // Items are released in stream order (one arrival on empty[] each), so the
+    // u-th completion of empty[st] is the release of item st + u * NS.  The
+    // producer only reads fail_sh: the compute warps' exits must not depend on
+    // a write that can land between their reads.
+    if (warp == RMS_CWARPS) {
         int issued = 0;
-        auto issue = [&](int c) {
-            const int st = c % RMS_NS;
-            const int el = dim - c * CW < CW ? dim - c * CW : CW;
-            const uint32_t bytes = uint32_t(el) * ESZ;
-            mbar_arrive_expect_tx(&bar[st], bytes * uint32_t(rv));
-            for (int r = 0; r < rv; ++r)
-                bulk_g2s(&stage[st][r][0], xb + (int64_t(r) * dim + int64_t(c) * CW) * ESZ, bytes, &bar[st]);
-        };
+        for (; issued < total; ++issued) {
+            const int st = issued % RMS_NS;
+            if (__any_sync(FULL, fail_sh != 0)) break;
+            if (issued >= RMS_NS &&
+                !__all_sync(FULL, mbar_wait(&empty[st], uint32_t(issued / RMS_NS - 1) & 1u, lane == 0 ? status : nullptr)))
+                break;                             // the consumers' own waits report the failure
+            issue(issued);
+        }
+        // Before the CTA may exit, every issued copy has landed.  Normally the
+        // consumers have already seen all of them; after a failure this waits
+        // (bounded) for the at most NS items still in flight.
         if (lane == 0)
-            for (; issued < nch && issued < RMS_NS; ++issued) issue(issued);
-        float acc = 0.0f;
-        int c = 0;
-        bool ok = true;
-        for (; c < nch; ++c) {
-            const int st = c % RMS_NS;
-            ok = __all_sync(FULL, mbar_wait(&bar[st], uint32_t(c / RMS_NS) & 1u, lane == 0 ? status : nullptr));
-            if (!ok) break;
-            if (lane < rv) {
-                const int el = dim - c * CW < CW ? dim - c * CW : CW;
-                acc = chain_sum<T>(acc, &stage[st][lane][0], el);
-            }
-            __syncwarp();
-            if (lane == 0 && c + RMS_NS < nch) { issue(c + RMS_NS); issued = c + RMS_NS + 1; }
-        }
-        if (!ok) {
-            // Drain: wait (bounded) for copies still in flight before leaving.
-            if (lane == 0) {
-                for (int d = c; d < issued; ++d) mbar_wait(&bar[d % RMS_NS], uint32_t(d / RMS_NS) & 1u, nullptr);
-                s_fail = 1;
-            }
-        } else if (lane < rv) {
-            s_ss[lane] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, float(n_div)), eps)));
-        }
+            for (int d = issued > RMS_NS ? issued - RMS_NS : 0; d < issued; ++d)
+                mbar_wait(&bar[d % RMS_NS], uint32_t(d / RMS_NS) & 1u, nullptr);
+        return;
     }
-    __syncthreads();
-    if (s_fail) return;
+    auto wait_item = [&](int i) {
+        return __all_sync(FULL, mbar_wait(&bar[i % RMS_NS], uint32_t(i / RMS_NS) & 1u, lane == 0 ? status : nullptr));
+    };
+    // The norm weights are re-read by every phase-2 step: while the chain warp runs the
+    // chains, the other warps pull them into L1.
+    if (warp != RMS_CHAIN)
+        for (int64_t off = int64_t(tid - (warp > RMS_CHAIN ? 32 : 0)) * 32; off < int64_t(dim); off += int64_t(RMS_CTHREADS - 32) * 32)
+            prefetch_l1(w + off);
 
-    // ---- phase 2: normalise, scale, store or quantize ----------------------
-    // Thread t owns the column vectors f = t + 128*j of every row of the block,
-    // so it loads each weight vector once and reuses it for the R rows; a warp
-    // covers 32 consecutive vectors, so a Q8_0 group (LPG vectors) never
-    // straddles warps.  JB column sweeps x R rows (8 loads) are issued before any
-    // is consumed: the rows come back from L2 and the loads in flight hide its
-    // latency.
-    constexpr int JB = R >= 8 ? 1 : 8 / R;
-    const int NV = dim / V;
-    const int NJ = (NV + RMS_THREADS - 1) / RMS_THREADS;
-    float ssr[R];
-#pragma unroll
-    for (int r = 0; r < R; ++r) ssr[r] = r < rv ? s_ss[r] : 0.0f;
-    for (int j0 = 0; j0 < NJ; j0 += JB) {
-        uint4 xr[JB][R];
-#pragma unroll
-        for (int jj = 0; jj < JB; ++jj) {
-            const int f = tid + RMS_THREADS * (j0 + jj);
-#pragma unroll
-            for (int r = 0; r < R; ++r)
-                if (j0 + jj < NJ && f < NV && r < rv)
-                    xr[jj][r] = ld_v4(x + (r0 + r) * int64_t(dim) + int64_t(f) * V);   // coherent: out may alias x
+    for (int k = 0, base = 0; k < nb && !fail_sh; ++k, base += per_block) {
+        int64_t r0; int rv;
+        block_rows(k, r0, rv);
+        // ---- phase 1: the chain warp runs the chains -------------------------
+        if (warp == RMS_CHAIN) {
+            float acc = 0.0f;
+            bool ok = true;
+            for (int c = 0; c < nch; ++c) {
+                ok = wait_item(base + c);
+                if (!ok) break;
+                if (lane < rv)
+                    acc = chain_sum<T>(acc, stage + (size_t((base + c) % RMS_NS) * RMS_MAXR + lane) * RMS_ROWB,
+                                       chunk_bytes(c) / ESZ);
+                __syncwarp();
+                if (c < nre && lane == 0) mbar_arrive(&empty[(base + c) % RMS_NS]);   // resident chunks: phase 2
+            }
+            if (lane < rv) ss_sh[lane] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, float(n_div)), eps)));
+            if (!ok && lane == 0) fail_sh = 1;
         }
+        named_sync(1, RMS_CTHREADS);               // ss visible to every compute warp
+        if (fail_sh) break;
+        // ---- phase 2: every warp, from shared memory -----------------------
+        // Step j handles item base + nre + j: the resident chunks nre..nch-1,
+        // then the second reads of chunks 0..nre-1.
+        for (int j = 0; j < nch; ++j) {
+            const int i = base + nre + j;
+            const int c = j < nch - nre ? nre + j : j - (nch - nre);
+            if (!wait_item(i)) fail_sh = 1;        // benign race: every writer stores 1
+            const bool live = __all_sync(FULL, !fail_sh);
+            const int cb = chunk_bytes(c);
+            const uint8_t *sb = stage + size_t(i % RMS_NS) * RMS_MAXR * RMS_ROWB;
+            const int64_t col0 = int64_t(c) * (RMS_CB / ESZ);     // first element of the chunk
+            if (cb == RMS_CB) {
+                // Full chunk.  Threads tid / 64 + 8p take row r, and the 64 threads of a row
+                // take its 8 (f32) or 16 (bf16) groups, LPG2 consecutive lanes per group; a lane
+                // holds two 16-byte vectors of its group, at element li*V of the group's first
+                // and second half, so each quarter-warp's shared-memory reads cover 128
+                // contiguous bytes (odd bf16 groups load their second half first, to take the
+                // other 16 banks).  Rows are whole warps, so every branch below is warp-uniform.
+                constexpr int LPG2 = GS / (2 * V), RPP = RMS_CTHREADS / 64;
+                constexpr int G = ESZ == 4 ? 4 : 1;          // passes in flight (bf16: register limit)
+                const int u = tid % 64, rr = tid / 64, gi = u / LPG2, li = u % LPG2;
+                const int h0 = ESZ == 2 ? (gi & 1) : 0;
+                const int eo0 = gi * GS + h0 * (GS / 2) + li * V, eo1 = gi * GS + (1 - h0) * (GS / 2) + li * V;
+                float wv[2 * V];
 #pragma unroll
-        for (int jj = 0; jj < JB; ++jj) {
-            if (j0 + jj >= NJ) break;                                // uniform across the CTA
-            const int f = tid + RMS_THREADS * (j0 + jj);
-            const bool act = f < NV;
-            float wv[V];
-            if (act) {
-                Vec<float>::widen(ld_nc_v4(w + f * V), wv);
-                if constexpr (V == 8) Vec<float>::widen(ld_nc_v4(w + f * V + 4), wv + 4);
-            }
-#pragma unroll
-            for (int r = 0; r < R; ++r) {
-                if (r >= rv) break;                                  // uniform across the CTA
-                const int64_t e = (r0 + r) * int64_t(dim) + int64_t(f) * V;
-                float o[V];
-                if (act) {
-                    float xv[V];
-                    Vec<T>::widen(xr[jj][r], xv);
-#pragma unroll
-                    for (int i = 0; i < V; ++i) o[i] = __fmul_rn(wv[i], __fmul_rn(ssr[r], xv[i]));
-                } else {
-#pragma unroll
-                    for (int i = 0; i < V; ++i) o[i] = 0.0f;
+                for (int k4 = 0; k4 < V / 4; ++k4) {
+                    Vec<float>::widen(ld_l1_v4(w + col0 + eo0 + 4 * k4), wv + 4 * k4);
+                    Vec<float>::widen(ld_l1_v4(w + col0 + eo1 + 4 * k4), wv + V + 4 * k4);
                 }
-                if constexpr (Q8) {
-                    float m = 0.0f;
+                for (int p0 = 0; p0 * RPP < rv; p0 += G) {
+                    float o[G][2 * V];
 #pragma unroll
-                    for (int i = 0; i < V; ++i) m = amax_fold(m, o[i]);
+                    for (int g = 0; g < G; ++g) {
+                        const int r = rr + (p0 + g) * RPP;
+                        if (!(live && r < rv)) continue;
+                        const uint8_t *row = sb + size_t(r) * RMS_ROWB;
+                        float xv[2 * V];
+                        Vec<T>::widen(*reinterpret_cast<const uint4 *>(row + eo0 * ESZ), xv);
+                        Vec<T>::widen(*reinterpret_cast<const uint4 *>(row + eo1 * ESZ), xv + V);
+                        const float ssr = ss_sh[r];
+                        const f2 ss2 = pk2(ssr, ssr);
 #pragma unroll
-                    for (int kk = LPG / 2; kk > 0; kk >>= 1) m = amax_merge(m, __shfl_xor_sync(FULL, m, kk));
-                    if (act) {
-                        const Q8Scale gs = q8_prepare(m);
-                        if constexpr (V == 4) st_cs_u32(q + e, q8_pack4(o, gs));
-                        else st_cs_v2(q + e, make_uint2(q8_pack4(o, gs), q8_pack4(o + 4, gs)));
-                        if ((lane % LPG) == 0) st_cs_f32(s + e / GS, gs.scale);
+                        for (int e = 0; e < 2 * V; e += 2)
+                            up2(mul2(pk2(wv[e], wv[e + 1]), mul2(ss2, pk2(xv[e], xv[e + 1]))), o[g][e], o[g][e + 1]);
                     }
-                } else {
-                    if (act) st_cs_v4(out + e, Vec<T>::narrow(o));
+#pragma unroll
+                    for (int g = 0; g < G; ++g) {
+                        const int r = rr + (p0 + g) * RPP;
+                        if (!(live && r < rv)) continue;
+                        const int64_t e = (r0 + r) * int64_t(dim) + col0;    // chunk start in the row
+                        if constexpr (Q8) {
+                            uint32_t codes[2 * V / 4];
+                            const float scale = q8_encode_lane<2 * V, LPG2>(o[g], codes);
+                            if constexpr (V == 4) {
+                                st_cs_u32(q + e + eo0, codes[0]);
+                                st_cs_u32(q + e + eo1, codes[1]);
+                            } else {
+                                st_cs_v2(q + e + eo0, make_uint2(codes[0], codes[1]));
+                                st_cs_v2(q + e + eo1, make_uint2(codes[2], codes[3]));
+                            }
+                            if (li == 0) st_cs_f32(s + ((e + gi * GS) >> 6), scale);
+                        } else {
+                            st_cs_v4(out + e + eo0, Vec<T>::narrow(o[g]));
+                            st_cs_v4(out + e + eo1, Vec<T>::narrow(o[g] + V));
+                        }
+                    }
+                }
+            } else {
+                // Partial last chunk: thread t handles 16-byte
+                // vectors f = t + RMS_CTHREADS*i of the [rv][vpr] chunk, U at a time.  vpr is a
+                // multiple of the group width (the chunk holds whole 64-groups), so one warp
+                // covers whole groups.
+                constexpr int U = 4;
+                const int vpr = cb / 16;           // 16-byte vectors per row in this chunk
+                const int nvec = rv * vpr;
+                for (int f0 = 0; f0 < nvec; f0 += RMS_CTHREADS * U) {
+                    float o[U][V];
+                    int64_t e[U];
+                    bool act[U];
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        const int f = f0 + u * RMS_CTHREADS + tid;
+                        act[u] = f < nvec && live;
+                        const int r = act[u] ? f / vpr : 0, v = act[u] ? f - (f / vpr) * vpr : 0;
+                        e[u] = (r0 + r) * int64_t(dim) + col0 + int64_t(v) * V;
+                        if (act[u]) {
+                            float wv[V], xv[V];
+                            Vec<float>::widen(ld_l1_v4(w + col0 + v * V), wv);
+                            if constexpr (V == 8) Vec<float>::widen(ld_l1_v4(w + col0 + v * V + 4), wv + 4);
+                            Vec<T>::widen(*reinterpret_cast<const uint4 *>(sb + size_t(r) * RMS_ROWB + v * 16), xv);
+                            const float ssr = ss_sh[r];
+#pragma unroll
+                            for (int i2 = 0; i2 < V; ++i2) o[u][i2] = __fmul_rn(wv[i2], __fmul_rn(ssr, xv[i2]));
+                        } else {
+#pragma unroll
+                            for (int i2 = 0; i2 < V; ++i2) o[u][i2] = 0.0f;
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < U; ++u) {
+                        if constexpr (Q8) {
+                            uint32_t codes[V / 4];
+                            const float scale = q8_encode_lane<V, NLPG>(o[u], codes);
+                            if (act[u]) {
+                                if constexpr (V == 4) st_cs_u32(q + e[u], codes[0]);
+                                else st_cs_v2(q + e[u], make_uint2(codes[0], codes[1]));
+                                if ((lane % NLPG) == 0) st_cs_f32(s + (e[u] >> 6), scale);
+                            }
+                        } else {
+                            if (act[u]) st_cs_v4(out + e[u], Vec<T>::narrow(o[u]));
+                        }
+                    }
                 }
             }
+            named_sync(1, RMS_CTHREADS);           // item i consumed by every compute warp
+            if (tid == 0) mbar_arrive(&empty[i % RMS_NS]);
         }
     }
 }
 
 template <typename T, bool Q8>
-static cudaError_t launch_rms_t(const T *x, const float *w, int64_t rows, int dim, int n_div, float eps, T *out, int8_t *q,
-                                float *s, uint32_t *status, cudaStream_t stream, int sms) {
-    // Rows per CTA: enough CTAs to keep every SM busy with several resident.
-    int R = 1;
-    if (rows >= int64_t(sms) * 64) R = 8;
-    else if (rows >= int64_t(sms) * 16) R = 4;
-    else if (rows >= int64_t(sms) * 4) R = 2;
-    const int64_t blocks = (rows + R - 1) / R;
-    if (blocks > 0x7fffffff) return cudaErrorInvalidValue;
-    const unsigned b = unsigned(blocks);
-    switch (R) {
-        case 8: rmsnorm_kernel<T, 8, Q8><<<b, RMS_THREADS, 0, stream>>>(x, w, rows, dim, n_div, eps, out, q, s, status); break;
-        case 4: rmsnorm_kernel<T, 4, Q8><<<b, RMS_THREADS, 0, stream>>>(x, w, rows, dim, n_div, eps, out, q, s, status); break;
-        case 2: rmsnorm_kernel<T, 2, Q8><<<b, RMS_THREADS, 0, stream>>>(x, w, rows, dim, n_div, eps, out, q, s, status); break;
-        default: rmsnorm_kernel<T, 1, Q8><<<b, RMS_THREADS, 0, stream>>>(x, w, rows, dim, n_div, eps, out, q, s, status); break;
-    }
+static cudaError_t launch_rms_t(const T *x, const float *w, int64_t rows, int dim, int n_div, float eps, T *out,
+                                int8_t *q, float *s, uint32_t *status, cudaStream_t stream, int sms) {
+    // Equal rows per SM: blocks of R <= 32 rows, the same number per SM, one CTA per SM.
+    const int64_t rows_per_sm = (rows + sms - 1) / sms;
+    const int64_t bps = (rows_per_sm + RMS_MAXR - 1) / RMS_MAXR;
+    const int R = int((rows_per_sm + bps - 1) / bps);
+    const int64_t nblocks = (rows + R - 1) / R;
+    const unsigned grid = unsigned(nblocks < sms ? nblocks : sms);
+    const int slot = 2 + (sizeof(T) == 4 ? 0 : 2) + (Q8 ? 1 : 0);
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(rmsnorm_kernel<T, Q8>), RMS_SMEM, slot);
+    if (e != cudaSuccess) return e;
+    rmsnorm_kernel<T, Q8><<<grid, RMS_THREADS, RMS_SMEM, stream>>>(x, w, rows, dim, n_div, eps, R, out, q, s, status);
     return cudaGetLastError();
 }
 

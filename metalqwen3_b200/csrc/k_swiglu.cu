@@ -82,16 +82,107 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const T *hb, const T *__res
     }
 }
 
+// The exact scalar chain for one element (the rare lanes the fast path flags).
+__device__ __forceinline__ float swiglu_exact(float a, float b, const ExpTab &tab) {
+    const float ex = expf_host(-a, tab);
+    return __fmul_rn(a, __fmul_rn(b, __frcp_rn(__fadd_rn(1.0f, ex))));
+}
+
+// Main kernel: 32 bytes of hb and hb2 per lane per step (8 f32 / 16 bf16), so a
+// 64-group spans 8 / 4 lanes.  Per element: the expf core (binary64, branch
+// free), then 1/(1+e) by a rcp.approx seed and two Newton steps, the last in
+// Markstein's exact-residual form (rcp_rn_ge1's arithmetic: correctly rounded
+// for 1 <= d < 2^120, checked against __frcp_rn on every such d), and the two
+// products.  Lanes holding a special expf input (|a| >= 88, NaN, inf)
+// or a huge d recompute their values with swiglu_exact before the group
+// reduction; codes come from q8_encode_lane.
+template <typename T, int U, bool Q8>
+__global__ void __launch_bounds__(256, sizeof(T) == 4 ? 4 : 2) swiglu_v8_kernel(const T *hb, const T *__restrict__ hb2, int64_t elems,
+                                                        T *out, int8_t *__restrict__ q, float *__restrict__ s) {
+    constexpr int N = Wide<T>::N;
+    constexpr int LPG = GS / N;
+    constexpr int STEP = 32 * N;
+    __shared__ ExpTab s_tab;
+    load_exp_table(s_tab);
+    __syncthreads();
+
+    const int lane = threadIdx.x & 31;
+    const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+    const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+    const int64_t nsteps = elems / STEP + ((elems % STEP) != 0);
+
+    for (int64_t st0 = warp * U; st0 < nsteps; st0 += nwarps * U) {
+        const int64_t e0 = st0 * STEP + lane * N;
+        U8 ra[U], rb[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int64_t e = e0 + int64_t(u) * STEP;
+            if (e < elems) {
+                ra[u] = ld_v8(hb + e);               // coherent: out may alias hb
+                rb[u] = ld_nc_v8(hb2 + e);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            if (st0 + u >= nsteps) break;            // warp-uniform
+            const int64_t e = e0 + int64_t(u) * STEP;
+            const bool ok = e < elems;
+            float o[N];
+            if (ok) {
+                float a[N], b[N];
+                Wide<T>::widen(ra[u], a);
+                Wide<T>::widen(rb[u], b);
+                bool slow = false;
+#pragma unroll
+                for (int i = 0; i < N; ++i) {
+                    const float na = -a[i];
+                    slow |= bool(q3_expf_special(na));
+                    const float d = __fadd_rn(1.0f, expf_core(na, s_tab));
+                    slow |= !(d < 0x1p120f);
+                    const float y0 = rcp_approx(d);
+                    const float y1 = __fmaf_rn(y0, __fmaf_rn(-d, y0, 1.0f), y0);
+                    const float y = __fmaf_rn(y1, __fmaf_rn(-d, y1, 1.0f), y1);
+                    o[i] = __fmul_rn(a[i], __fmul_rn(b[i], y));
+                }
+                if (__builtin_expect(slow, 0)) {
+#pragma unroll
+                    for (int i = 0; i < N; ++i) o[i] = swiglu_exact(a[i], b[i], s_tab);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < N; ++i) o[i] = 0.0f;
+            }
+            if constexpr (Q8) {
+                uint32_t codes[N / 4];
+                const float scale = q8_encode_lane<N, LPG>(o, codes);
+                if (!ok) continue;
+                if constexpr (N == 8) st_cs_v2(q + e, make_uint2(codes[0], codes[1]));
+                else st_cs_v4(q + e, make_uint4(codes[0], codes[1], codes[2], codes[3]));
+                if ((lane % LPG) == 0) st_cs_f32(s + (e >> 6), scale);
+            } else {
+                if (ok) st_cs_v8(out + e, Wide<T>::narrow(o));
+            }
+        }
+    }
+}
+
 template <typename T, bool Q8>
 static cudaError_t launch_swiglu_t(const T *hb, const T *hb2, int64_t elems, T *out, int8_t *q, float *s,
                                    cudaStream_t stream, int sms) {
     constexpr int U = 2;
-    constexpr int STEP = 32 * Vec<T>::N;
-    const int64_t steps = (elems + STEP - 1) / STEP;
+    const bool v8 = (elems % Wide<T>::N) == 0 && (reinterpret_cast<uintptr_t>(hb) % 32) == 0 &&
+                    (reinterpret_cast<uintptr_t>(hb2) % 32) == 0 &&
+                    (Q8 ? (reinterpret_cast<uintptr_t>(q) % (Wide<T>::N)) == 0
+                        : (reinterpret_cast<uintptr_t>(out) % 32) == 0);
+    const int step = 32 * (v8 ? Wide<T>::N : Vec<T>::N);
+    const int64_t steps = (elems + step - 1) / step;
     const int64_t warps = (steps + U - 1) / U;
     int64_t blocks = (warps + 7) / 8;
     if (blocks > int64_t(sms) * 8) blocks = int64_t(sms) * 8;
-    swiglu_kernel<T, U, Q8><<<unsigned(blocks), 256, 0, stream>>>(hb, hb2, elems, out, q, s);
+    if (v8)
+        swiglu_v8_kernel<T, U, Q8><<<unsigned(blocks), 256, 0, stream>>>(hb, hb2, elems, out, q, s);
+    else
+        swiglu_kernel<T, U, Q8><<<unsigned(blocks), 256, 0, stream>>>(hb, hb2, elems, out, q, s);
     return cudaGetLastError();
 }
 

@@ -141,15 +141,26 @@ Q3_HD double q3_hilo(uint32_t hi, uint32_t lo) { return q3_u2d(((uint64_t)hi << 
 Q3_HD uint32_t q3_dlo(double d) { return (uint32_t)q3_d2u(d); }
 #endif
 
+/* Inputs the core below does not cover: |x| >= 88, NaN, +-inf. */
+Q3_HD int q3_expf_special(float x) { return ((q3_f2u(x) >> 20) & 0x7ffu) >= 0x42bu; }
+
+/* The method's main path, valid when !q3_expf_special(x).  Branch-free, so a
+ * kernel can evaluate it for every element and patch the rare special inputs
+ * afterwards (for those it returns an unspecified finite or NaN value). */
+Q3_HD float q3_expf_core(float x, const uint32_t *tab_hi, const uint32_t *tab_lo);
+
 Q3_HD float q3_expf_fast(float x, const uint32_t *tab_hi, const uint32_t *tab_lo) {
     uint32_t ux = q3_f2u(x);
-    uint32_t abstop = (ux >> 20) & 0x7ffu;
-    if (abstop >= 0x42bu) {                        /* |x| >= 88 or x is NaN/inf */
+    if (q3_expf_special(x)) {                      /* |x| >= 88 or x is NaN/inf */
         if (ux == 0xff800000u) return 0.0f;
-        if (abstop >= 0x7f8u) return x + x;
+        if (((ux >> 20) & 0x7ffu) >= 0x7f8u) return x + x;
         if (x > 0x1.62e42ep6f) return (float)(Q3_EXP_SHIFT * Q3_EXP_SHIFT * Q3_EXP_SHIFT);
         if (x < -0x1.9fe368p6f) return 0.0f;
     }
+    return q3_expf_core(x, tab_hi, tab_lo);
+}
+
+Q3_HD float q3_expf_core(float x, const uint32_t *tab_hi, const uint32_t *tab_lo) {
     double xd = (double)x;
     double kd = Q3_FMA(Q3_EXP_INVLN2N, xd, Q3_EXP_SHIFT);
     uint32_t ki = q3_dlo(kd);

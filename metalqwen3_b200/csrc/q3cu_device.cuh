@@ -41,6 +41,14 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void *p) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
 }
+// Read-only data that a CTA re-reads many times (norm weights): non-coherent
+// path, cached in L1.
+__device__ __forceinline__ uint4 ld_l1_v4(const void *p) {
+    uint4 v;
+    asm volatile("ld.global.nc.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+    return v;
+}
 // Coherent load (data the same kernel may have written).
 __device__ __forceinline__ uint4 ld_v4(const void *p) {
     uint4 v;
@@ -197,6 +205,130 @@ __device__ __forceinline__ uint32_t q8_pack4(const float *o, const Q8Scale &g) {
 }
 
 // ---------------------------------------------------------------------------
+// 32-byte vectors (one 256-bit access per lane; sm_100) and packed f32 pairs
+// ---------------------------------------------------------------------------
+struct U8 { uint32_t w[8]; };
+
+__device__ __forceinline__ U8 ld_nc_v8(const void *p) {
+    U8 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                   "=r"(v.w[6]), "=r"(v.w[7]) : "l"(p));
+    return v;
+}
+__device__ __forceinline__ U8 ld_v8(const void *p) {
+    U8 v;
+    asm volatile("ld.global.v8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+                 : "=r"(v.w[0]), "=r"(v.w[1]), "=r"(v.w[2]), "=r"(v.w[3]), "=r"(v.w[4]), "=r"(v.w[5]),
+                   "=r"(v.w[6]), "=r"(v.w[7]) : "l"(p) : "memory");
+    return v;
+}
+__device__ __forceinline__ void st_cs_v8(void *p, const U8 &v) {
+    asm volatile("st.global.cs.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+                 :: "l"(p), "r"(v.w[0]), "r"(v.w[1]), "r"(v.w[2]), "r"(v.w[3]), "r"(v.w[4]), "r"(v.w[5]),
+                    "r"(v.w[6]), "r"(v.w[7]) : "memory");
+}
+
+// 32 bytes of T widened to float (8 f32 or 16 bf16), and back.
+template <typename T> struct Wide;
+template <> struct Wide<float> {
+    static constexpr int N = 8;
+    __device__ __forceinline__ static void widen(const U8 &u, float *o) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) o[i] = __uint_as_float(u.w[i]);
+    }
+    __device__ __forceinline__ static U8 narrow(const float *o) {
+        U8 u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) u.w[i] = __float_as_uint(o[i]);
+        return u;
+    }
+};
+template <> struct Wide<bf16raw> {
+    static constexpr int N = 16;
+    __device__ __forceinline__ static void widen(const U8 &u, float *o) {
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            o[2 * i] = bf16_to_f32(u.w[i] & 0xffffu);
+            o[2 * i + 1] = bf16_to_f32(u.w[i] >> 16);
+        }
+    }
+    __device__ __forceinline__ static U8 narrow(const float *o) {
+        U8 u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) u.w[i] = f32_to_bf16(o[2 * i]) | (f32_to_bf16(o[2 * i + 1]) << 16);
+        return u;
+    }
+};
+
+// Packed pairs of binary32 (sm_100 add/sub/mul/fma.rn.f32x2): each half is an
+// independent IEEE operation with round-to-nearest, as the scalar forms.
+typedef uint64_t f2;
+__device__ __forceinline__ f2 pk2(float a, float b) {
+    f2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+    return r;
+}
+__device__ __forceinline__ void up2(f2 p, float &a, float &b) { asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(p)); }
+__device__ __forceinline__ f2 add2(f2 a, f2 b) { f2 r; asm("add.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b)); return r; }
+__device__ __forceinline__ f2 sub2(f2 a, f2 b) { f2 r; asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b)); return r; }
+__device__ __forceinline__ f2 mul2(f2 a, f2 b) { f2 r; asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b)); return r; }
+__device__ __forceinline__ f2 fma2(f2 a, f2 b, f2 c) {
+    f2 r;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
+    return r;
+}
+
+// Q8_0 codes of the N values one lane holds of a 64-group that spans LPG lanes
+// (N * LPG == 64).  The fast path is the one of q8_prepare/q8_code_g, done on
+// pairs, with the code read from the low byte of (q + 1.5*2^23): for
+// |k| < 2^22 that float's bit pattern is 0x4B400000 + k.  Lanes whose group
+// needs the exact division (tiny/huge/zero scale) or that have a quotient near
+// a tie redo their codes with q8_code afterwards (lane-local, rare).
+// Returns the group scale; codes[] receives N/4 little-endian words.
+template <int N, int LPG>
+__device__ __forceinline__ float q8_encode_lane(const float *o, uint32_t *codes) {
+    static_assert(N * LPG == GS, "a group is 64 values");
+    float m = 0.0f;
+#pragma unroll
+    for (int i = 0; i < N; ++i) m = fmaxf(m, fabsf(o[i]));           // NaN never wins; starts at 0
+#pragma unroll
+    for (int k = LPG / 2; k > 0; k >>= 1) m = fmaxf(m, __shfl_xor_sync(FULL, m, k));
+    const float c = 0x1.020408p-7f;
+    const float s0 = __fmul_rn(m, c);
+    float scale = __fmaf_rn(__fmaf_rn(-s0, 127.0f, m), c, s0);
+    const bool exact_group = !(m >= 0x1p-90f && m <= 0x1p+100f);
+    if (__builtin_expect(exact_group, 0)) scale = q8_scale(m);
+    const float inv = rcp_approx(scale);
+    const f2 inv2 = pk2(inv, inv), M2 = pk2(12582912.0f, 12582912.0f);
+    bool fix = exact_group;
+    uint32_t tb[N];
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+        const f2 qa = mul2(pk2(o[i], o[i + 1]), inv2);
+        const f2 t = add2(qa, M2);
+        const f2 d = sub2(qa, sub2(t, M2));
+        float d0, d1, t0, t1;
+        up2(d, d0, d1);
+        up2(t, t0, t1);
+        fix |= !(fabsf(d0) <= 0.49993896484375f) | !(fabsf(d1) <= 0.49993896484375f);
+        tb[i] = __float_as_uint(t0);
+        tb[i + 1] = __float_as_uint(t1);
+    }
+#pragma unroll
+    for (int w = 0; w < N / 4; ++w)
+        codes[w] = __byte_perm(__byte_perm(tb[4 * w], tb[4 * w + 1], 0x0040),
+                               __byte_perm(tb[4 * w + 2], tb[4 * w + 3], 0x0040), 0x5410);
+    if (__builtin_expect(fix, 0)) {
+#pragma unroll
+        for (int w = 0; w < N / 4; ++w)
+            codes[w] = q8_code(o[4 * w], scale) | (q8_code(o[4 * w + 1], scale) << 8) |
+                       (q8_code(o[4 * w + 2], scale) << 16) | (q8_code(o[4 * w + 3], scale) << 24);
+    }
+    return scale;
+}
+
+// ---------------------------------------------------------------------------
 // expf with the host libm's bits (q3_expf.h); the table lives in shared memory
 // ---------------------------------------------------------------------------
 static __constant__ uint64_t c_exp_tab[32] = Q3_EXP2_TAB32_INIT;
@@ -216,6 +348,7 @@ __device__ __forceinline__ void load_exp_table(ExpTab &t) {
     }
 }
 __device__ __forceinline__ float expf_host(float x, const ExpTab &t) { return q3_expf_fast(x, t.hi, t.lo); }
+__device__ __forceinline__ float expf_core(float x, const ExpTab &t) { return q3_expf_core(x, t.hi, t.lo); }
 
 // ---------------------------------------------------------------------------
 // TMA bulk copies (cp.async.bulk, no tensor map, no multicast) and mbarriers
@@ -232,6 +365,16 @@ __device__ __forceinline__ void mbar_init_fence() {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
                  :: "r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_addr(bar)) : "memory");
+}
+// Barrier `id` (1..15) over the first `threads` threads of the CTA (a multiple of 32).
+__device__ __forceinline__ void named_sync(int id, int threads) {
+    asm volatile("bar.sync %0, %1;" :: "r"(id), "r"(threads) : "memory");
+}
+__device__ __forceinline__ void prefetch_l1(const void *p) {
+    asm volatile("prefetch.global.L1 [%0];" :: "l"(p));
 }
 __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
