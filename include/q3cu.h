@@ -176,6 +176,26 @@ q3cu_status q3cu_execute_quantize(q3cu_ctx *ctx, int8_t *q, float *s, const floa
 q3cu_status q3cu_execute_embedding(q3cu_ctx *ctx, float *out, const int8_t *q, const float *s,
                                    int token, int dim);
 
+/* ---- allocation-free executeRMSNorm ----------------------------------------
+ * No counterpart in the reference.  Same result as q3cu_execute_rmsnorm, for
+ * callers that must not allocate device memory when they normalise a row: it
+ * takes no context and stages x, w and the output in a fixed array inside the
+ * library's device image (Q3CU_STATIC_SCRATCH_BYTES per device) instead of a
+ * cudaMalloc'd buffer.  Synchronous on `stream` (NULL: the legacy default
+ * stream) of the current device.
+ *   - size must be 1..Q3CU_STATIC_RMSNORM_MAX; larger sizes return
+ *     Q3CU_ERR_INVALID and touch nothing.
+ *   - The first call on a device looks up the array's address (and loads the
+ *     library's device code if that has not happened yet); make one call per
+ *     device before any stream capture.
+ *   - There is one array per device: calls that overlap on the same device
+ *     (several host threads or streams) race and must be serialised by the
+ *     caller. */
+#define Q3CU_STATIC_RMSNORM_MAX 16384
+#define Q3CU_STATIC_SCRATCH_BYTES (256 + 3 * 4 * Q3CU_STATIC_RMSNORM_MAX)
+q3cu_status q3cu_execute_rmsnorm_static(float *output, const float *input, const float *weight,
+                                        int size, q3cu_stream stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -508,3 +508,110 @@ q3cu_status q3cu_execute_embedding(q3cu_ctx *ctx, float *out, const int8_t *q, c
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// executeRMSNorm without device allocation (q3cu_execute_rmsnorm_static)
+// ---------------------------------------------------------------------------
+// q3cu_execute_rmsnorm stages its row in a per-context buffer that grows with
+// cudaMalloc, and creating the context allocates too.  Some callers cannot
+// allocate at the moment they normalise a row: an engine that reserved all of
+// the device's memory for weights and KV cache up front (a new allocation
+// fails, or fragments its pool); a decode loop with a latency budget, where
+// cudaMalloc / cudaFree may synchronise the device and stall other streams; a
+// host application that forbids allocations once it is running.  This path
+// stages through a fixed array in the library's own device image instead, and
+// reuses the RMSNorm launcher unchanged.
+//
+// Layout of the array (one instance per device, zero when the module loads):
+//   [0, 4)                 status word (Q3CU_DEV_* bits).  Must be 0 when the
+//                          kernel starts: every call clears it first.
+//   [256, 256 + R)         x, then zeros up to a multiple of 4 elements
+//   [256 + R, 256 + 2R)    w, same zero tail
+//   [256 + 2R, 256 + 3R)   output
+// with R = 4 * Q3CU_STATIC_RMSNORM_MAX bytes.  The zero tails (elements
+// size..padded-1 of x and w) must be zero when the kernel runs, since the
+// kernel sums over the padded row: every call writes them.
+namespace {
+
+constexpr size_t kStaticRow = size_t(4) * Q3CU_STATIC_RMSNORM_MAX;
+static_assert(Q3CU_STATIC_SCRATCH_BYTES == 256 + 3 * kStaticRow, "scratch layout");
+
+struct StaticScratch {
+    std::atomic<uint8_t *> base{nullptr};
+    int sms = 0;
+};
+StaticScratch g_static[64];
+std::mutex g_static_mu;
+
+}  // namespace
+
+static __device__ __align__(256) uint8_t g_static_scratch[Q3CU_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+// The array's address on `dev` (the current device), looked up on the first
+// call for that device.
+q3cu_status static_scratch(int dev, uint8_t **base, int *sms) {
+    if (dev < 0 || dev >= 64) return fail(Q3CU_ERR_DEVICE, "device %d out of range", dev);
+    StaticScratch &s = g_static[dev];
+    uint8_t *b = s.base.load(std::memory_order_acquire);
+    if (!b) {
+        std::lock_guard<std::mutex> lock(g_static_mu);
+        b = s.base.load(std::memory_order_acquire);
+        if (!b) {
+            int major = 0, minor = 0, n = 0;
+            cudaError_t e = cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+            if (e == cudaSuccess) e = cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+            if (e == cudaSuccess) e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+            if (major != 10 || minor != 0)
+                return fail(Q3CU_ERR_DEVICE, "device %d is sm_%d%d; this library is built for sm_100a only", dev, major,
+                            minor);
+            void *p = nullptr;
+            e = cudaGetSymbolAddress(&p, g_static_scratch);
+            if (e != cudaSuccess) return cuda_fail(e, "cudaGetSymbolAddress (static scratch)");
+            s.sms = n;
+            b = static_cast<uint8_t *>(p);
+            s.base.store(b, std::memory_order_release);
+        }
+    }
+    *base = b;
+    *sms = s.sms;
+    return Q3CU_OK;
+}
+
+}  // namespace
+
+extern "C" q3cu_status q3cu_execute_rmsnorm_static(float *output, const float *input, const float *weight, int size,
+                                                   q3cu_stream stream) {
+    if (!output || !input || !weight || size <= 0)
+        return fail(Q3CU_ERR_INVALID, "executeRMSNorm (static scratch): bad argument");
+    if (size > Q3CU_STATIC_RMSNORM_MAX)
+        return fail(Q3CU_ERR_INVALID, "executeRMSNorm (static scratch): size %d exceeds the limit of %d elements", size,
+                    Q3CU_STATIC_RMSNORM_MAX);
+    int dev = -1;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+    uint8_t *base = nullptr;
+    int sms = 0;
+    if (q3cu_status st = static_scratch(dev, &base, &sms)) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int padded = (size + 3) & ~3;
+    uint32_t *d_status = reinterpret_cast<uint32_t *>(base);
+    float *dx = reinterpret_cast<float *>(base + 256), *dw = reinterpret_cast<float *>(base + 256 + kStaticRow),
+          *dout = reinterpret_cast<float *>(base + 256 + 2 * kStaticRow);
+    TRY_CUDA(cudaMemsetAsync(d_status, 0, 4, s), "memset (status)");
+    if (padded != size) {
+        TRY_CUDA(cudaMemsetAsync(dx + size, 0, size_t(padded - size) * 4, s), "memset (tail)");
+        TRY_CUDA(cudaMemsetAsync(dw + size, 0, size_t(padded - size) * 4, s), "memset (tail)");
+    }
+    TRY_CUDA(cudaMemcpyAsync(dx, input, size_t(size) * 4, cudaMemcpyHostToDevice, s), "H2D");
+    TRY_CUDA(cudaMemcpyAsync(dw, weight, size_t(size) * 4, cudaMemcpyHostToDevice, s), "H2D");
+    TRY_CUDA(q3::launch_rmsnorm_padded(dx, dw, size, padded, dout, d_status, s, sms), "rmsnorm");
+    TRY_CUDA(cudaMemcpyAsync(output, dout, size_t(size) * 4, cudaMemcpyDeviceToHost, s), "D2H");
+    uint32_t flags = 0;
+    TRY_CUDA(cudaMemcpyAsync(&flags, d_status, 4, cudaMemcpyDeviceToHost, s), "D2H (status)");
+    TRY_CUDA(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+    if (flags & Q3CU_DEV_TIMEOUT) return fail(Q3CU_ERR_TIMEOUT, "executeRMSNorm (static scratch): a device wait gave up");
+    return Q3CU_OK;
+}
