@@ -90,14 +90,13 @@ __device__ __forceinline__ float swiglu_exact(float a, float b, const ExpTab &ta
 
 // Main kernel: 32 bytes of hb and hb2 per lane per step (8 f32 / 16 bf16), so a
 // 64-group spans 8 / 4 lanes.  Per element: the expf core (binary64, branch
-// free), then 1/(1+e) by a rcp.approx seed and two Newton steps, the last in
-// Markstein's exact-residual form (rcp_rn_ge1's arithmetic: correctly rounded
-// for 1 <= d < 2^120, checked against __frcp_rn on every such d), and the two
-// products.  Lanes holding a special expf input (|a| >= 88, NaN, inf)
-// or a huge d recompute their values with swiglu_exact before the group
-// reduction; codes come from q8_encode_lane.
+// free), then 1/(1+e) by a rcp.approx seed and one Markstein correction step
+// (rcp_rn_1to2p120: correctly rounded for 1 <= d < 2^120, checked against
+// __frcp_rn on every such d), and the two products, element pairs in packed
+// f32x2 arithmetic.  Lanes holding an |a| >= 83 (or NaN) recompute their values
+// with swiglu_exact before the group reduction; codes come from q8_encode_lane.
 template <typename T, int U, bool Q8>
-__global__ void __launch_bounds__(256, sizeof(T) == 4 ? 4 : 2) swiglu_v8_kernel(const T *hb, const T *__restrict__ hb2, int64_t elems,
+__global__ void __launch_bounds__(256, sizeof(T) == 4 ? 3 : 2) swiglu_v8_kernel(const T *hb, const T *__restrict__ hb2, int64_t elems,
                                                         T *out, int8_t *__restrict__ q, float *__restrict__ s) {
     constexpr int N = Wide<T>::N;
     constexpr int LPG = GS / N;
@@ -132,17 +131,21 @@ __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 4 : 2) swiglu_v8_kernel(
                 float a[N], b[N];
                 Wide<T>::widen(ra[u], a);
                 Wide<T>::widen(rb[u], b);
+                // |a| < 83 keeps -a off expf's special inputs (|x| >= 88, NaN, inf) and
+                // d = 1 + e^-a inside [1, 2^120), where rcp_rn_1to2p120's one correction
+                // step is exact.  Pairs use packed f32x2 arithmetic; nd = -1 - e is -d
+                // exactly (round-to-nearest is symmetric), so d's negation costs nothing.
                 bool slow = false;
+                const f2 NEG1 = pk2(-1.0f, -1.0f), ONE = pk2(1.0f, 1.0f);
 #pragma unroll
-                for (int i = 0; i < N; ++i) {
-                    const float na = -a[i];
-                    slow |= bool(q3_expf_special(na));
-                    const float d = __fadd_rn(1.0f, expf_core(na, s_tab));
-                    slow |= !(d < 0x1p120f);
-                    const float y0 = rcp_approx(d);
-                    const float y1 = __fmaf_rn(y0, __fmaf_rn(-d, y0, 1.0f), y0);
-                    const float y = __fmaf_rn(y1, __fmaf_rn(-d, y1, 1.0f), y1);
-                    o[i] = __fmul_rn(a[i], __fmul_rn(b[i], y));
+                for (int i = 0; i < N; i += 2) {
+                    slow |= !(fabsf(a[i]) < 83.0f) | !(fabsf(a[i + 1]) < 83.0f);
+                    const f2 nd = sub2(NEG1, pk2(expf_core(-a[i], s_tab), expf_core(-a[i + 1], s_tab)));
+                    float nd0, nd1;
+                    up2(nd, nd0, nd1);
+                    const f2 y0 = pk2(rcp_approx(-nd0), rcp_approx(-nd1));
+                    const f2 y = fma2(y0, fma2(nd, y0, ONE), y0);      // y0 + y0*(1 - d*y0)
+                    up2(mul2(pk2(a[i], a[i + 1]), mul2(pk2(b[i], b[i + 1]), y)), o[i], o[i + 1]);
                 }
                 if (__builtin_expect(slow, 0)) {
 #pragma unroll
@@ -178,7 +181,8 @@ static cudaError_t launch_swiglu_t(const T *hb, const T *hb2, int64_t elems, T *
     const int64_t steps = (elems + step - 1) / step;
     const int64_t warps = (steps + U - 1) / U;
     int64_t blocks = (warps + 7) / 8;
-    if (blocks > int64_t(sms) * 8) blocks = int64_t(sms) * 8;
+    const int per_sm = v8 ? (sizeof(T) == 4 ? 3 : 2) : 8;    // v8: one resident wave (its launch bounds)
+    if (blocks > int64_t(sms) * per_sm) blocks = int64_t(sms) * per_sm;
     if (v8)
         swiglu_v8_kernel<T, U, Q8><<<unsigned(blocks), 256, 0, stream>>>(hb, hb2, elems, out, q, s);
     else

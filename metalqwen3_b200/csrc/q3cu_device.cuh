@@ -162,6 +162,15 @@ __device__ __forceinline__ float rcp_rn_ge1(float d) {
     return __fmaf_rn(y1, __fmaf_rn(-d, y1, 1.0f), y1);
 }
 
+// One correction step is enough on [1, 2^120): the rcp.approx seed is within
+// one ulp of 1/d there, and y0 + y0*(1 - d*y0) (two fused multiply-adds) is
+// then equal to __frcp_rn(d) for every binary32 d in that range (exhaustive
+// check in tests/test_device_math.py).  The caller guarantees the range.
+__device__ __forceinline__ float rcp_rn_1to2p120(float d) {
+    const float y0 = rcp_approx(d);
+    return __fmaf_rn(y0, __fmaf_rn(-d, y0, 1.0f), y0);
+}
+
 // Per-group state for the fast code path.
 //  * scale = RN(wmax/127): one multiply by RN(1/127) = 0x1.020408p-7 and one
 //    FMA-based correction (Markstein); equal to the IEEE quotient for every

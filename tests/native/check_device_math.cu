@@ -20,6 +20,17 @@ __global__ void check_rcp(uint32_t lo, uint32_t hi, unsigned long long *bad) {
     if (n) atomicAdd(bad, n);
 }
 
+// (1b) the one-step form on [1, 2^120)
+__global__ void check_rcp1(uint32_t lo, uint32_t hi, unsigned long long *bad) {
+    unsigned long long n = 0;
+    for (uint64_t u = lo + uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; u < hi;
+         u += uint64_t(gridDim.x) * blockDim.x) {
+        const float d = __uint_as_float(uint32_t(u));
+        if (__float_as_uint(rcp_rn_1to2p120(d)) != __float_as_uint(__frcp_rn(d))) ++n;
+    }
+    if (n) atomicAdd(bad, n);
+}
+
 // (2) scale and codes of the fast path == the exact path
 //     q8_scale (IEEE m/127) and q8_code (IEEE division + round half away)
 __device__ __forceinline__ uint32_t hash32(uint32_t x) {
@@ -60,14 +71,15 @@ __global__ void check_q8(uint32_t nm, unsigned long long *bad_scale, unsigned lo
 
 int main() {
     unsigned long long *d;
-    cudaMalloc(&d, 3 * sizeof(unsigned long long));
-    cudaMemset(d, 0, 3 * sizeof(unsigned long long));
+    cudaMalloc(&d, 4 * sizeof(unsigned long long));
+    cudaMemset(d, 0, 4 * sizeof(unsigned long long));
     check_rcp<<<148 * 16, 256>>>(0x3f800000u, 0x7f800001u, d);           // [1, +inf]
     check_q8<<<148 * 8, 128>>>(1u << 20, d + 1, d + 2);
+    check_rcp1<<<148 * 16, 256>>>(0x3f800000u, 0x7b800000u, d + 3);     // [1, 2^120)
     cudaError_t e = cudaDeviceSynchronize();
-    unsigned long long h[3] = {~0ull, ~0ull, ~0ull};
+    unsigned long long h[4] = {~0ull, ~0ull, ~0ull, ~0ull};
     cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) { printf("cuda error %s\n", cudaGetErrorString(e)); return 1; }
-    printf("%llu %llu %llu\n", h[0], h[1], h[2]);
+    printf("%llu %llu %llu %llu\n", h[0], h[1], h[2], h[3]);
     return 0;
 }

@@ -3,7 +3,8 @@
 * Q8_0 scale RN(wmax/127) by a Markstein correction step == IEEE division
   for every binary32 wmax in [2^-100, 2^100]  (CPU, exhaustive, fmaf);
 * on the GPU (tests/native/check_device_math.cu, built with nvcc):
-  the Markstein reciprocal == __frcp_rn for every binary32 d >= 1, and the
+  the Markstein reciprocal == __frcp_rn for every binary32 d >= 1 (two
+  steps) and every d in [1, 2^120) (one step), and the
   multiply-by-reciprocal code path == the IEEE-division path on 2^20 random
   scales x values placed on and around every rounding tie.
 """
@@ -59,7 +60,8 @@ def test_fast_device_math_on_gpu():
                         "-I", CSRC, "-I", os.path.join(ROOT, "include"),
                         os.path.join(ROOT, "tests", "native", "check_device_math.cu"), "-o", exe], check=True)
         out = subprocess.run([exe], check=True, capture_output=True, text=True, timeout=300).stdout.split()
-    bad_rcp, bad_scale, bad_code = map(int, out[:3])
+    bad_rcp, bad_scale, bad_code, bad_rcp1 = map(int, out[:4])
     assert bad_rcp == 0, f"{bad_rcp} binary32 d >= 1 where the Markstein reciprocal != __frcp_rn"
+    assert bad_rcp1 == 0, f"{bad_rcp1} binary32 d in [1, 2^120) where the one-step reciprocal != __frcp_rn"
     assert bad_scale == 0, f"{bad_scale} scales differ from the IEEE quotient"
     assert bad_code == 0, f"{bad_code} codes differ between the fast and the exact path"
