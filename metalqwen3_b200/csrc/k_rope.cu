@@ -9,15 +9,21 @@
 //                   v[j] = x*c - y*s;  v[j+hd/2] = x*s + y*c
 //
 // q [T][n_heads][128] and k [T][n_kv][128] are flat lists of 128-element head
-// rows.  A warp owns a tile of 16 consecutive head rows of one tensor:
-//   * lane i bulk-copies head row i into a padded shared-memory slot (TMA,
-//     one mbarrier per buffer; two buffers per warp so the next tile streams
-//     in while this one is processed);
+// rows.  A warp owns a tile of 32 consecutive head rows of one tensor, one row
+// per lane:
+//   * the warp copies the tile (one contiguous 16 KB / 8 KB range) into 32
+//     padded shared-memory row slots with 16-byte cp.async copies, 512 bytes per
+//     instruction; two buffers per warp, so the next tile streams in while this
+//     one is processed.  (A bulk copy per 512-byte row costs ~30 ns of
+//     copy-engine time per row per SM, more than the HBM time of the row.)
 //   * lane i runs row i's sum of squares in index order (the reference's
 //     rounding sequence, so the normalised values are bit-exact);
-//   * then the warp walks the 16 rows: lane l rotates the pairs (2l, 2l+64)
-//     and (2l+1, 2l+65), reading the row from shared memory and writing it
-//     back to HBM with coalesced stores.
+//   * the warp fills a table with cos/sin of every token the tile touches
+//     (two sincosf per lane per token), then lane i normalises and rotates
+//     its own row in place: 64 independent pairs per lane, 16-byte shared
+//     memory accesses (the row padding puts the 32 lanes on different banks;
+//     table and weight reads are broadcasts);
+//   * the warp writes the tile back to HBM with coalesced 16-byte stores.
 // freq_j comes from the host (the C library's powf, the reference's own
 // call); the angle pos*freq_j is the same binary32 product; cos/sin are CUDA's
 // sincosf (a few ulp from the host's cosf/sinf, inside the 1e-5 tolerance).
@@ -26,55 +32,78 @@
 namespace q3 {
 
 constexpr int HD = 128;
-constexpr int ROPE_WARPS = 12;                   // 12 warps x 2 tiles of 16 rows: 203 KB (f32), 104 KB (bf16)
-constexpr int ROPE_TILE = 16;
-
-template <typename T>
-__device__ __forceinline__ void load_pair(const uint8_t *rowp, int j, float &a, float &b) {
-    if constexpr (sizeof(T) == 4) {
-        const float2 v = *reinterpret_cast<const float2 *>(rowp + j * 4);
-        a = v.x; b = v.y;
-    } else {
-        const uint32_t v = *reinterpret_cast<const uint32_t *>(rowp + j * 2);
-        a = bf16_to_f32(v & 0xffffu); b = bf16_to_f32(v >> 16);
-    }
+constexpr int ROPE_TILE = 32;                    // head rows per warp tile (one per lane)
+constexpr int ROPE_TOKS = 8;                     // tokens in a warp's cos/sin table (32 rows / 4 heads)
+constexpr int ROPE_TABB = 2 * (HD / 2) * 4 + 16; // one token: cos[64], sin[64], padding
+template <typename T> __host__ __device__ constexpr int rope_rowb() { return HD * int(sizeof(T)) + 16; }
+template <typename T> __host__ __device__ constexpr int rope_warp_bytes() {
+    return 2 * ROPE_TILE * rope_rowb<T>() + ROPE_TOKS * ROPE_TABB;
 }
+// Warps per CTA (one CTA per SM): 6 x 38,016 B (f32), 10 x 21,632 B (bf16).
+template <typename T> __host__ __device__ constexpr int rope_warps() { return sizeof(T) == 4 ? 6 : 10; }
 
+// Normalises and rotates one head row in place (lane-private).  Same operation
+// order as the reference: x' = w_lo*(ss*x), y' = w_hi*(ss*y),
+// x'' = x'c - y's, y'' = x's + y'c, each product and sum rounded once.
 template <typename T>
-__device__ __forceinline__ void store_pair(T *p, float a, float b) {
-    if constexpr (sizeof(T) == 4) {
-        st_cs_v2(p, make_uint2(__float_as_uint(a), __float_as_uint(b)));
-    } else {
-        st_cs_u32(p, f32_to_bf16(a) | (f32_to_bf16(b) << 16));
-    }
-}
-
-template <typename T>
-__global__ void __launch_bounds__(ROPE_WARPS * 32) qk_norm_rope_kernel(
-    T *q, T *k, const int32_t *__restrict__ pos, int64_t q_rows, int64_t k_rows, int n_heads, int n_kv,
-    const float *__restrict__ q_norm, const float *__restrict__ k_norm, InvFreq invf, float eps, uint32_t *status) {
+__device__ __forceinline__ void rotate_row(uint8_t *row, const float *w, const float *cs, float ss) {
+    constexpr int P = Vec<T>::N;                 // pairs per 16-byte access (4 f32, 8 bf16)
     constexpr int ESZ = sizeof(T);
+    const f2 ss2 = pk2(ss, ss);
+#pragma unroll 2
+    for (int j = 0; j < HD / 2; j += P) {
+        uint4 *px = reinterpret_cast<uint4 *>(row + j * ESZ);
+        uint4 *py = reinterpret_cast<uint4 *>(row + (HD / 2 + j) * ESZ);
+        float x[P], y[P], wl[P], wh[P], c[P], s[P], a[P], b[P];
+        Vec<T>::widen(*px, x);
+        Vec<T>::widen(*py, y);
+#pragma unroll
+        for (int i = 0; i < P; i += 4) {
+            Vec<float>::widen(*reinterpret_cast<const uint4 *>(w + j + i), wl + i);
+            Vec<float>::widen(*reinterpret_cast<const uint4 *>(w + HD / 2 + j + i), wh + i);
+            Vec<float>::widen(*reinterpret_cast<const uint4 *>(cs + j + i), c + i);
+            Vec<float>::widen(*reinterpret_cast<const uint4 *>(cs + HD / 2 + j + i), s + i);
+        }
+#pragma unroll
+        for (int i = 0; i < P; i += 2) {
+            const f2 xn = mul2(pk2(wl[i], wl[i + 1]), mul2(ss2, pk2(x[i], x[i + 1])));
+            const f2 yn = mul2(pk2(wh[i], wh[i + 1]), mul2(ss2, pk2(y[i], y[i + 1])));
+            const f2 c2 = pk2(c[i], c[i + 1]), s2 = pk2(s[i], s[i + 1]);
+            up2(sub2(mul2(xn, c2), mul2(yn, s2)), a[i], a[i + 1]);
+            up2(add2(mul2(xn, s2), mul2(yn, c2)), b[i], b[i + 1]);
+        }
+        *px = Vec<T>::narrow(a);
+        *py = Vec<T>::narrow(b);
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(rope_warps<T>() * 32, 1) qk_norm_rope_kernel(
+    T *q, T *k, const int32_t *__restrict__ pos, int64_t q_rows, int64_t k_rows, int n_heads, int n_kv,
+    const float *__restrict__ q_norm, const float *__restrict__ k_norm, InvFreq invf, float eps) {
+    constexpr int ESZ = sizeof(T);
+    constexpr int RW = rope_warps<T>();
     constexpr int ROWBYTES = HD * ESZ;
-    constexpr int ROWB = ROWBYTES + 16;                 // padded: lanes hit distinct banks
+    constexpr int ROWB = rope_rowb<T>();                // padded: lane-per-row accesses hit distinct banks
+    constexpr int CPR = ROWBYTES / 16;                  // 16-byte chunks per row (32 / 16)
     constexpr int V = Vec<T>::N;
     extern __shared__ __align__(128) uint8_t smem[];
-    __shared__ __align__(8) uint64_t bars[ROPE_WARPS][2];
+    __shared__ __align__(16) float wsh[2][HD];          // q_norm, k_norm
 
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    uint8_t *buf0 = smem + size_t(wid) * 2 * ROPE_TILE * ROWB;
-    uint64_t *bar = bars[wid];
-    if (lane == 0) {
-        mbar_init(&bar[0], 1);
-        mbar_init(&bar[1], 1);
-        mbar_init_fence();
+    uint8_t *buf0 = smem + size_t(wid) * rope_warp_bytes<T>();
+    uint8_t *tab = buf0 + 2 * ROPE_TILE * ROWB;
+    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
+        wsh[0][i] = q_norm[i];
+        wsh[1][i] = k_norm[i];
     }
-    __syncwarp();
+    __syncthreads();
 
     const int64_t q_tiles = (q_rows + ROPE_TILE - 1) / ROPE_TILE;
     const int64_t k_tiles = (k_rows + ROPE_TILE - 1) / ROPE_TILE;
     const int64_t ntiles = q_tiles + k_tiles;
-    const int64_t gw = int64_t(blockIdx.x) * ROPE_WARPS + wid;
-    const int64_t GW = int64_t(gridDim.x) * ROPE_WARPS;
+    const int64_t gw = int64_t(blockIdx.x) * RW + wid;
+    const int64_t GW = int64_t(gridDim.x) * RW;
 
     // per-lane frequencies for j = 2*lane, 2*lane+1
     const float f0 = invf.v[2 * lane], f1 = invf.v[2 * lane + 1];
@@ -87,37 +116,37 @@ __global__ void __launch_bounds__(ROPE_WARPS * 32) qk_norm_rope_kernel(
         nvalid = left < ROPE_TILE ? int(left) : ROPE_TILE;
         heads = isq ? n_heads : n_kv;
     };
-    auto issue = [&](int64_t t, int b) {
-        T *base; int64_t row0; int nvalid, heads;
-        tile_info(t, base, row0, nvalid, heads);
-        if (lane == 0) mbar_arrive_expect_tx(&bar[b], uint32_t(nvalid) * ROWBYTES);
-        __syncwarp();
-        if (lane < nvalid)
-            bulk_g2s(buf0 + size_t(b) * ROPE_TILE * ROWB + size_t(lane) * ROWB,
-                     reinterpret_cast<const uint8_t *>(base) + (row0 + lane) * ROWBYTES, ROWBYTES, &bar[b]);
+    // Copies tile t into buffer b and commits them as one group (an empty group
+    // when t is past the end, so every lane's group count stays in step).
+    auto load_tile = [&](int64_t t, int b) {
+        if (t < ntiles) {
+            T *base; int64_t row0; int nvalid, heads;
+            tile_info(t, base, row0, nvalid, heads);
+            const uint8_t *src = reinterpret_cast<const uint8_t *>(base + row0 * HD);
+            uint8_t *dst = buf0 + size_t(b) * ROPE_TILE * ROWB;
+            for (int c = lane; c < nvalid * CPR; c += 32)
+                cp_async16(dst + (c / CPR) * ROWB + (c % CPR) * 16, src + size_t(c) * 16);
+        }
+        cp_async_commit();
     };
 
-    if (gw < ntiles) issue(gw, 0);
+    load_tile(gw, 0);
     int64_t kk = 0;
     for (int64_t t = gw; t < ntiles; t += GW, ++kk) {
         const int b = int(kk & 1);
-        const int64_t tn = t + GW;
-        if (tn < ntiles) issue(tn, b ^ 1);
-        const bool ok = __all_sync(FULL, mbar_wait(&bar[b], uint32_t(kk >> 1) & 1u, lane == 0 ? status : nullptr));
-        if (!ok) {
-            // drain the prefetch (bounded) and leave; the rows stay unmodified
-            if (tn < ntiles) mbar_wait(&bar[b ^ 1], uint32_t((kk + 1) >> 1) & 1u, nullptr);
-            return;
-        }
+        load_tile(t + GW, b ^ 1);
+        cp_async_wait<1>();                        // this lane's copies of tile t have landed
+        __syncwarp();                              // ... and every other lane's
         T *base; int64_t row0; int nvalid, heads;
         tile_info(t, base, row0, nvalid, heads);
-        const float *nw = (t < q_tiles) ? q_norm : k_norm;
-        const uint8_t *tb = buf0 + size_t(b) * ROPE_TILE * ROWB;
+        const float *w = wsh[t < q_tiles ? 0 : 1];
+        uint8_t *tb = buf0 + size_t(b) * ROPE_TILE * ROWB;
+        uint8_t *row = tb + size_t(lane) * ROWB;
 
         // ordered sum of squares of head row `lane`
         float acc = 0.0f;
         if (lane < nvalid) {
-            const uint4 *p4 = reinterpret_cast<const uint4 *>(tb + size_t(lane) * ROWB);
+            const uint4 *p4 = reinterpret_cast<const uint4 *>(row);
 #pragma unroll
             for (int c = 0; c < HD / V; ++c) {
                 float v[V];
@@ -126,60 +155,54 @@ __global__ void __launch_bounds__(ROPE_WARPS * 32) qk_norm_rope_kernel(
                 for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, __fmul_rn(v[i], v[i]));
             }
         }
-        const float ssl = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, float(HD)), eps)));
+        const float ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, float(HD)), eps)));
 
-        const float2 wlo = *reinterpret_cast<const float2 *>(nw + 2 * lane);
-        const float2 whi = *reinterpret_cast<const float2 *>(nw + 64 + 2 * lane);
-        // token of each head row, tracked incrementally (one division per tile)
-        int64_t tok = row0 / heads;
-        int hin = int(row0 - tok * heads);
-        float c0 = 0.f, s0 = 0.f, c1 = 0.f, s1 = 0.f;
-        for (int i = 0; i < nvalid; ++i) {
-            const float ss = __shfl_sync(FULL, ssl, i);
-            const int64_t hr = row0 + i;
-            if (i == 0 || hin == 0) {                      // warp-uniform: a new token
-                const float p = float(__ldg(pos + tok));
+        // tokens of the tile's rows, ROPE_TOKS at a time (one pass for >= 4 heads)
+        const int64_t tok0 = row0 / heads;
+        const int my_tok = int((row0 + lane) / heads - tok0);
+        const int ntok = int((row0 + nvalid - 1) / heads - tok0) + 1;
+        for (int tt0 = 0; tt0 < ntok; tt0 += ROPE_TOKS) {
+            const int nt = ntok - tt0 < ROPE_TOKS ? ntok - tt0 : ROPE_TOKS;
+            for (int tt = 0; tt < nt; ++tt) {
+                const float p = float(__ldg(pos + tok0 + tt0 + tt));
+                float c0, s0, c1, s1;
                 sincosf(__fmul_rn(p, f0), &s0, &c0);
                 sincosf(__fmul_rn(p, f1), &s1, &c1);
+                float *ct = reinterpret_cast<float *>(tab + tt * ROPE_TABB);
+                *reinterpret_cast<float2 *>(ct + 2 * lane) = make_float2(c0, c1);
+                *reinterpret_cast<float2 *>(ct + HD / 2 + 2 * lane) = make_float2(s0, s1);
             }
-            if (++hin == heads) { hin = 0; ++tok; }
-            const uint8_t *rp = tb + size_t(i) * ROWB;
-            float x0, x1, y0, y1;
-            load_pair<T>(rp, 2 * lane, x0, x1);
-            load_pair<T>(rp, 64 + 2 * lane, y0, y1);
-            x0 = __fmul_rn(wlo.x, __fmul_rn(ss, x0));
-            x1 = __fmul_rn(wlo.y, __fmul_rn(ss, x1));
-            y0 = __fmul_rn(whi.x, __fmul_rn(ss, y0));
-            y1 = __fmul_rn(whi.y, __fmul_rn(ss, y1));
-            const float a0 = __fsub_rn(__fmul_rn(x0, c0), __fmul_rn(y0, s0));
-            const float b0 = __fadd_rn(__fmul_rn(x0, s0), __fmul_rn(y0, c0));
-            const float a1 = __fsub_rn(__fmul_rn(x1, c1), __fmul_rn(y1, s1));
-            const float b1 = __fadd_rn(__fmul_rn(x1, s1), __fmul_rn(y1, c1));
-            T *dst = base + hr * HD;
-            store_pair<T>(dst + 2 * lane, a0, a1);
-            store_pair<T>(dst + 64 + 2 * lane, b0, b1);
+            __syncwarp();
+            const int slot = my_tok - tt0;
+            if (lane < nvalid && slot >= 0 && slot < nt)
+                rotate_row<T>(row, w, reinterpret_cast<const float *>(tab + slot * ROPE_TABB), ss);
+            __syncwarp();                          // table reuse / rows complete
         }
+        // coalesced write-back of the tile
+        uint8_t *dst = reinterpret_cast<uint8_t *>(base + row0 * HD);
+        for (int c = lane; c < nvalid * CPR; c += 32)
+            st_cs_v4(dst + size_t(c) * 16, *reinterpret_cast<const uint4 *>(tb + (c / CPR) * ROWB + (c % CPR) * 16));
         __syncwarp();          // all reads of buffer b done before it is refilled
     }
+    cp_async_wait<0>();        // no copy may still be landing when the CTA exits
 }
 
 template <typename T>
 static cudaError_t launch_rope_t(T *q, T *k, const int32_t *pos, int64_t rows, int nh, int nkv, const float *qn,
                                  const float *kn, const InvFreq &invf, float eps, uint32_t *status,
                                  cudaStream_t stream, int sms) {
-    constexpr int ROWB = HD * int(sizeof(T)) + 16;
-    constexpr size_t SMEM = size_t(ROPE_WARPS) * 2 * ROPE_TILE * ROWB;
+    constexpr int RW = rope_warps<T>();
+    constexpr size_t SMEM = size_t(RW) * rope_warp_bytes<T>();
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(qk_norm_rope_kernel<T>), SMEM,
                                      sizeof(T) == 4 ? 0 : 1);
     if (e != cudaSuccess) return e;
     const int64_t qr = rows * nh, kr = rows * nkv;
     const int64_t tiles = (qr + ROPE_TILE - 1) / ROPE_TILE + (kr + ROPE_TILE - 1) / ROPE_TILE;
-    const int per_sm = (sizeof(T) == 4) ? 1 : 2;                // CTAs that fit an SM's shared memory
-    int64_t blocks = (tiles + ROPE_WARPS - 1) / ROPE_WARPS;
-    const int64_t cap = int64_t(sms) * per_sm;
-    if (blocks > cap) blocks = cap;
-    qk_norm_rope_kernel<T><<<unsigned(blocks), ROPE_WARPS * 32, SMEM, stream>>>(q, k, pos, qr, kr, nh, nkv, qn, kn,
-                                                                              invf, eps, status);
+    int64_t blocks = (tiles + RW - 1) / RW;                      // one CTA per SM (shared memory)
+    if (blocks > sms) blocks = sms;
+    (void)status;                                                // no polling waits: nothing to report
+    qk_norm_rope_kernel<T><<<unsigned(blocks), RW * 32, SMEM, stream>>>(q, k, pos, qr, kr, nh, nkv, qn, kn, invf,
+                                                                      eps);
     return cudaGetLastError();
 }
 

@@ -406,6 +406,24 @@ __device__ __forceinline__ uint64_t global_ns() {
     return t;
 }
 
+// Per-thread asynchronous 16-byte global -> shared copies (cp.async, L2 only).
+// Both addresses 16-byte aligned.  A thread's copies are grouped by commit;
+// wait<N> blocks until at most N of its groups are still in flight (a hardware
+// wait for outstanding loads, not a polling loop).  Other threads see the data
+// after a barrier that follows their wait.
+__device__ __forceinline__ void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_addr(dst)), "l"(src) : "memory");
+}
+// Makes `bar`'s current phase wait for all of this thread's earlier cp.async
+// copies: the pending count rises by one now and falls by one when they have
+// landed (no net arrival, so the barrier's expected count is unaffected).
+__device__ __forceinline__ void cp_async_track(uint64_t *bar) {
+    asm volatile("cp.async.mbarrier.arrive.shared::cta.b64 [%0];" :: "r"(smem_addr(bar)) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
 // Every wait is bounded: after ~2 s (or 2^26 polls) it records
 // Q3CU_DEV_TIMEOUT in the status word and returns false; callers then skip
 // their remaining work for the affected rows.
