@@ -14,11 +14,10 @@
 // of latency; 28 chains keep pace with an SM's share of HBM for f32 rows).
 //
 // Persistent CTA per SM over blocks of R <= 32 rows (the same number of rows
-// per SM): 16 compute warps and one producer warp.  All data moves through one ring of NS = 3 stages of
-// 32 rows x 2 KB in shared memory, filled by TMA bulk copies (cp.async.bulk,
-// one 2 KB copy per row per stage, an mbarrier per stage, rows padded so the
-// chain lanes read distinct banks), so two stages are in flight while the
-// chain consumes the third.  Per block:
+// per SM): 16 compute warps and one producer warp.  All data moves through one
+// ring of NS = 3 stages of 32 rows x 2 KB in shared memory (an mbarrier per
+// stage, rows padded so the chain lanes read distinct banks), so two stages
+// are in flight while the chain consumes the third.  Per block:
 //   phase 1  the row chunks in order; chain-warp lane r folds row r's chunk into
 //            its running sum.  The first nch - NS chunks are released as soon
 //            as the chain has read them; the last NS stay in their stages.
@@ -29,10 +28,11 @@
 //            xor-shuffle) into int8 codes + f32 scales.
 // For a 2560-wide f32 row (5 chunks) only 2 of the 5 chunks are read twice.
 // The copies form one stream per CTA (first reads, then second reads, block
-// after block).  The producer warp issues item it into stage it % NS once the
-// consumers have released item it - NS (an "empty" mbarrier per stage), so
-// the ring runs across phases and blocks, and the ~1 us it takes to issue a
-// stage's 32 row copies is spent by a warp that has nothing else to do.
+// after block).  The first NS items are copied by every thread (cp.async);
+// then the producer warp issues item it into stage it % NS, one bulk copy per
+// row, once the consumers have released item it - NS (an "empty" mbarrier per
+// stage), so the ring runs across phases and blocks, and the ~1 us it takes
+// to issue a stage's row copies is spent by a warp with nothing else to do.
 #include "q3cu_internal.h"
 
 namespace q3 {
@@ -85,6 +85,36 @@ __device__ __forceinline__ float chain_sum(float acc, const uint8_t *p, int elem
     return acc;
 }
 
+// The same fold over one full 2 KB chunk, fully unrolled: two register batches
+// of 8 vectors alternate, so the next batch is in flight while the current one
+// is folded in and no copies between them are needed.  (With a run-time trip
+// count the loop stays rolled and the batch copies slow the chain by ~40%.)
+template <typename T>
+__device__ __forceinline__ float chain_full(float acc, const uint8_t *p) {
+    constexpr int V = Vec<T>::N, NB = RMS_CB / 16 / 8;     // 16 batches of 8 vectors
+    const uint4 *p4 = reinterpret_cast<const uint4 *>(p);
+    uint4 buf[2][8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) buf[0][j] = p4[j];
+#pragma unroll
+    for (int b = 0; b < NB; ++b) {
+        if (b + 1 < NB) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) buf[(b + 1) & 1][j] = p4[(b + 1) * 8 + j];
+        }
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            float v[V], sq[V];
+            Vec<T>::widen(buf[b & 1][j], v);
+#pragma unroll
+            for (int i = 0; i < V; i += 2) up2(mul2(pk2(v[i], v[i + 1]), pk2(v[i], v[i + 1])), sq[i], sq[i + 1]);
+#pragma unroll
+            for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, sq[i]);     // in index order
+        }
+    }
+    return acc;
+}
+
 template <typename T, bool Q8>
 __global__ void __launch_bounds__(RMS_THREADS, 1) rmsnorm_kernel(const T *x, const float *__restrict__ w, int64_t rows,
                                                                  int dim, int n_div, float eps, int R, T *out,
@@ -129,6 +159,35 @@ __global__ void __launch_bounds__(RMS_THREADS, 1) rmsnorm_kernel(const T *x, con
     };
     // Item it: block it / per_block; j = it % per_block is the first read of
     // chunk j (j < nch) or the second read of chunk j - nch.  Stage it % NS.
+    // Every stage barrier expects one plain arrival per item.
+    //
+    // The first NS items are copied by every thread with 16-byte cp.async
+    // pieces (a warp instruction moves 512 contiguous bytes of one row), so the
+    // first chunk lands within about a microsecond; each copying thread attaches
+    // its pieces to the stage barrier (a balanced arrival: the pending count
+    // rises now and falls when they land), and after a CTA barrier thread 0
+    // makes the item's one arrival.
+    const int first_items = total < RMS_NS ? total : RMS_NS;
+    for (int it = 0; it < first_items; ++it) {
+        const int kb = it / per_block, j = it % per_block, c = j < nch ? j : j - nch, st = it % RMS_NS;
+        int64_t r0; int rv;
+        block_rows(kb, r0, rv);
+        const int vpr = chunk_bytes(c) / 16;            // 16-byte vectors per row
+        const uint8_t *src = reinterpret_cast<const uint8_t *>(x) + r0 * row_bytes + int64_t(c) * RMS_CB;
+        uint8_t *dst = stage + size_t(st) * RMS_MAXR * RMS_ROWB;
+        for (int f = tid; f < rv * vpr; f += RMS_THREADS) {
+            const int r = f / vpr, v = f - (f / vpr) * vpr;
+            cp_async16(dst + r * RMS_ROWB + v * 16, src + r * row_bytes + v * 16);
+        }
+        cp_async_track(&bar[st]);
+    }
+    __syncthreads();
+    if (tid == 0)
+        for (int it = 0; it < first_items; ++it) mbar_arrive(&bar[it]);
+    // Later items: the producer warp, one bulk copy per row (lane r copies row
+    // r's piece); the expect-tx arrival is the item's one arrival.  Bulk copies
+    // do not count against the SM's cap on outstanding cp.async bytes (~50 KB),
+    // so two stages can be in flight while the chain reads the third.
     auto issue = [&](int it) {
         const int k = it / per_block, j = it % per_block, c = j < nch ? j : j - nch, st = it % RMS_NS;
         int64_t r0; int rv;
@@ -147,20 +206,21 @@ __global__ void __launch_bounds__(RMS_THREADS, 1) rmsnorm_kernel(const T *x, con
     // producer only reads fail_sh: the compute warps' exits must not depend on
     // a write that can land between their reads.
     if (warp == RMS_CWARPS) {
-        int issued = 0;
+        int issued = first_items;
         for (; issued < total; ++issued) {
             const int st = issued % RMS_NS;
             if (__any_sync(FULL, fail_sh != 0)) break;
-            if (issued >= RMS_NS &&
-                !__all_sync(FULL, mbar_wait(&empty[st], uint32_t(issued / RMS_NS - 1) & 1u, lane == 0 ? status : nullptr)))
+            if (!__all_sync(FULL, mbar_wait(&empty[st], uint32_t(issued / RMS_NS - 1) & 1u, lane == 0 ? status : nullptr)))
                 break;                             // the consumers' own waits report the failure
             issue(issued);
         }
-        // Before the CTA may exit, every issued copy has landed.  Normally the
-        // consumers have already seen all of them; after a failure this waits
-        // (bounded) for the at most NS items still in flight.
+        // Before the CTA may exit, every copy has landed: the producer's own
+        // cp.async pieces, and (bounded wait) the at most NS bulk-copied items
+        // that may still be in flight after a failure (normally the consumers
+        // have seen them all).
+        cp_async_wait<0>();
         if (lane == 0)
-            for (int d = issued > RMS_NS ? issued - RMS_NS : 0; d < issued; ++d)
+            for (int d = issued > first_items + RMS_NS ? issued - RMS_NS : first_items; d < issued; ++d)
                 mbar_wait(&bar[d % RMS_NS], uint32_t(d / RMS_NS) & 1u, nullptr);
         return;
     }
@@ -183,9 +243,11 @@ __global__ void __launch_bounds__(RMS_THREADS, 1) rmsnorm_kernel(const T *x, con
             for (int c = 0; c < nch; ++c) {
                 ok = wait_item(base + c);
                 if (!ok) break;
-                if (lane < rv)
-                    acc = chain_sum<T>(acc, stage + (size_t((base + c) % RMS_NS) * RMS_MAXR + lane) * RMS_ROWB,
-                                       chunk_bytes(c) / ESZ);
+                if (lane < rv) {
+                    const uint8_t *rp = stage + (size_t((base + c) % RMS_NS) * RMS_MAXR + lane) * RMS_ROWB;
+                    const int cb = chunk_bytes(c);
+                    acc = cb == RMS_CB ? chain_full<T>(acc, rp) : chain_sum<T>(acc, rp, cb / ESZ);
+                }
                 __syncwarp();
                 if (c < nre && lane == 0) mbar_arrive(&empty[(base + c) % RMS_NS]);   // resident chunks: phase 2
             }
