@@ -2,6 +2,8 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
+Workloads: prefill4b (default: the headline line), decode8b, embed, prefill14b.
+
 A step is one pass of the layer's memory-bound kernels over one batch of
 token rows already resident in HBM.  Default workload `prefill4b`: the
 Qwen3-4B-shaped prefill layer, 4096 fp32 tokens per GPU, dim 2560, 32 q / 8 kv
@@ -40,6 +42,8 @@ GS = 64
 class Workload:
     name = ""
     tokens = 0
+    dtype = "f32"
+    e2e_note = ""
 
     def kernels(self):              # [(name, algorithmic bytes per launch)]
         raise NotImplementedError
@@ -140,7 +144,260 @@ class Prefill4B(Workload):
         return self.total_bytes() * n / self.tokens
 
 
-WORKLOADS = {"prefill4b": Prefill4B}
+def _ragged(np, pos, nh):
+    """Offsets and lengths of the attention score rows of tokens at `pos`:
+    row t*nh + h has length pos[t] + 1 (causal)."""
+    lens = np.repeat(pos.astype(np.int64) + 1, nh)
+    off = np.concatenate([[0], np.cumsum(lens)[:-1]]).astype(np.int64)
+    return off, lens.astype(np.int32)
+
+
+class _BF16Layer(Workload):
+    """Shared parts of the bf16 layer workloads: rmsnorm_q8 + qk_norm_rope +
+    swiglu_q8 on bf16 token rows, then the attention softmax over every head's
+    score row (length pos+1, f32 scores N(0, sigma=2), in place)."""
+    dtype = "bf16 (softmax scores f32)"
+    outliers = False
+
+    def scores(self, pos):
+        return int(pos.astype("int64").sum() + pos.size) * self.nh
+
+    def kernel_bytes(self, pos):
+        T, D, H = pos.size, self.dim, self.hidden
+        rms = T * D * 2 + T * D + T * (D // GS) * 4 + D * 4
+        rope = 2 * T * (self.nh + self.nkv) * self.hd * 2 + T * 4 + 2 * self.hd * 4
+        swi = 2 * T * H * 2 + T * H + T * (H // GS) * 4
+        smx = 8 * self.scores(pos) + 12 * T * self.nh
+        return [("rmsnorm_q8", rms), ("qk_norm_rope", rope), ("swiglu_q8", swi), ("softmax_rows", smx)]
+
+    def kernels(self):
+        return self.kernel_bytes(self.pos)
+
+    def _batch(self, torch, dev, g, pos):
+        import numpy as np
+        T, D, H = pos.size, self.dim, self.hidden
+        off, lens = _ragged(np, pos, self.nh)
+
+        def act(rows, cols):
+            a = torch.randn(rows, cols, device=dev, generator=g)
+            if self.outliers:
+                ch = torch.randperm(cols, device=dev, generator=g)[:max(1, round(cols * 0.01))]
+                a[:, ch] *= 20.0
+            return a.to(torch.bfloat16)
+
+        return {
+            "x": act(T, D), "hb": act(T, H), "hb2": act(T, H),
+            "q": torch.randn(T, self.nh, self.hd, device=dev, generator=g).to(torch.bfloat16),
+            "k": torch.randn(T, self.nkv, self.hd, device=dev, generator=g).to(torch.bfloat16),
+            "pos": torch.from_numpy(pos).to(dev),
+            "att": 2.0 * torch.randn(int(lens.sum()), device=dev, generator=g),
+            "off": torch.from_numpy(off).to(dev), "len": torch.from_numpy(lens).to(dev),
+            "xq": torch.empty(T, D, dtype=torch.int8, device=dev),
+            "xs": torch.empty(T, D // GS, dtype=torch.float32, device=dev),
+            "hq": torch.empty(T, H, dtype=torch.int8, device=dev),
+            "hs": torch.empty(T, H // GS, dtype=torch.float32, device=dev),
+        }
+
+    def make(self, torch, dev, seed):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        d = self._batch(torch, dev, g, self.pos)
+        d["w"] = 1.0 + 0.1 * torch.randn(self.dim, device=dev, generator=g)
+        d["qn"] = 1.0 + 0.1 * torch.randn(self.hd, device=dev, generator=g)
+        d["kn"] = 1.0 + 0.1 * torch.randn(self.hd, device=dev, generator=g)
+        if self.e2e_tokens < self.tokens:
+            e = self._batch(torch, dev, g, self.pos[: self.e2e_tokens])
+            for k, v in e.items():
+                d[k + "_e2e"] = v
+        else:
+            for k in ("x", "hb", "hb2", "q", "k", "pos", "att", "off", "len", "xq", "xs", "hq", "hs"):
+                d[k + "_e2e"] = d[k]
+        return d
+
+    def _ops(self, q3, d, stream, sfx=""):
+        return [
+            lambda: q3.rmsnorm_q8(d["x" + sfx], d["w"], q=d["xq" + sfx], s=d["xs" + sfx], stream=stream),
+            lambda: q3.qk_norm_rope(d["q" + sfx], d["k" + sfx], d["pos" + sfx], d["qn"], d["kn"], stream=stream),
+            lambda: q3.swiglu_q8(d["hb" + sfx], d["hb2" + sfx], q=d["hq" + sfx], s=d["hs" + sfx], stream=stream),
+            lambda: q3.softmax_rows(d["att" + sfx], d["off" + sfx], d["len" + sfx], stream=stream),
+        ]
+
+    def launch(self, q3, d, stream, events=None):
+        ops = self._ops(q3, d, stream)
+        for i, op in enumerate(ops):
+            if events is not None:
+                events[i][0].record(stream)
+            op()
+            if events is not None:
+                events[i][1].record(stream)
+        return len(ops)
+
+    def launch_e2e(self, q3, d, stream):
+        for op in self._ops(q3, d, stream, "_e2e"):
+            op()
+        return 4
+
+    h2d_keys = tuple(k + "_e2e" for k in ("x", "q", "k", "pos", "hb", "hb2", "att"))
+    d2h_keys = tuple(k + "_e2e" for k in ("xq", "xs", "q", "k", "hq", "hs", "att"))
+
+    def e2e_bytes(self):
+        return sum(b for _, b in self.kernel_bytes(self.pos[: self.e2e_tokens]))
+
+    def cpu_step(self, oracle, np, sample, threads, rng):
+        # The reference computes in binary32: the CPU rows are f32 with the same shapes.
+        if not hasattr(self, "_cpu"):
+            D, H = self.dim, self.hidden
+            f = lambda *shape: rng.standard_normal(shape, dtype=np.float32)
+            pos = self.sample_pos(sample)
+            off, lens = _ragged(np, pos, self.nh)
+            self._cpu = (f(sample, D), (1 + 0.1 * f(D)).astype(np.float32), f(sample, self.nh, self.hd),
+                         f(sample, self.nkv, self.hd), pos, (1 + 0.1 * f(self.hd)).astype(np.float32),
+                         (1 + 0.1 * f(self.hd)).astype(np.float32), f(sample, H), f(sample, H),
+                         (2.0 * f(int(lens.sum()))).astype(np.float32), off, lens)
+        x, w, q, k, pos, qn, kn, hb, hb2, att, off, lens = self._cpu
+        oracle.rows_rmsnorm_q8(x, w, threads=threads)
+        oracle.rows_qk_norm_rope(q, k, pos, qn, kn, threads=threads)
+        oracle.rows_swiglu_q8(hb, hb2, threads=threads)
+        oracle.rows_softmax(att, off, lens, threads=threads)
+
+    def bytes_for_tokens(self, n):
+        return sum(b for _, b in self.kernel_bytes(self.sample_pos(n)))
+
+
+class Decode8B(_BF16Layer):
+    """Qwen3-8B-shaped batched decode: T bf16 tokens at positions uniform in
+    0..32767 (seed 0)."""
+    name = "decode8b"
+
+    def __init__(self, tokens=256, dim=4096, nh=32, nkv=8, hd=128, hidden=12288, maxpos=32767, seed=0):
+        import numpy as np
+        self.tokens, self.dim, self.nh, self.nkv, self.hd, self.hidden = tokens, dim, nh, nkv, hd, hidden
+        self.pos = np.random.default_rng(seed).integers(0, maxpos + 1, size=tokens).astype(np.int32)
+        self.e2e_tokens = tokens
+
+    def sample_pos(self, n):
+        return self.pos[:n]
+
+    def config(self):
+        return {"workload": "Qwen3-8B-shaped batched decode (rmsnorm_q8 + qk_norm_rope + swiglu_q8 on bf16 rows; "
+                            "softmax over each head's score row of length pos+1)",
+                "tokens_per_gpu": self.tokens, "dim": self.dim, "n_heads": self.nh, "n_kv_heads": self.nkv,
+                "head_dim": self.hd, "hidden": self.hidden, "positions": "uniform 0..32767 (seed 0)",
+                "softmax_rows": self.tokens * self.nh, "softmax_scores": self.scores(self.pos),
+                "scores": "f32 N(0, sigma=2)", "rope_theta": 1e6, "input_dtype": "bf16"}
+
+
+class Prefill14B(_BF16Layer):
+    """Qwen3-14B-shaped long-context prefill, one layer: per GPU T bf16 tokens
+    in sequences of 4096 (positions 0..4095 each), 1% outlier channels x20,
+    causal softmax of every head's row."""
+    name = "prefill14b"
+    outliers = True
+
+    def __init__(self, tokens=16384, dim=5120, nh=40, nkv=8, hd=128, hidden=17408, seqlen=4096, e2e_tokens=512):
+        import numpy as np
+        self.tokens, self.dim, self.nh, self.nkv, self.hd, self.hidden, self.seqlen = \
+            tokens, dim, nh, nkv, hd, hidden, seqlen
+        self.pos = (np.arange(tokens) % seqlen).astype(np.int32)
+        self.e2e_tokens = min(e2e_tokens, tokens)
+        self.e2e_note = (f"end to end on the first {self.e2e_tokens} tokens of a sequence per step (a full step "
+                         f"would move {self.scores(self.pos) * 4 / 1e9:.1f} GB of scores each way)")
+
+    def sample_pos(self, n):
+        import numpy as np
+        return ((np.arange(n) * self.seqlen) // max(n, 1)).astype(np.int32)    # spread over 0..seqlen-1
+
+    def config(self):
+        return {"workload": "Qwen3-14B-shaped long-context prefill, one layer (rmsnorm_q8 + qk_norm_rope + "
+                            "swiglu_q8 on bf16 rows; causal softmax of every head's row)",
+                "tokens_per_gpu": self.tokens, "sequences_per_gpu": self.tokens // self.seqlen,
+                "positions": f"0..{self.seqlen - 1} per sequence", "dim": self.dim, "n_heads": self.nh,
+                "n_kv_heads": self.nkv, "head_dim": self.hd, "hidden": self.hidden,
+                "softmax_scores": self.scores(self.pos), "scores": "f32 N(0, sigma=2)", "rope_theta": 1e6,
+                "input_dtype": "bf16 (1% outlier channels x20)"}
+
+
+class Embed(Workload):
+    """Q8_0 embedding dequant/gather: a vocab x dim Q8_0 table on the device, N
+    Zipf(1.1)-distributed token ids; each lookup writes the f32 row and its
+    re-quantized Q8_0 codes + scales."""
+    name = "embed"
+    dtype = "int8 codes + f32 scales -> f32 rows + Q8_0"
+
+    def __init__(self, tokens=1048576, vocab=151936, dim=4096, seed=0, e2e_lookups=65536):
+        import numpy as np
+        self.tokens, self.vocab, self.dim = tokens, vocab, dim
+        rng = np.random.default_rng(seed)
+        ranks = np.empty(0, np.int64)
+        while ranks.size < tokens:                     # Zipf(1.1), truncated to the vocab by rejection
+            r = rng.zipf(1.1, size=tokens)
+            ranks = np.concatenate([ranks, r[r <= vocab]])
+        perm = rng.permutation(vocab)                  # rank -> token id: a seeded permutation
+        self.ids = perm[ranks[:tokens] - 1].astype(np.int32)
+        self.e2e_lookups = min(e2e_lookups, tokens)
+        self.e2e_note = (f"end to end on a sub-batch of {self.e2e_lookups} lookups per step (one full step "
+                         f"moves {tokens * dim * 5 / 1e9:.1f} GB of rows to the host)")
+
+    def kernels(self):
+        D = self.dim
+        per = 4 + D + D // 16 + 4 * D + D + D // 16
+        return [("embed_gather", per * self.tokens)]
+
+    def config(self):
+        return {"workload": "Q8_0 embedding dequant/gather with fused re-quantize",
+                "lookups_per_gpu": self.tokens, "vocab": self.vocab, "dim": self.dim,
+                "ids": "Zipf(s=1.1) ranks truncated to the vocab, mapped through a seeded permutation (seed 0)",
+                "table": "codes uniform in [-127,127], scales |N(0,0.01)|", "outputs": "f32 rows + Q8_0 codes/scales"}
+
+    def make(self, torch, dev, seed):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        V, D, N = self.vocab, self.dim, self.tokens
+        d = {
+            "tq": torch.randint(-127, 128, (V, D), device=dev, dtype=torch.int8, generator=g),
+            "ts": (0.01 * torch.randn(V, D // GS, device=dev, generator=g)).abs(),
+            "ids": torch.from_numpy(self.ids).to(dev),
+            "out": torch.empty(N, D, dtype=torch.float32, device=dev),
+            "oq": torch.empty(N, D, dtype=torch.int8, device=dev),
+            "os": torch.empty(N, D // GS, dtype=torch.float32, device=dev),
+        }
+        n = self.e2e_lookups
+        d["ids_e2e"] = d["ids"][:n].clone()
+        d["out_e2e"], d["oq_e2e"], d["os_e2e"] = d["out"][:n], d["oq"][:n], d["os"][:n]
+        return d
+
+    def launch(self, q3, d, stream, events=None):
+        if events is not None:
+            events[0][0].record(stream)
+        q3.embed_gather(d["tq"], d["ts"], d["ids"], out=d["out"], oq=d["oq"], os_=d["os"], stream=stream)
+        if events is not None:
+            events[0][1].record(stream)
+        return 1
+
+    def launch_e2e(self, q3, d, stream):
+        q3.embed_gather(d["tq"], d["ts"], d["ids_e2e"], out=d["out_e2e"], oq=d["oq_e2e"], os_=d["os_e2e"],
+                        stream=stream)
+        return 1
+
+    h2d_keys = ("ids_e2e",)
+    d2h_keys = ("out_e2e", "oq_e2e", "os_e2e")
+
+    def e2e_bytes(self):
+        return self.kernels()[0][1] * self.e2e_lookups / self.tokens
+
+    def cpu_step(self, oracle, np, sample, threads, rng):
+        if not hasattr(self, "_cpu"):
+            tq = rng.integers(-127, 128, size=(self.vocab, self.dim), dtype=np.int8)
+            ts = np.abs(0.01 * rng.standard_normal((self.vocab, self.dim // GS))).astype(np.float32)
+            self._cpu = (tq, ts, self.ids[: max(sample, 1)])
+        tq, ts, ids = self._cpu
+        oracle.rows_embed(tq, ts, ids[:sample], want_q8=True, threads=threads)
+
+    def bytes_for_tokens(self, n):
+        return self.total_bytes() * n / self.tokens
+
+
+WORKLOADS = {"prefill4b": Prefill4B, "decode8b": Decode8B, "embed": Embed, "prefill14b": Prefill14B}
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -269,7 +526,7 @@ def run_reference(args, wl):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
         "config": dict(wl.config(), sample_tokens_per_step=sample),
         "tokens_per_s": round(sample * args.steps / el, 2),
         "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": kind,
@@ -282,8 +539,8 @@ def run_reference(args, wl):
 
 
 CPU_NOTE = {
-    "reference": "src/cpu/qwen3_original.c compiled unmodified (rmsnorm, quantize); its inline RoPE and "
-                 "SwiGLU loops restated in oracle/ref_rows.c",
+    "reference": "src/cpu/qwen3_original.c compiled unmodified (rmsnorm, softmax, quantize, dequantize); its "
+                 "inline RoPE and SwiGLU loops restated in oracle/ref_rows.c",
     "port": "oracle/q3_oracle.c, the restatement of src/cpu/qwen3_original.c",
 }
 
@@ -377,7 +634,7 @@ def main():
         with torch.cuda.stream(stream):
             for k, t in hin.items():
                 d[k].copy_(t, non_blocking=True)
-            wl.launch(q3, d, stream)
+            (wl.launch_e2e if hasattr(wl, "launch_e2e") else wl.launch)(q3, d, stream)
             for k, t in hout.items():
                 t.copy_(d[k], non_blocking=True)
 
@@ -401,6 +658,7 @@ def main():
     # ---- report ---------------------------------------------------------------
     if rank == 0:
         step_bytes = wl.total_bytes()
+        e2e_bytes = wl.e2e_bytes() if hasattr(wl, "e2e_bytes") else step_bytes
         ms_per_step = total_ms / args.steps
         gbs = world * step_bytes * args.steps / (total_ms / 1e3) / 1e9
         kern = {}
@@ -414,10 +672,10 @@ def main():
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
             "config": dict(wl.config(), parallelism=f"token rows x{world} (weak)",
                            l2="flushed between timed steps (256 MiB write outside the events); "
-                              "step working set 582 MB > 126 MB L2"),
+                              f"step working set {step_bytes / 1e6:.0f} MB vs 126 MB L2"),
             "tokens_per_s": round(world * wl.tokens * args.steps / (total_ms / 1e3), 1),
             "hbm_frac": round(gbs / world / peak, 4),
             "kernels": kern,
@@ -426,10 +684,11 @@ def main():
                          else "fallback 6650 GB/s", "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": profiled_traffic(wl.name, dom_name),
                          "algorithmic_bytes_per_launch": dom_bytes},
-            "e2e": {"value": round(world * step_bytes * args.e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
+            "e2e": {"value": round(world * e2e_bytes * args.e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
-                    "path": "pinned host inputs -> cudaMemcpyAsync H2D -> q3cu C ABI kernels -> D2H, per step"},
+                    "path": "pinned host inputs -> cudaMemcpyAsync H2D -> q3cu C ABI kernels -> D2H, per step"
+                            + (f"; {wl.e2e_note}" if wl.e2e_note else "")},
             "gpu_launches": launches,
             "clocks": clk,
         }
