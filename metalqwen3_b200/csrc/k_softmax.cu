@@ -5,12 +5,16 @@
 //     max_val = 0; for i: if (x[i] > max_val) max_val = x[i];   // starts at 0
 //     sum = 0;     for i: x[i] = expf(x[i] - max_val); sum += x[i];
 //     for i: x[i] /= sum;
-// The max is order-independent and exact.  Each exponential is q3_expf_tab,
-// bit-identical to the host libm's expf.  The sum is accumulated in binary64
-// (per thread, then a tree), so it is closer to the exact sum than the
-// reference's sequential binary32 sum; the outputs differ from the reference
-// by that sum's rounding error, which the tests bound (1e-5 rel / 1e-6 abs and
-// no further from the oracle than the oracle is from a binary64 softmax).
+// The max is order-independent and exact.  Softmax owes the reference 1e-5
+// relative, not its bits, so each exponential of d = x - max in [-80, 0] is
+// exp_m80_0 (binary32 Cody-Waite reduction + ex2.approx, ~2^-22 relative); d
+// below -80 or NaN takes the libm-identical expf, so the reference's underflow
+// (a row entirely below -104 is 0/0 = NaN) is reproduced.  Each float4's four
+// exponentials are added in binary32 and the partial sums accumulated in
+// binary64 (per thread, then a tree): closer to the exact sum than the
+// reference's sequential binary32 sum.  The tests bound the outputs (1e-5 rel /
+// 1e-6 abs of a binary64 softmax, and no further from the oracle than the
+// oracle is from it).
 //
 // Rows are bucketed by length into five kernels, each a grid-stride loop over
 // all rows that skips rows outside its bucket:
@@ -45,6 +49,17 @@ __device__ __forceinline__ int scalar_index(const RowSplit &s, int t) {
     if (t < s.a) return t;
     if (t - s.a < s.tl) return s.a + 4 * s.nb + (t - s.a);
     return -1;
+}
+
+__device__ __forceinline__ float smx_exp(float d, const ExpTab &tab) {
+    return d >= -80.0f ? exp_m80_0(d) : expf_host(d, tab);
+}
+__device__ __forceinline__ float4 smx_exp4(float4 v, float m, const ExpTab &tab) {
+    return make_float4(smx_exp(__fsub_rn(v.x, m), tab), smx_exp(__fsub_rn(v.y, m), tab),
+                       smx_exp(__fsub_rn(v.z, m), tab), smx_exp(__fsub_rn(v.w, m), tab));
+}
+__device__ __forceinline__ double sum4(float4 v) {
+    return double(__fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w)));
 }
 
 template <int NW>
@@ -111,14 +126,11 @@ __global__ void __launch_bounds__(NW * 32) softmax_reg_kernel(float *x, const in
 #pragma unroll
         for (int j = 0; j < NB; ++j) {
             if (t + j * NT < sp.nb) {
-                v[j].x = expf_host(__fsub_rn(v[j].x, m), s_tab);
-                v[j].y = expf_host(__fsub_rn(v[j].y, m), s_tab);
-                v[j].z = expf_host(__fsub_rn(v[j].z, m), s_tab);
-                v[j].w = expf_host(__fsub_rn(v[j].w, m), s_tab);
-                sum += double(v[j].x) + double(v[j].y) + double(v[j].z) + double(v[j].w);
+                v[j] = smx_exp4(v[j], m, s_tab);
+                sum += sum4(v[j]);
             }
         }
-        if (si >= 0) { xs = expf_host(__fsub_rn(xs, m), s_tab); sum += double(xs); }
+        if (si >= 0) { xs = smx_exp(__fsub_rn(xs, m), s_tab); sum += double(xs); }
         sum = block_sum<NW>(sum, sh_d);
         const float inv = float(1.0 / sum);
 
@@ -171,16 +183,12 @@ __global__ void __launch_bounds__(SMX_LONG_THREADS) softmax_long_kernel(float *x
         double sum = 0.0;
 #pragma unroll 4
         for (int bi = t; bi < sp.nb; bi += NT) {
-            float4 v = u4_as_f4(ld_v4(body + bi));
-            v.x = expf_host(__fsub_rn(v.x, m), s_tab);
-            v.y = expf_host(__fsub_rn(v.y, m), s_tab);
-            v.z = expf_host(__fsub_rn(v.z, m), s_tab);
-            v.w = expf_host(__fsub_rn(v.w, m), s_tab);
-            sum += double(v.x) + double(v.y) + double(v.z) + double(v.w);
+            const float4 v = smx_exp4(u4_as_f4(ld_v4(body + bi)), m, s_tab);
+            sum += sum4(v);
             *reinterpret_cast<uint4 *>(body + bi) = f4_as_u4(v);
         }
         if (si >= 0) {
-            const float e = expf_host(__fsub_rn(row[si], m), s_tab);
+            const float e = smx_exp(__fsub_rn(row[si], m), s_tab);
             row[si] = e;
             sum += double(e);
         }

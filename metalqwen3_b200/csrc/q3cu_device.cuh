@@ -359,6 +359,32 @@ __device__ __forceinline__ void load_exp_table(ExpTab &t) {
 __device__ __forceinline__ float expf_host(float x, const ExpTab &t) { return q3_expf_fast(x, t.hi, t.lo); }
 __device__ __forceinline__ float expf_core(float x, const ExpTab &t) { return q3_expf_core(x, t.hi, t.lo); }
 
+// exp(d) for -80 <= d <= 0, where only accuracy is required (softmax: 1e-5
+// relative), in binary32 without the binary64 core.  Cody & Waite's argument
+// reduction (Software Manual for the Elementary Functions, 1980): k = rint(d/ln2)
+// and r = d - k*ln2 with ln2 split as 355/512 (so k*C1 is exact for |k| < 2^15)
+// plus RN(ln2 - 355/512), |r| <= ln2/2; then 2^(r/ln2) from ex2.approx (an
+// argument in [-0.5, 0.5], result in [0.7, 1.42]) and the factor 2^k added to the
+// exponent field (d >= -80 keeps the result a normal number).  Relative error
+// about 2^-22 over the whole range (tests/test_device_math.py sweeps every
+// binary32 d in [-80, 0] against the libm-identical expf).
+__device__ __forceinline__ float ex2_approx_ftz(float x) {
+    float r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+    return r;
+}
+__device__ __forceinline__ float exp_m80_0(float d) {
+    constexpr float LOG2E = 1.44269504088896341f;       // RN(1/ln2)
+    constexpr float C1 = 0.693359375f;                   // 355/512
+    constexpr float C2 = -2.12194440054690583e-4f;       // RN(ln2 - 355/512)
+    const float tm = __fadd_rn(__fmul_rn(d, LOG2E), 12582912.0f);   // k + 1.5*2^23 (round to nearest)
+    const float k = __fsub_rn(tm, 12582912.0f);
+    const float r = __fmaf_rn(-k, C2, __fmaf_rn(-k, C1, d));
+    const float e = ex2_approx_ftz(__fmul_rn(r, LOG2E));
+    const uint32_t scale = uint32_t(__float_as_int(tm) - 0x4B400000) << 23;   // k in the exponent field
+    return __uint_as_float(__float_as_uint(e) + scale);
+}
+
 // ---------------------------------------------------------------------------
 // TMA bulk copies (cp.async.bulk, no tensor map, no multicast) and mbarriers
 // ---------------------------------------------------------------------------

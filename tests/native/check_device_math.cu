@@ -31,6 +31,22 @@ __global__ void check_rcp1(uint32_t lo, uint32_t hi, unsigned long long *bad) {
     if (n) atomicAdd(bad, n);
 }
 
+// (1c) exp_m80_0 (softmax's binary32 exp) on every binary32 d in [-80, 0]:
+//      largest relative error against the binary64 exp, in units of 1e-12
+__global__ void check_exp80(unsigned long long *worst) {
+    unsigned long long w = 0;
+    const uint32_t lo = 0x80000000u, hi = 0xc2a00000u;             // -0 .. -80 (bit patterns ascend)
+    for (uint64_t u = lo + uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; u <= hi;
+         u += uint64_t(gridDim.x) * blockDim.x) {
+        const float d = __uint_as_float(uint32_t(u));
+        const double ref = exp(double(d));
+        const double rel = fabs(double(exp_m80_0(d)) - ref) / ref;
+        const unsigned long long e = (unsigned long long)(rel * 1e12);
+        if (e > w) w = e;
+    }
+    atomicMax(worst, w);
+}
+
 // (2) scale and codes of the fast path == the exact path
 //     q8_scale (IEEE m/127) and q8_code (IEEE division + round half away)
 __device__ __forceinline__ uint32_t hash32(uint32_t x) {
@@ -71,15 +87,16 @@ __global__ void check_q8(uint32_t nm, unsigned long long *bad_scale, unsigned lo
 
 int main() {
     unsigned long long *d;
-    cudaMalloc(&d, 4 * sizeof(unsigned long long));
-    cudaMemset(d, 0, 4 * sizeof(unsigned long long));
+    cudaMalloc(&d, 5 * sizeof(unsigned long long));
+    cudaMemset(d, 0, 5 * sizeof(unsigned long long));
     check_rcp<<<148 * 16, 256>>>(0x3f800000u, 0x7f800001u, d);           // [1, +inf]
     check_q8<<<148 * 8, 128>>>(1u << 20, d + 1, d + 2);
     check_rcp1<<<148 * 16, 256>>>(0x3f800000u, 0x7b800000u, d + 3);     // [1, 2^120)
+    check_exp80<<<148 * 16, 256>>>(d + 4);                                 // [-80, 0]
     cudaError_t e = cudaDeviceSynchronize();
-    unsigned long long h[4] = {~0ull, ~0ull, ~0ull, ~0ull};
+    unsigned long long h[5] = {~0ull, ~0ull, ~0ull, ~0ull, ~0ull};
     cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) { printf("cuda error %s\n", cudaGetErrorString(e)); return 1; }
-    printf("%llu %llu %llu %llu\n", h[0], h[1], h[2], h[3]);
+    printf("%llu %llu %llu %llu %llu\n", h[0], h[1], h[2], h[3], h[4]);
     return 0;
 }
