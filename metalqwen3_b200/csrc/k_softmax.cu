@@ -22,8 +22,9 @@
 //       elements per thread) -> one HBM read, one HBM write;
 //   len > 4096: 512 threads, three passes (max; exp stored in place + sum;
 //       scale), the second and third reads served from L2.
-// Rows start at arbitrary offsets: up to three leading elements reach a
-// 16-byte boundary, the body moves in float4, the remainder is scalar.
+// Rows start at arbitrary addresses (4-byte aligned): up to three leading
+// elements reach a 16-byte boundary, the body moves in float4, the remainder is
+// scalar.
 #include "q3cu_internal.h"
 
 namespace q3 {
@@ -36,9 +37,11 @@ struct RowSplit {
     int nb;     // float4 body count
     int tl;     // trailing scalar elements
 };
-__device__ __forceinline__ RowSplit split_row(int64_t off, int len) {
+// The split of the row starting at `row` (4-byte aligned): by its address, not
+// its offset, since the API asks only 4-byte alignment of the buffer.
+__device__ __forceinline__ RowSplit split_row(const float *row, int len) {
     RowSplit s;
-    s.a = int((4 - (off & 3)) & 3);
+    s.a = int(((16u - (uint32_t(reinterpret_cast<uintptr_t>(row)) & 15u)) & 15u) >> 2);
     if (s.a > len) s.a = len;
     s.nb = (len - s.a) >> 2;
     s.tl = len - s.a - 4 * s.nb;
@@ -51,8 +54,12 @@ __device__ __forceinline__ int scalar_index(const RowSplit &s, int t) {
     return -1;
 }
 
+// The libm-identical exp, out of line: taken for d < -80 or NaN only, so the
+// compiler branches around it instead of predicating it into every element.
+static __device__ __noinline__ float smx_exp_slow(float d, const ExpTab *tab) { return expf_host(d, *tab); }
 __device__ __forceinline__ float smx_exp(float d, const ExpTab &tab) {
-    return d >= -80.0f ? exp_m80_0(d) : expf_host(d, tab);
+    if (__builtin_expect(d >= -80.0f, 1)) return exp_m80_0(d);
+    return smx_exp_slow(d, &tab);
 }
 __device__ __forceinline__ float4 smx_exp4(float4 v, float m, const ExpTab &tab) {
     return make_float4(smx_exp(__fsub_rn(v.x, m), tab), smx_exp(__fsub_rn(v.y, m), tab),
@@ -104,7 +111,7 @@ __global__ void __launch_bounds__(NW * 32) softmax_reg_kernel(float *x, const in
         if (len <= lo || len > hi) continue;                    // block-uniform
         const int64_t off = __ldg(offs + r);
         float *row = x + off;
-        const RowSplit sp = split_row(off, len);
+        const RowSplit sp = split_row(row, len);
         float4 *body = reinterpret_cast<float4 *>(row + sp.a);
 
         float4 v[NB];
@@ -165,7 +172,7 @@ __global__ void __launch_bounds__(SMX_LONG_THREADS) softmax_long_kernel(float *x
         if (len <= lo) continue;
         const int64_t off = __ldg(offs + r);
         float *row = x + off;
-        const RowSplit sp = split_row(off, len);
+        const RowSplit sp = split_row(row, len);
         float4 *body = reinterpret_cast<float4 *>(row + sp.a);
         const int si = scalar_index(sp, t);
 

@@ -304,6 +304,29 @@ def test_softmax_ragged(q3, oracle, lens):
     assert np.array_equal(bits(g[~inrow]), bits(x[~inrow]))
 
 
+@pytest.mark.parametrize("shift", [1, 2, 3])
+def test_softmax_buffer_only_4_byte_aligned(q3, oracle, shift):
+    """The API asks only 4-byte alignment of x: rows of a buffer that starts
+    1-3 floats past a 16-byte boundary, short and long, ragged offsets."""
+    rng = np.random.default_rng(shift)
+    lens = np.array([5, 300, 4096, 4099, 9000, 1, 70], np.int32)
+    off = np.concatenate([[0], np.cumsum(lens + rng.integers(0, 4, lens.size))[:-1]]).astype(np.int64)
+    total = int(off[-1] + lens[-1])
+    x = (2.0 * rng.standard_normal(total)).astype(np.float32)
+    base = dev(np.concatenate([np.zeros(shift, np.float32), x]))
+    view = base[shift:]
+    assert view.data_ptr() % 16 == 4 * shift
+    q3.softmax_rows(view, dev(off), dev(lens))
+    o = oracle.rows_softmax(x, off, lens)
+    g = host(view)
+    inrow = np.zeros(total, bool)
+    for a, n in zip(off, lens):
+        inrow[a:a + n] = True
+    check_softmax(g[inrow], o[inrow], softmax_f64(x, off, lens)[inrow], off, lens)
+    assert np.array_equal(bits(g[~inrow]), bits(x[~inrow]))
+    assert np.array_equal(bits(host(base[:shift])), bits(np.zeros(shift, np.float32)))
+
+
 def test_softmax_max_starts_at_zero(q3, oracle):
     """All-negative rows: the reference's max is 0, not max(x); a row with
     every score below -104 underflows to 0/0 = NaN in the reference."""
