@@ -36,6 +36,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 GS = 64
+E2E_CHUNKS = 8          # token-row chunks of the pipelined end-to-end step
 
 
 # ---------------------------------------------------------------------------- workloads
@@ -120,6 +121,10 @@ class Prefill4B(Workload):
     # -- host (end-to-end) data: inputs copied in, outputs copied out each step
     h2d_keys = ("x", "q", "k", "pos", "hb", "hb2")
     d2h_keys = ("xq", "xs", "q", "k", "hq", "hs")
+
+    def slice(self, d, a, b):
+        """Views of token rows [a, b) of every per-token tensor (weights whole)."""
+        return {k: (v if k in ("w", "qn", "kn") else v[a:b]) for k, v in d.items()}
 
     # -- CPU oracle on a token sample
     def cpu_step(self, oracle, np, sample, threads, rng):
@@ -630,24 +635,54 @@ def main():
     h2d = sum(t.numel() * t.element_size() for t in hin.values())
     d2h = sum(t.numel() * t.element_size() for t in hout.values())
 
+    # Row-sliceable workloads pipeline each step over E2E_CHUNKS token-row chunks:
+    # copy-in on one stream, kernels on another, copy-out on a third, so PCIe
+    # moves inputs and outputs at the same time (it is full duplex).  A chunk's
+    # copy-in for the next step waits for its copy-out (q and k are updated in
+    # place).  Other workloads copy in, run and copy out on one stream.
+    chunks = [(i * wl.tokens // E2E_CHUNKS, (i + 1) * wl.tokens // E2E_CHUNKS)
+              for i in range(E2E_CHUNKS)] if hasattr(wl, "slice") else None
+    s_in, s_out = torch.cuda.Stream(device=dev), torch.cuda.Stream(device=dev)
+    ev_in = [torch.cuda.Event() for _ in range(E2E_CHUNKS)]
+    ev_done = [torch.cuda.Event() for _ in range(E2E_CHUNKS)]
+    ev_out = [torch.cuda.Event() for _ in range(E2E_CHUNKS)]
+
     def e2e_step():
-        with torch.cuda.stream(stream):
-            for k, t in hin.items():
-                d[k].copy_(t, non_blocking=True)
-            (wl.launch_e2e if hasattr(wl, "launch_e2e") else wl.launch)(q3, d, stream)
-            for k, t in hout.items():
-                t.copy_(d[k], non_blocking=True)
+        if chunks is None:
+            with torch.cuda.stream(stream):
+                for k, t in hin.items():
+                    d[k].copy_(t, non_blocking=True)
+                (wl.launch_e2e if hasattr(wl, "launch_e2e") else wl.launch)(q3, d, stream)
+                for k, t in hout.items():
+                    t.copy_(d[k], non_blocking=True)
+            return
+        for c, (a, b) in enumerate(chunks):
+            s_in.wait_event(ev_out[c])
+            with torch.cuda.stream(s_in):
+                for k, t in hin.items():
+                    d[k][a:b].copy_(t[a:b], non_blocking=True)
+                ev_in[c].record(s_in)
+            stream.wait_event(ev_in[c])
+            with torch.cuda.stream(stream):
+                wl.launch(q3, wl.slice(d, a, b), stream)
+                ev_done[c].record(stream)
+            s_out.wait_event(ev_done[c])
+            with torch.cuda.stream(s_out):
+                for k, t in hout.items():
+                    t[a:b].copy_(d[k][a:b], non_blocking=True)
+                ev_out[c].record(s_out)
 
     for _ in range(2):
         e2e_step()
-    stream.synchronize()
+    torch.cuda.synchronize(dev)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
+    first, last = (stream, stream) if chunks is None else (s_in, s_out)
+    e0.record(first)
     for _ in range(args.e2e_steps):
         e2e_step()
-    e1.record(stream)
-    stream.synchronize()
+    e1.record(last)
+    torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
     if world > 1:
         t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
@@ -687,8 +722,9 @@ def main():
             "e2e": {"value": round(world * e2e_bytes * args.e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
-                    "path": "pinned host inputs -> cudaMemcpyAsync H2D -> q3cu C ABI kernels -> D2H, per step"
-                            + (f"; {wl.e2e_note}" if wl.e2e_note else "")},
+                    "path": ("pinned host inputs -> cudaMemcpyAsync H2D -> q3cu C ABI kernels -> D2H, per step"
+                             + (f", pipelined over {E2E_CHUNKS} token-row chunks on three streams (copy-in, "
+                                "kernels, copy-out)" if chunks else "") + (f"; {wl.e2e_note}" if wl.e2e_note else ""))},
             "gpu_launches": launches,
             "clocks": clk,
         }
