@@ -19,7 +19,8 @@ value = algorithmic bytes (every input read once + every output written once)
 of all ranks / max-over-ranks device time.  Under torchrun each rank runs its own
 batch on its own GPU (token rows are independent: weak scaling, no collective on
 the data path).  Between timed steps L2 is flushed by writing a 256 MiB buffer
-outside the timed events.
+and then reading another 256 MiB buffer, outside the timed events (the read
+makes the write's dirty lines drain there, not in the next step's first kernel).
 """
 from __future__ import annotations
 
@@ -469,14 +470,21 @@ def measured_hbm_peak():
         return 6650.0, "fallback"
 
 
-def profiled_traffic(workload, kernel):
-    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, or None."""
+def profiled_traffic(workload, kernel, units=None):
+    """Per-launch DRAM bytes of `kernel` from the committed ncu summary, or None.
+
+    A capture taken on a smaller batch (its entry names the units it processed)
+    is scaled to `units` in proportion."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(p) as f:
-            return json.load(f)[workload][kernel]["dram_bytes_per_launch"]
+            e = json.load(f)[workload][kernel]
     except Exception:
         return None
+    b = e["dram_bytes_per_launch"]
+    if "units" in e and units is not None and units != e["units"]:
+        b = round(b * units / e["units"])
+    return b
 
 
 def cpu_baseline(workload, seconds=10.0):
@@ -589,7 +597,15 @@ def main():
     stream = torch.cuda.Stream(device=dev)
     d = wl.make(torch, dev, seed=1234 + rank)
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    flush_r = torch.zeros(32 << 20, dtype=torch.int64, device=dev)
     nk = len(wl.kernels())
+
+    def cold_l2():
+        # Write 256 MiB, then read another 256 MiB: the step's inputs leave L2
+        # and the lines the write left dirty are written back here, not inside
+        # the next step's first kernel.
+        flush.fill_(1)
+        flush_r.amax()
 
     def barrier():
         if world > 1:
@@ -599,7 +615,7 @@ def main():
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
             wl.launch(q3, d, stream)
-            flush.fill_(1)
+            cold_l2()
     stream.synchronize()
     if q3.device_status(stream) != 0:
         raise RuntimeError("device status set during warm-up")
@@ -613,7 +629,7 @@ def main():
     with torch.cuda.stream(stream):
         for i in range(args.steps):
             launches += wl.launch(q3, d, stream, events=ev[i])
-            flush.fill_(1)                      # outside the events: L2 cold for the next step
+            cold_l2()                           # outside the events: L2 cold for the next step
     stream.synchronize()
     torch.cuda.synchronize(dev)
     barrier()
@@ -709,7 +725,7 @@ def main():
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
             "config": dict(wl.config(), parallelism=f"token rows x{world} (weak)",
-                           l2="flushed between timed steps (256 MiB write outside the events); "
+                           l2="flushed between timed steps (256 MiB write + 256 MiB read of another buffer, outside the events); "
                               f"step working set {step_bytes / 1e6:.0f} MB vs 126 MB L2"),
             "tokens_per_s": round(world * wl.tokens * args.steps / (total_ms / 1e3), 1),
             "hbm_frac": round(gbs / world / peak, 4),
@@ -717,7 +733,7 @@ def main():
             "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s", "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": profiled_traffic(wl.name, dom_name),
+                         "traffic": profiled_traffic(wl.name, dom_name, wl.tokens),
                          "algorithmic_bytes_per_launch": dom_bytes},
             "e2e": {"value": round(world * e2e_bytes * args.e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
