@@ -11,26 +11,46 @@
 // below -80 or NaN takes the libm-identical expf, so the reference's underflow
 // (a row entirely below -104 is 0/0 = NaN) is reproduced.  Each float4's four
 // exponentials are added in binary32 and the partial sums accumulated in
-// binary64 (per thread, then a tree): closer to the exact sum than the
-// reference's sequential binary32 sum.  The tests bound the outputs (1e-5 rel /
-// 1e-6 abs of a binary64 softmax, and no further from the oracle than the
-// oracle is from it).
+// binary64 (per thread, then a fixed tree): closer to the exact sum than the
+// reference's sequential binary32 sum, and deterministic.  The tests bound the
+// outputs (1e-5 rel / 1e-6 abs of a binary64 softmax, and no further from the
+// oracle than the oracle is from it).
 //
-// Rows are bucketed by length into five kernels, each a grid-stride loop over
-// all rows that skips rows outside its bucket:
-//   len <= 512*NW (NW = 1, 2, 4, 8 warps): the row lives in registers (16
-//       elements per thread) -> one HBM read, one HBM write;
-//   len > 4096: 512 threads, three passes (max; exp stored in place + sum;
-//       scale), the second and third reads served from L2.
-// Rows start at arbitrary addresses (4-byte aligned): up to three leading
-// elements reach a 16-byte boundary, the body moves in float4, the remainder is
-// scalar.
+// One launch for every row length.  A persistent CTA per SM streams whole rows
+// through a 224 KB shared-memory ring, so HBM sees each score read once and
+// written once, with up to the whole ring in flight per SM:
+//
+//   producer warp   takes units of `unit` consecutive rows from a device
+//                   counter (dynamic balance across SMs), and for each row of
+//                   positive length reserves ring space in order, fills a slot
+//                   descriptor (offset, length, the up-to-six scalars outside
+//                   the row's 16-byte-aligned body) and bulk-copies the body
+//                   (cp.async.bulk, completing on the slot's mbarrier);
+//   15 consumer     walk the slots in order.  A row of <= SMX_WMAX scores
+//   warps           belongs to one warp (round-robin); a longer row is shared
+//                   by all 15, whose two reductions meet on mbarriers (bounded
+//                   waits, no unbounded bar.sync).  A row too long for the ring
+//                   is read from and written to global memory in three passes.
+//                   Max, then exp written back over the staged scores with the
+//                   sum, then the scaled scores stored straight to HBM.  Every
+//                   warp arrives once per slot on its `empty` barrier.
+//
+// The ring is reclaimed in order (the producer waits for the oldest slot's
+// release), so slot k's buffer is reused only after all 15 warps are done
+// with it; the parity waits stay exact because every consumer warp waits on
+// every slot in sequence.  The counter pair {next unit, finished CTAs} is reset
+// by the last CTA to finish, so it is zero for the next launch on that pair.
 #include "q3cu_internal.h"
 
 namespace q3 {
 
-constexpr int SMX_PER_THREAD = 16;            // register-resident elements per thread (body)
-constexpr int SMX_LONG_THREADS = 512;
+constexpr int SMX_CW = 15;                       // consumer warps (16 warps in all: 128 registers each)
+constexpr int SMX_CT = SMX_CW * 32;              // consumer threads
+constexpr int SMX_THREADS = SMX_CT + 32;         // + the producer warp
+constexpr int SMX_NSLOT = 32;                    // slots (rows staged or queued) per CTA
+constexpr uint32_t SMX_RING = 224u * 1024u;      // ring bytes: rows of up to 57344 scores are staged
+constexpr int SMX_WMAX = 4096;                   // rows up to this length: one warp
+constexpr int SMX_UNIT_MAX = 32;                 // rows per unit taken from the counter (lanes of the producer)
 
 struct RowSplit {
     int a;      // leading scalar elements before the first 16-byte boundary
@@ -47,185 +67,326 @@ __device__ __forceinline__ RowSplit split_row(const float *row, int len) {
     s.tl = len - s.a - 4 * s.nb;
     return s;
 }
-// scalar element handled by thread t (head then tail), or -1
-__device__ __forceinline__ int scalar_index(const RowSplit &s, int t) {
-    if (t < s.a) return t;
-    if (t - s.a < s.tl) return s.a + 4 * s.nb + (t - s.a);
-    return -1;
-}
 
-// The libm-identical exp, out of line: taken for d < -80 or NaN only, so the
-// compiler branches around it instead of predicating it into every element.
-static __device__ __noinline__ float smx_exp_slow(float d, const ExpTab *tab) { return expf_host(d, *tab); }
-__device__ __forceinline__ float smx_exp(float d, const ExpTab &tab) {
-    if (__builtin_expect(d >= -80.0f, 1)) return exp_m80_0(d);
-    return smx_exp_slow(d, &tab);
+struct SmxDesc {
+    int64_t off;      // first score of the row in x
+    int32_t len;      // < 0: end of the sequence
+    int32_t sidx;     // float4 index of the staged body in the ring; -1: not staged (global)
+    int32_t nb;       // float4 body count
+    int16_t a, tl;    // leading / trailing scalar counts (<= 3 each)
+    float sc[6];      // sc[0..a) leading scalars, sc[3..3+tl) trailing scalars
+};
+static_assert(sizeof(SmxDesc) == 48, "descriptor layout");
+
+// exp(v - m) of four scores: exp_m80_0 for d = v - m in [-80, 0] (every d once
+// the max is known, except far-below-max scores and NaN).  Returns false if any
+// d is outside that range, in which case the caller recomputes the four with
+// smx_exp4_exact (the libm-identical expf: subnormal results and NaN as the
+// reference has them), a branch that is cold in practice and kept out of the
+// hot loop's register allocation.
+__device__ __forceinline__ bool smx_exp4(float4 &v, float m) {
+    const float d0 = __fsub_rn(v.x, m), d1 = __fsub_rn(v.y, m), d2 = __fsub_rn(v.z, m), d3 = __fsub_rn(v.w, m);
+    const bool ok = (d0 >= -80.0f) & (d1 >= -80.0f) & (d2 >= -80.0f) & (d3 >= -80.0f);
+    v = make_float4(exp_m80_0(d0), exp_m80_0(d1), exp_m80_0(d2), exp_m80_0(d3));
+    return ok;
 }
-__device__ __forceinline__ float4 smx_exp4(float4 v, float m, const ExpTab &tab) {
-    return make_float4(smx_exp(__fsub_rn(v.x, m), tab), smx_exp(__fsub_rn(v.y, m), tab),
-                       smx_exp(__fsub_rn(v.z, m), tab), smx_exp(__fsub_rn(v.w, m), tab));
+static __device__ __noinline__ float smx_exp_slow(float d, const ExpTab *tab) { return expf_host(d, *tab); }
+__device__ __forceinline__ float smx_exp1(float d, const ExpTab &tab) {
+    return d >= -80.0f ? exp_m80_0(d) : smx_exp_slow(d, &tab);
+}
+__device__ __forceinline__ float4 smx_exp4_exact(float4 v, float m, const ExpTab &tab) {
+    return make_float4(smx_exp1(__fsub_rn(v.x, m), tab), smx_exp1(__fsub_rn(v.y, m), tab),
+                       smx_exp1(__fsub_rn(v.z, m), tab), smx_exp1(__fsub_rn(v.w, m), tab));
 }
 __device__ __forceinline__ double sum4(float4 v) {
     return double(__fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w)));
 }
-
-template <int NW>
-__device__ __forceinline__ float block_max(float v, float *sh) {
-    v = warp_max(v);
-    if constexpr (NW == 1) return v;
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    __syncthreads();                          // sh free from a previous reduction
-    if (lane == 0) sh[w] = v;
-    __syncthreads();
-    float r = lane < NW ? sh[lane] : 0.0f;
-    return warp_max(r);
+__device__ __forceinline__ float max4(float m, float4 v) {
+    return fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
 }
-template <int NW>
-__device__ __forceinline__ double block_sum(double v, double *sh) {
-    v = warp_sum_d(v);
-    if constexpr (NW == 1) return v;
-    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
-    __syncthreads();
-    if (lane == 0) sh[w] = v;
-    __syncthreads();
-    double r = lane < NW ? sh[lane] : 0.0;
-    return warp_sum_d(r);
+__device__ __forceinline__ float4 scale4(float4 v, float inv) {
+    return make_float4(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv), __fmul_rn(v.w, inv));
+}
+// Orders this thread's earlier generic-proxy shared-memory writes before the
+// bulk copies the producer issues into the same bytes after the release.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// ---- register-resident rows: lo < len <= hi ------------------------------
-template <int NW>
-__global__ void __launch_bounds__(NW * 32) softmax_reg_kernel(float *x, const int64_t *__restrict__ offs,
-                                                              const int32_t *__restrict__ lens, int64_t rows,
-                                                              int lo, int hi) {
-    constexpr int NT = NW * 32;
-    constexpr int NB = SMX_PER_THREAD / 4;    // float4 slots per thread
-    __shared__ ExpTab s_tab;
-    __shared__ float sh_f[NW];
-    __shared__ double sh_d[NW];
-    load_exp_table(s_tab);
-    __syncthreads();
-    const int t = threadIdx.x;
+// One row by NT threads (t = 0..NT-1): a warp (NT = 32) or the 15 consumer
+// warps (NT = 480, reductions on the two mbarriers of `red`).  Returns false
+// if a reduction wait gave up (status recorded).
+template <int NT, int U, bool STAGED>
+__device__ __forceinline__ bool smx_row(float *x, float4 *ring, const SmxDesc &d, int t, const ExpTab &tab,
+                                        uint64_t *red, uint32_t red_par, float *red_f, double *red_d,
+                                        uint32_t *status) {
+    const int lane = t & 31, w = t >> 5;
+    float *row = x + d.off;
+    const int a = d.a, tl = d.tl, nb = d.nb;
+    float4 *sb = STAGED ? ring + d.sidx : nullptr;
+    float4 *gb = reinterpret_cast<float4 *>(row + a);
+    // scalar handled by thread t: head t (t < a) or tail t - a
+    const int si = t < a ? t : (t - a < tl ? 3 + (t - a) : -1);
+    const int64_t spos = t < a ? t : a + 4 * int64_t(nb) + (t - a);
 
-    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-        const int len = __ldg(lens + r);
-        if (len <= lo || len > hi) continue;                    // block-uniform
-        const int64_t off = __ldg(offs + r);
-        float *row = x + off;
-        const RowSplit sp = split_row(row, len);
-        float4 *body = reinterpret_cast<float4 *>(row + sp.a);
-
-        float4 v[NB];
-        float m = 0.0f;                                         // the reference's max starts at 0
+    // Each pass moves U float4 per thread per step: all U loads are issued
+    // before their uses (the asm loads and stores are ordered).
+    auto load4 = [&](int j0, float4 *v) {
 #pragma unroll
-        for (int j = 0; j < NB; ++j) {
-            const int bi = t + j * NT;
-            if (bi < sp.nb) {
-                v[j] = u4_as_f4(ld_v4(body + bi));
-                m = fmaxf(m, fmaxf(fmaxf(v[j].x, v[j].y), fmaxf(v[j].z, v[j].w)));
-            }
+        for (int u = 0; u < U; ++u) {
+            const int j = j0 + u * NT;
+            if (j < nb) v[u] = STAGED ? sb[j] : u4_as_f4(ld_v4(gb + j));
         }
-        const int si = scalar_index(sp, t);
-        float xs = 0.0f;
-        if (si >= 0) { xs = row[si]; m = fmaxf(m, xs); }
-        m = block_max<NW>(m, sh_f);
-
-        double sum = 0.0;
-#pragma unroll
-        for (int j = 0; j < NB; ++j) {
-            if (t + j * NT < sp.nb) {
-                v[j] = smx_exp4(v[j], m, s_tab);
-                sum += sum4(v[j]);
-            }
-        }
-        if (si >= 0) { xs = smx_exp(__fsub_rn(xs, m), s_tab); sum += double(xs); }
-        sum = block_sum<NW>(sum, sh_d);
-        const float inv = float(1.0 / sum);
-
-#pragma unroll
-        for (int j = 0; j < NB; ++j) {
-            const int bi = t + j * NT;
-            if (bi < sp.nb) {
-                float4 o = make_float4(__fmul_rn(v[j].x, inv), __fmul_rn(v[j].y, inv), __fmul_rn(v[j].z, inv),
-                                       __fmul_rn(v[j].w, inv));
-                st_cs_v4(body + bi, f4_as_u4(o));
-            }
-        }
-        if (si >= 0) row[si] = __fmul_rn(xs, inv);
-    }
-}
-
-// ---- long rows (len > lo): three passes -----------------------------------
-__global__ void __launch_bounds__(SMX_LONG_THREADS) softmax_long_kernel(float *x, const int64_t *__restrict__ offs,
-                                                                        const int32_t *__restrict__ lens,
-                                                                        int64_t rows, int lo) {
-    constexpr int NW = SMX_LONG_THREADS / 32;
-    constexpr int NT = SMX_LONG_THREADS;
-    __shared__ ExpTab s_tab;
-    __shared__ float sh_f[NW];
-    __shared__ double sh_d[NW];
-    load_exp_table(s_tab);
-    __syncthreads();
-    const int t = threadIdx.x;
-
-    for (int64_t r = blockIdx.x; r < rows; r += gridDim.x) {
-        const int len = __ldg(lens + r);
-        if (len <= lo) continue;
-        const int64_t off = __ldg(offs + r);
-        float *row = x + off;
-        const RowSplit sp = split_row(row, len);
-        float4 *body = reinterpret_cast<float4 *>(row + sp.a);
-        const int si = scalar_index(sp, t);
-
-        // pass A: max
-        float m = 0.0f;
-#pragma unroll 4
-        for (int bi = t; bi < sp.nb; bi += NT) {
-            const float4 v = u4_as_f4(ld_v4(body + bi));
-            m = fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
-        }
-        if (si >= 0) m = fmaxf(m, row[si]);
-        m = block_max<NW>(m, sh_f);
-
-        // pass B: exponentials in place, binary64 sum
-        double sum = 0.0;
-#pragma unroll 4
-        for (int bi = t; bi < sp.nb; bi += NT) {
-            const float4 v = smx_exp4(u4_as_f4(ld_v4(body + bi)), m, s_tab);
-            sum += sum4(v);
-            *reinterpret_cast<uint4 *>(body + bi) = f4_as_u4(v);
-        }
-        if (si >= 0) {
-            const float e = smx_exp(__fsub_rn(row[si], m), s_tab);
-            row[si] = e;
-            sum += double(e);
-        }
-        sum = block_sum<NW>(sum, sh_d);      // its barriers also order pass B's stores before pass C
-        const float inv = float(1.0 / sum);
-
-        // pass C: scale
-#pragma unroll 4
-        for (int bi = t; bi < sp.nb; bi += NT) {
-            const float4 v = u4_as_f4(ld_v4(body + bi));
-            st_cs_v4(body + bi, f4_as_u4(make_float4(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv),
-                                                     __fmul_rn(v.z, inv), __fmul_rn(v.w, inv))));
-        }
-        if (si >= 0) row[si] = __fmul_rn(row[si], inv);
-        __syncthreads();
-    }
-}
-
-cudaError_t launch_softmax_rows(float *x, const int64_t *off, const int32_t *len, int64_t rows, cudaStream_t stream,
-                                int sms) {
-    if (rows == 0) return cudaSuccess;
-    auto grid = [&](int per_sm) {
-        int64_t g = int64_t(sms) * per_sm;
-        return unsigned(rows < g ? rows : g);
     };
-    softmax_reg_kernel<1><<<grid(32), 32, 0, stream>>>(x, off, len, rows, 0, 512);
-    softmax_reg_kernel<2><<<grid(16), 64, 0, stream>>>(x, off, len, rows, 512, 1024);
-    softmax_reg_kernel<4><<<grid(8), 128, 0, stream>>>(x, off, len, rows, 1024, 2048);
-    softmax_reg_kernel<8><<<grid(4), 256, 0, stream>>>(x, off, len, rows, 2048, 4096);
-    softmax_long_kernel<<<grid(4), SMX_LONG_THREADS, 0, stream>>>(x, off, len, rows, 4096);
+    float m = 0.0f;                               // the reference's max starts at 0
+    for (int j0 = t; j0 < nb; j0 += U * NT) {
+        float4 v[U];
+        load4(j0, v);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (j0 + u * NT < nb) m = max4(m, v[u]);
+    }
+    float xs = 0.0f;
+    if (si >= 0) { xs = d.sc[si]; m = fmaxf(m, xs); }
+    m = warp_max(m);
+    if constexpr (NT > 32) {
+        if (lane == 0) red_f[w] = m;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&red[0]);
+        if (!__all_sync(FULL, mbar_wait(&red[0], red_par, lane == 0 ? status : nullptr))) return false;
+        m = warp_max(lane < NT / 32 ? red_f[lane] : 0.0f);
+    }
+
+    double s = 0.0;
+    for (int j0 = t; j0 < nb; j0 += U * NT) {
+        float4 v[U];
+        load4(j0, v);
+        float4 e[U];
+        bool ok = true;
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            e[u] = v[u];
+            if (j0 + u * NT < nb) ok &= smx_exp4(e[u], m);
+        }
+        if (__builtin_expect(!ok, 0)) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) e[u] = smx_exp4_exact(v[u], m, tab);
+        }
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int j = j0 + u * NT;
+            if (j < nb) {
+                if constexpr (STAGED) sb[j] = e[u];
+                else *reinterpret_cast<uint4 *>(gb + j) = f4_as_u4(e[u]);
+                s += sum4(e[u]);
+            }
+        }
+    }
+    if (si >= 0) { xs = smx_exp1(__fsub_rn(xs, m), tab); s += double(xs); }
+    s = warp_sum_d(s);
+    if constexpr (NT > 32) {
+        if (lane == 0) red_d[w] = s;
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&red[1]);
+        if (!__all_sync(FULL, mbar_wait(&red[1], red_par, lane == 0 ? status : nullptr))) return false;
+        s = warp_sum_d(lane < NT / 32 ? red_d[lane] : 0.0);
+    }
+    const float inv = float(1.0 / s);
+
+    for (int j0 = t; j0 < nb; j0 += U * NT) {
+        float4 v[U];
+        load4(j0, v);
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+            if (j0 + u * NT < nb) st_cs_v4(gb + j0 + u * NT, f4_as_u4(scale4(v[u], inv)));
+    }
+    if (si >= 0) row[spos] = __fmul_rn(xs, inv);
+    return true;
+}
+
+__global__ void __launch_bounds__(SMX_THREADS, 1)
+softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *__restrict__ lens, int64_t rows,
+                    int unit, uint32_t *sched, uint32_t *status) {
+    extern __shared__ __align__(128) float4 ring[];
+    __shared__ ExpTab s_tab;
+    __shared__ __align__(8) uint64_t full[SMX_NSLOT], empty[SMX_NSLOT], red[2];
+    __shared__ SmxDesc desc[SMX_NSLOT];
+    __shared__ uint64_t s_end[SMX_NSLOT];        // ring position just past each slot's bytes
+    __shared__ float red_f[SMX_CW];
+    __shared__ double red_d[SMX_CW];
+    __shared__ int fail_sh;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+    load_exp_table(s_tab);
+    if (tid == 0) {
+        for (int i = 0; i < SMX_NSLOT; ++i) {
+            mbar_init(&full[i], 1);
+            mbar_init(&empty[i], SMX_CW);
+        }
+        mbar_init(&red[0], SMX_CW);
+        mbar_init(&red[1], SMX_CW);
+        fail_sh = 0;
+        mbar_init_fence();
+    }
+    __syncthreads();
+
+    // ---- producer warp -----------------------------------------------------
+    if (warp == SMX_CW) {
+        const uint64_t units = (uint64_t(rows) + unit - 1) / unit;
+        uint32_t nxt = 0;
+        if (lane == 0) nxt = atomicAdd(&sched[0], 1u);
+        nxt = __shfl_sync(FULL, nxt, 0);
+        uint64_t alloc = 0, freed = 0;            // monotonic ring byte positions
+        uint32_t k = 0, oldest = 0;               // next sequence number; oldest not yet reclaimed
+        bool ok = true;
+        // Reserves `bytes` (a multiple of 16) for sequence k; *at = ring byte offset.
+        // Regions are contiguous (one that would cross the end starts at 0) and
+        // reclaimed in sequence order, so [freed, alloc) holds every live byte.
+        auto reserve = [&](uint32_t bytes, uint32_t *at) -> bool {
+            uint64_t start = alloc;
+            const uint64_t o = start % SMX_RING;
+            if (o + bytes > SMX_RING) start += SMX_RING - o;
+            while (oldest + SMX_NSLOT <= k || start + bytes > freed + SMX_RING) {
+                if (oldest == k) { freed = start; break; }            // nothing live: the skipped tail is free
+                if (__any_sync(FULL, fail_sh != 0)) return false;
+                if (!__all_sync(FULL, mbar_wait(&empty[oldest % SMX_NSLOT], (oldest / SMX_NSLOT) & 1u,
+                                                lane == 0 ? status : nullptr)))
+                    return false;
+                freed = s_end[oldest % SMX_NSLOT];
+                ++oldest;
+            }
+            alloc = start + bytes;
+            *at = uint32_t(start % SMX_RING);
+            s_end[k % SMX_NSLOT] = alloc;         // every lane stores the same value and later reads its own
+            return true;
+        };
+        uint8_t *ring_b = reinterpret_cast<uint8_t *>(ring);
+        while (ok) {
+            const uint64_t b = nxt;
+            if (b >= units) break;
+            if (lane == 0) nxt = atomicAdd(&sched[0], 1u);      // the next unit, in flight meanwhile
+            const int64_t r = int64_t(b) * unit + lane;
+            const bool valid = lane < unit && r < rows;
+            const int len = valid ? __ldg(lens + r) : 0;
+            const int64_t off = valid ? __ldg(offs + r) : 0;
+            float *row = x + off;
+            RowSplit sp{0, 0, 0};
+            if (len > 0) sp = split_row(row, len);
+            const bool staged = len > 0 && (len <= SMX_WMAX || uint64_t(sp.nb) * 16u <= SMX_RING);
+            const uint32_t bytes = staged ? uint32_t(sp.nb) * 16u : 0u;
+            float sc[6];
+#pragma unroll
+            for (int i = 0; i < 3; ++i) {
+                sc[i] = i < sp.a ? row[i] : 0.0f;
+                sc[3 + i] = i < sp.tl ? row[sp.a + 4 * int64_t(sp.nb) + i] : 0.0f;
+            }
+            uint32_t live = __ballot_sync(FULL, len > 0);
+            while (live) {
+                const int j = __ffs(live) - 1;
+                live &= live - 1;
+                const uint32_t bj = __shfl_sync(FULL, bytes, j);
+                uint32_t at = 0;
+                if (!reserve(bj, &at)) { ok = false; break; }
+                if (lane == j) {
+                    const int s = int(k % SMX_NSLOT);
+                    SmxDesc &d = desc[s];
+                    d.off = off;
+                    d.len = len;
+                    d.sidx = staged ? int32_t(at / 16u) : -1;
+                    d.nb = sp.nb;
+                    d.a = int16_t(sp.a);
+                    d.tl = int16_t(sp.tl);
+#pragma unroll
+                    for (int i = 0; i < 6; ++i) d.sc[i] = sc[i];
+                    if (bytes) {
+                        mbar_arrive_expect_tx(&full[s], bytes);
+                        bulk_g2s(ring_b + at, row + sp.a, bytes, &full[s]);
+                    } else {
+                        mbar_arrive(&full[s]);
+                    }
+                }
+                ++k;
+                __syncwarp();
+            }
+            nxt = __shfl_sync(FULL, nxt, 0);
+        }
+        if (ok) {                                  // end of the sequence
+            uint32_t at = 0;
+            if (reserve(0, &at)) {
+                if (lane == 0) {
+                    desc[k % SMX_NSLOT].len = -1;
+                    mbar_arrive(&full[k % SMX_NSLOT]);
+                }
+                ++k;
+            } else {
+                ok = false;
+            }
+        }
+        if (!ok) {
+            // After a failure, no copy may still be landing when the CTA exits:
+            // bounded wait for every slot not yet reclaimed.
+            if (lane == 0)
+                for (uint32_t s = oldest; s < k; ++s)
+                    mbar_wait(&full[s % SMX_NSLOT], (s / SMX_NSLOT) & 1u, nullptr);
+        }
+        // The last CTA to finish resets the counter pair for the next launch.
+        if (lane == 0) {
+            __threadfence();
+            if (atomicAdd(&sched[1], 1u) == gridDim.x - 1) {
+                sched[0] = 0;
+                sched[1] = 0;
+                __threadfence();
+            }
+        }
+        return;
+    }
+
+    // ---- consumer warps ----------------------------------------------------
+    uint32_t wc = 0, cc = 0;                      // rows seen of one warp / of all warps
+    for (uint32_t k = 0;; ++k) {
+        const int s = int(k % SMX_NSLOT);
+        if (__any_sync(FULL, fail_sh != 0)) break;
+        if (!__all_sync(FULL, mbar_wait(&full[s], (k / SMX_NSLOT) & 1u, lane == 0 ? status : nullptr))) {
+            fail_sh = 1;
+            break;
+        }
+        const SmxDesc &d = desc[s];
+        const int len = d.len;
+        if (len < 0) break;
+        bool ok = true;
+        if (len <= SMX_WMAX) {
+            if (int(wc % SMX_CW) == warp) smx_row<32, 4, true>(x, ring, d, lane, s_tab, nullptr, 0, nullptr, nullptr, status);
+            ++wc;
+        } else {
+            ok = d.sidx >= 0 ? smx_row<SMX_CT, 2, true>(x, ring, d, tid, s_tab, red, cc & 1u, red_f, red_d, status)
+                             : smx_row<SMX_CT, 1, false>(x, ring, d, tid, s_tab, red, cc & 1u, red_f, red_d, status);
+            ++cc;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&empty[s]);
+        if (!ok) {
+            fail_sh = 1;
+            break;
+        }
+    }
+}
+
+constexpr int SMX_SMEM_SLOT = 8;
+
+cudaError_t launch_softmax_rows(float *x, const int64_t *off, const int32_t *len, int64_t rows, uint32_t *sched,
+                                uint32_t *status, cudaStream_t stream, int sms) {
+    if (rows <= 0) return cudaSuccess;
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(softmax_ring_kernel), SMX_RING, SMX_SMEM_SLOT);
+    if (e != cudaSuccess) return e;
+    // Units small enough that every SM takes about 16 of them (balance), at
+    // most one row per producer lane.
+    int64_t unit = rows / (int64_t(sms) * 16);
+    unit = unit < 1 ? 1 : (unit > SMX_UNIT_MAX ? SMX_UNIT_MAX : unit);
+    const int64_t units = (rows + unit - 1) / unit;
+    if (units > int64_t(0x7fffffff)) return cudaErrorInvalidValue;     // the unit counter is 32-bit
+    const unsigned grid = unsigned(units < sms ? units : sms);
+    softmax_ring_kernel<<<grid, SMX_THREADS, SMX_RING, stream>>>(x, off, len, rows, int(unit), sched, status);
     return cudaGetLastError();
 }
 

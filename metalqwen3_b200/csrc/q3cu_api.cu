@@ -16,10 +16,18 @@
 
 #include "q3cu_internal.h"
 
+// Softmax launches take their row counters from a ring of pairs (see
+// launch_softmax below).
+constexpr int SCHED_PAIRS = 64;
+
 struct q3cu_ctx {
     int device = -1;
     int sms = 0;
     uint32_t *d_status = nullptr;           // device status word (Q3CU_DEV_* bits)
+    uint32_t *d_sched = nullptr;            // SCHED_PAIRS softmax counter pairs, zero between launches
+    cudaEvent_t sched_ev[SCHED_PAIRS] = {}; // the latest launch on each pair
+    uint32_t sched_next = 0;
+    std::mutex sched_mu;
     cudaStream_t stream = nullptr;          // the host-pointer wrappers' stream
     void *d_scratch = nullptr;              // staging for the host-pointer wrappers
     size_t scratch_bytes = 0;
@@ -86,6 +94,31 @@ const q3::InvFreq &inv_freq_for(q3cu_ctx *ctx, int head_dim, float theta) {
     const int half = head_dim / 2;
     for (int j = 0; j < half && j < 64; ++j) f.v[j] = powf(theta, -(float)j / half);
     return ctx->inv_freq.emplace(key, f).first->second;
+}
+
+// The softmax kernel balances rows across SMs with a pair of device counters
+// that must be zero at launch; the kernel's last CTA zeroes them again.  Each
+// launch takes the next pair of a ring of SCHED_PAIRS, and the stream first
+// waits for the previous launch on that pair (its event), so launches on
+// different streams never share a pair while running.  Inside a stream capture
+// the wait and record are left out (the event was recorded outside the
+// capture); the captured launch keeps its pair.
+q3cu_status launch_softmax(q3cu_ctx *ctx, float *x, const int64_t *off, const int32_t *len, int64_t rows,
+                           cudaStream_t stream) {
+    if (rows == 0) return Q3CU_OK;
+    std::lock_guard<std::mutex> lock(ctx->sched_mu);
+    const uint32_t i = ctx->sched_next++ % SCHED_PAIRS;
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    cudaError_t e = cudaStreamIsCapturing(stream, &cs);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamIsCapturing");
+    const bool eager = cs == cudaStreamCaptureStatusNone;
+    if (eager && (e = cudaStreamWaitEvent(stream, ctx->sched_ev[i], 0)) != cudaSuccess)
+        return cuda_fail(e, "cudaStreamWaitEvent");
+    e = q3::launch_softmax_rows(x, off, len, rows, ctx->d_sched + size_t(i) * q3::SMX_SCHED_WORDS, ctx->d_status,
+                                stream, ctx->sms);
+    if (e != cudaSuccess) return cuda_fail(e, "softmax launch");
+    if (eager && (e = cudaEventRecord(ctx->sched_ev[i], stream)) != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+    return Q3CU_OK;
 }
 
 q3cu_status grow_scratch(q3cu_ctx *ctx, size_t bytes) {
@@ -165,12 +198,22 @@ q3cu_status q3cu_init(int device, q3cu_ctx **out) {
     if (e == cudaSuccess) e = cudaMalloc(&ctx->d_status, sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaMemset(ctx->d_status, 0, sizeof(uint32_t));
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking);
-    cudaSetDevice(prev);
+    const size_t sched_bytes = size_t(SCHED_PAIRS) * q3::SMX_SCHED_WORDS * sizeof(uint32_t);
+    if (e == cudaSuccess) e = cudaMalloc(&ctx->d_sched, sched_bytes);
+    if (e == cudaSuccess) e = cudaMemset(ctx->d_sched, 0, sched_bytes);
+    for (int i = 0; i < SCHED_PAIRS && e == cudaSuccess; ++i)
+        e = cudaEventCreateWithFlags(&ctx->sched_ev[i], cudaEventDisableTiming);
     if (e != cudaSuccess) {
+        for (int i = 0; i < SCHED_PAIRS; ++i)
+            if (ctx->sched_ev[i]) cudaEventDestroy(ctx->sched_ev[i]);
+        if (ctx->d_sched) cudaFree(ctx->d_sched);
+        if (ctx->stream) cudaStreamDestroy(ctx->stream);
         if (ctx->d_status) cudaFree(ctx->d_status);
+        cudaSetDevice(prev);
         delete ctx;
         return cuda_fail(e, "q3cu_init");
     }
+    cudaSetDevice(prev);
     ctx->alive = true;
     *out = ctx;
     return Q3CU_OK;
@@ -184,6 +227,11 @@ q3cu_status q3cu_destroy(q3cu_ctx *ctx) {
     if (ctx->stream) cudaStreamSynchronize(ctx->stream);
     if (ctx->stream) cudaStreamDestroy(ctx->stream);
     if (ctx->d_scratch) cudaFree(ctx->d_scratch);
+    for (int i = 0; i < SCHED_PAIRS; ++i) {
+        if (ctx->sched_ev[i]) cudaEventSynchronize(ctx->sched_ev[i]);
+        if (ctx->sched_ev[i]) cudaEventDestroy(ctx->sched_ev[i]);
+    }
+    if (ctx->d_sched) cudaFree(ctx->d_sched);
     if (ctx->d_status) cudaFree(ctx->d_status);
     cudaSetDevice(prev);
     ctx->alive = false;
@@ -320,8 +368,7 @@ q3cu_status q3cu_softmax_rows(q3cu_ctx *ctx, float *x, const int64_t *row_off, c
     if (rows > 0 && (!x || !row_off || !row_len)) return fail(Q3CU_ERR_INVALID, "NULL pointer");
     if (!aligned(x, 4) || !aligned(row_off, 8) || !aligned(row_len, 4)) return fail(Q3CU_ERR_ALIGN, "misaligned array");
     if (q3cu_status st = use_device(ctx)) return st;
-    return launched(q3::launch_softmax_rows(x, row_off, row_len, rows, static_cast<cudaStream_t>(stream), ctx->sms),
-                    "softmax launch");
+    return launch_softmax(ctx, x, row_off, row_len, rows, static_cast<cudaStream_t>(stream));
 }
 
 q3cu_status q3cu_quantize_q8(q3cu_ctx *ctx, const void *x, q3cu_dtype dtype, int64_t rows, int n, int8_t *q, float *s,
@@ -417,7 +464,7 @@ q3cu_status q3cu_execute_softmax(q3cu_ctx *ctx, float *x, int size) {
     TRY_CUDA(cudaMemcpyAsync(dx, x, size_t(size) * 4, cudaMemcpyHostToDevice, ctx->stream), "H2D");
     TRY_CUDA(cudaMemcpyAsync(doff, &off, 8, cudaMemcpyHostToDevice, ctx->stream), "H2D");
     TRY_CUDA(cudaMemcpyAsync(dlen, &len, 4, cudaMemcpyHostToDevice, ctx->stream), "H2D");
-    TRY_CUDA(q3::launch_softmax_rows(dx, doff, dlen, 1, ctx->stream, ctx->sms), "softmax");
+    if (q3cu_status st = launch_softmax(ctx, dx, doff, dlen, 1, ctx->stream)) return st;
     TRY_CUDA(cudaMemcpyAsync(x, dx, size_t(size) * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
     return finish(ctx);
 }

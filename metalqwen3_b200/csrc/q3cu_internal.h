@@ -37,7 +37,11 @@ cudaError_t launch_qk_norm_rope(void *q, void *k, q3cu_dtype dt, const int32_t *
 cudaError_t launch_swiglu(const void *hb, const void *hb2, q3cu_dtype dt, int64_t elems, void *out, int8_t *q,
                           float *s, cudaStream_t stream, int sms);
 
-cudaError_t launch_softmax_rows(float *x, const int64_t *off, const int32_t *len, int64_t rows,
-                                cudaStream_t stream, int sms);
+// `sched` is a pair of device counters, zero before the launch and zero
+// again after it (the last CTA resets them); no two launches that may run at
+// the same time share a pair.
+constexpr int SMX_SCHED_WORDS = 2;
+cudaError_t launch_softmax_rows(float *x, const int64_t *off, const int32_t *len, int64_t rows, uint32_t *sched,
+                                uint32_t *status, cudaStream_t stream, int sms);
 
 }  // namespace q3

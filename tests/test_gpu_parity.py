@@ -361,6 +361,76 @@ def test_softmax_decode_batch(q3, oracle):
     np.testing.assert_allclose(g, o, rtol=1e-4, atol=ATOL)
 
 
+def _ragged_case(rng, lens, scale=2.0):
+    lens = np.asarray(lens, np.int32)
+    gaps = rng.integers(0, 5, lens.size)
+    off = np.concatenate([[0], np.cumsum(np.maximum(lens, 0) + gaps)[:-1]]).astype(np.int64) + 3
+    total = int(off[-1] + max(int(lens[-1]), 0) + 2)
+    x = (scale * rng.standard_normal(total)).astype(np.float32)
+    return x, off, lens
+
+
+def _check_ragged(g, x, o, off, lens):
+    inrow = np.zeros(x.size, bool)
+    for a, n in zip(off, lens):
+        if n > 0:
+            inrow[a:a + n] = True
+    check_softmax(g[inrow], o[inrow], softmax_f64(x, off, np.maximum(lens, 0))[inrow], off, lens)
+    assert np.array_equal(bits(g[~inrow]), bits(x[~inrow]))
+
+
+def test_softmax_row_classes(q3, oracle):
+    """Every path of the kernel in one call: rows of one warp (<= 4096), rows
+    shared by the CTA and staged in shared memory (<= 57344 after the leading
+    scalars), rows longer than the ring (global memory), empty and negative
+    lengths; some rows hold scores far below their max (the exact-exp branch:
+    subnormal and zero exponentials) and one holds a NaN."""
+    rng = np.random.default_rng(7)
+    lens = [0, 3, 4096, 4097, -5, 57340, 57344, 57345, 57347, 60000, 131072, 1, 9000, 20000]
+    x, off, lens = _ragged_case(rng, lens)
+    for r, n in ((3, 4097), (9, 60000), (12, 9000), (1, 3)):     # far-below-max scores
+        idx = off[r] + rng.choice(n, min(n, 40), replace=False)
+        x[idx] = rng.uniform(-110.0, -82.0, idx.size).astype(np.float32)
+    x[off[13] + 777] = np.nan
+    t = dev(x)
+    q3.softmax_rows(t, dev(off), dev(lens))
+    assert q3.device_status() == 0
+    g, o = host(t), oracle.rows_softmax(x, off, np.maximum(lens, 0))
+    assert np.isnan(g[off[13]:off[13] + 20000]).all()
+    _check_ragged(g, x, o, off, lens)
+
+
+def test_softmax_many_rows_repeat_and_two_streams(q3, oracle):
+    """81920 rows (40 heads x 2048 tokens, lengths 1..512): the largest rows
+    per unit.  The same call is made twice on one stream, then on two streams
+    at once: the per-launch row counters must be back at zero each time."""
+    import torch
+    rng = np.random.default_rng(11)
+    pos = np.arange(2048) % 512
+    lens = np.repeat(pos + 1, 40).astype(np.int32)
+    x, off, lens = _ragged_case(rng, lens)
+    o = oracle.rows_softmax(x, off, lens, threads=8)
+    doff, dlen = dev(off), dev(lens)
+    for _ in range(2):
+        t = dev(x)
+        q3.softmax_rows(t, doff, dlen)
+        g = host(t)
+        for r in rng.choice(lens.size, 200, replace=False):            # binary64 bound on a row sample
+            a, n = off[r], lens[r]
+            check_softmax(g[a:a + n], o[a:a + n], softmax_f64(x[a:a + n], [0], [n]), [0], [n])
+        np.testing.assert_allclose(g, o, rtol=1e-4, atol=ATOL)         # every row; gaps untouched
+    s1, s2 = torch.cuda.Stream(), torch.cuda.Stream()
+    t1, t2 = dev(x), dev(x)
+    torch.cuda.synchronize()
+    q3.softmax_rows(t1, doff, dlen, stream=s1)
+    q3.softmax_rows(t2, doff, dlen, stream=s2)
+    torch.cuda.synchronize()
+    assert q3.device_status() == 0
+    g1, g2 = host(t1), host(t2)
+    assert np.array_equal(bits(g1), bits(g2))
+    np.testing.assert_allclose(g1, o, rtol=1e-4, atol=ATOL)
+
+
 # --------------------------------------------------------------------------- embedding
 @pytest.mark.parametrize("dim", [64, 1024, 4096, 4160])
 def test_embed_gather(q3, oracle, dim):
