@@ -211,7 +211,7 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
     __shared__ ExpTab s_tab;
     __shared__ __align__(8) uint64_t full[SMX_NSLOT], empty[SMX_NSLOT], red[2];
     __shared__ SmxDesc desc[SMX_NSLOT];
-    __shared__ uint64_t s_end[SMX_NSLOT];        // ring position just past each slot's bytes
+    __shared__ uint32_t s_end[SMX_NSLOT];        // ring position (16-byte units) just past each slot's bytes
     __shared__ float red_f[SMX_CW];
     __shared__ double red_d[SMX_CW];
     __shared__ int fail_sh;
@@ -231,103 +231,149 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
     __syncthreads();
 
     // ---- producer warp -----------------------------------------------------
+    // Ring positions count 16-byte units (float4): `alloc` (monotonic) is the
+    // end of the newest region, `head` its offset in the ring, `freed` the end
+    // of the newest reclaimed region; [freed, alloc) spans every live byte
+    // (plus the tail skipped when a region would cross the ring's end).
+    // Slots are reclaimed in sequence order.  A unit's rows are reserved
+    // together: an exclusive scan of their sizes places every row that fits
+    // (slot free, space free, not crossing the end) and those lanes issue at
+    // once; the rest wait for reclaims.
     if (warp == SMX_CW) {
+        constexpr uint32_t R16 = SMX_RING / 16u;
         const uint64_t units = (uint64_t(rows) + unit - 1) / unit;
-        uint32_t nxt = 0;
-        if (lane == 0) nxt = atomicAdd(&sched[0], 1u);
-        nxt = __shfl_sync(FULL, nxt, 0);
-        uint64_t alloc = 0, freed = 0;            // monotonic ring byte positions
-        uint32_t k = 0, oldest = 0;               // next sequence number; oldest not yet reclaimed
+        const uint32_t lt = (1u << lane) - 1u;       // lanes below this one
+        uint32_t alloc = 0, head = 0, freed = 0;
+        uint32_t k = 0, oldest = 0;                   // next sequence number; oldest not yet reclaimed
         bool ok = true;
-        // Reserves `bytes` (a multiple of 16) for sequence k; *at = ring byte offset.
-        // Regions are contiguous (one that would cross the end starts at 0) and
-        // reclaimed in sequence order, so [freed, alloc) holds every live byte.
-        auto reserve = [&](uint32_t bytes, uint32_t *at) -> bool {
-            uint64_t start = alloc;
-            const uint64_t o = start % SMX_RING;
-            if (o + bytes > SMX_RING) start += SMX_RING - o;
-            while (oldest + SMX_NSLOT <= k || start + bytes > freed + SMX_RING) {
-                if (oldest == k) { freed = start; break; }            // nothing live: the skipped tail is free
-                if (__any_sync(FULL, fail_sh != 0)) return false;
-                if (!__all_sync(FULL, mbar_wait(&empty[oldest % SMX_NSLOT], (oldest / SMX_NSLOT) & 1u,
-                                                lane == 0 ? status : nullptr)))
-                    return false;
+        auto reclaim_ready = [&]() {                  // every released slot, without waiting (warp-uniform)
+            while (oldest != k && __all_sync(FULL, mbar_test_wait(&empty[oldest % SMX_NSLOT], (oldest / SMX_NSLOT) & 1u))) {
                 freed = s_end[oldest % SMX_NSLOT];
                 ++oldest;
             }
-            alloc = start + bytes;
-            *at = uint32_t(start % SMX_RING);
-            s_end[k % SMX_NSLOT] = alloc;         // every lane stores the same value and later reads its own
+            if (oldest == k) freed = alloc;           // nothing live: a skipped tail is free too
+        };
+        auto reclaim_one = [&]() -> bool {            // the oldest slot, bounded wait
+            if (__any_sync(FULL, fail_sh != 0)) return false;
+            if (!__all_sync(FULL, mbar_wait(&empty[oldest % SMX_NSLOT], (oldest / SMX_NSLOT) & 1u,
+                                            lane == 0 ? status : nullptr)))
+                return false;
+            freed = s_end[oldest % SMX_NSLOT];
+            ++oldest;
             return true;
         };
         uint8_t *ring_b = reinterpret_cast<uint8_t *>(ring);
-        while (ok) {
-            const uint64_t b = nxt;
-            if (b >= units) break;
-            if (lane == 0) nxt = atomicAdd(&sched[0], 1u);      // the next unit, in flight meanwhile
+
+        uint32_t cur = 0;
+        if (lane == 0) cur = atomicAdd(&sched[0], 1u);
+        cur = __shfl_sync(FULL, cur, 0);
+        int len = 0;
+        int64_t off = 0;
+        auto load_unit = [&](uint32_t b) {
             const int64_t r = int64_t(b) * unit + lane;
-            const bool valid = lane < unit && r < rows;
-            const int len = valid ? __ldg(lens + r) : 0;
-            const int64_t off = valid ? __ldg(offs + r) : 0;
+            const bool valid = b < units && lane < unit && r < rows;
+            len = valid ? __ldg(lens + r) : 0;
+            off = valid ? __ldg(offs + r) : 0;
+        };
+        load_unit(cur);
+        while (ok && cur < units) {
+            uint32_t nxt = 0;
+            if (lane == 0) nxt = atomicAdd(&sched[0], 1u);      // the next unit, in flight meanwhile
             float *row = x + off;
             RowSplit sp{0, 0, 0};
             if (len > 0) sp = split_row(row, len);
-            const bool staged = len > 0 && (len <= SMX_WMAX || uint64_t(sp.nb) * 16u <= SMX_RING);
-            const uint32_t bytes = staged ? uint32_t(sp.nb) * 16u : 0u;
+            const bool staged = len > 0 && (len <= SMX_WMAX || uint32_t(sp.nb) <= R16);
+            const uint32_t b16 = staged ? uint32_t(sp.nb) : 0u;
             float sc[6];
 #pragma unroll
             for (int i = 0; i < 3; ++i) {
                 sc[i] = i < sp.a ? row[i] : 0.0f;
                 sc[3 + i] = i < sp.tl ? row[sp.a + 4 * int64_t(sp.nb) + i] : 0.0f;
             }
-            uint32_t live = __ballot_sync(FULL, len > 0);
-            while (live) {
-                const int j = __ffs(live) - 1;
-                live &= live - 1;
-                const uint32_t bj = __shfl_sync(FULL, bytes, j);
-                uint32_t at = 0;
-                if (!reserve(bj, &at)) { ok = false; break; }
-                if (lane == j) {
-                    const int s = int(k % SMX_NSLOT);
-                    SmxDesc &d = desc[s];
-                    d.off = off;
-                    d.len = len;
-                    d.sidx = staged ? int32_t(at / 16u) : -1;
-                    d.nb = sp.nb;
-                    d.a = int16_t(sp.a);
-                    d.tl = int16_t(sp.tl);
+            const int my_len = len;
+            const int64_t my_off = off;
+            cur = __shfl_sync(FULL, nxt, 0);
+            load_unit(cur);                           // the next unit's lengths and offsets, in flight meanwhile
+
+            uint32_t pend = __ballot_sync(FULL, my_len > 0);
+            while (pend) {
+                reclaim_ready();
+                const bool mine = (pend >> lane) & 1u;
+                // inclusive scan of the pending rows' sizes, in lane order
+                uint32_t incl = mine ? b16 : 0u;
 #pragma unroll
-                    for (int i = 0; i < 6; ++i) d.sc[i] = sc[i];
-                    if (bytes) {
-                        mbar_arrive_expect_tx(&full[s], bytes);
-                        bulk_g2s(ring_b + at, row + sp.a, bytes, &full[s]);
-                    } else {
-                        mbar_arrive(&full[s]);
-                    }
+                for (int o = 1; o < 32; o <<= 1) {
+                    const uint32_t v = __shfl_up_sync(FULL, incl, o);
+                    if (lane >= o) incl += v;
                 }
-                ++k;
-                __syncwarp();
+                const uint32_t rank = __popc(pend & lt);
+                const bool fits = k + rank < oldest + SMX_NSLOT && head + incl <= R16 && alloc + incl - freed <= R16;
+                const uint32_t bad = __ballot_sync(FULL, mine && !fits);
+                const uint32_t go = bad ? pend & ((1u << (__ffs(bad) - 1)) - 1u) : pend;
+                if (go) {
+                    if ((go >> lane) & 1u) {
+                        const uint32_t seq = k + rank, sl = seq % SMX_NSLOT;
+                        const uint32_t at = head + incl - b16;              // float4 index in the ring
+                        SmxDesc &d = desc[sl];
+                        d.off = my_off;
+                        d.len = my_len;
+                        d.sidx = staged ? int32_t(at) : -1;
+                        d.nb = sp.nb;
+                        d.a = int16_t(sp.a);
+                        d.tl = int16_t(sp.tl);
+#pragma unroll
+                        for (int i = 0; i < 6; ++i) d.sc[i] = sc[i];
+                        s_end[sl] = alloc + incl;
+                        if (b16) {
+                            mbar_arrive_expect_tx(&full[sl], b16 * 16u);
+                            bulk_g2s(ring_b + size_t(at) * 16u, row + sp.a, b16 * 16u, &full[sl]);
+                        } else {
+                            mbar_arrive(&full[sl]);
+                        }
+                    }
+                    const int last = 31 - __clz(go);
+                    const uint32_t used = __shfl_sync(FULL, incl, last);
+                    k += __popc(go);
+                    alloc += used;
+                    head += used;
+                    if (head == R16) head = 0;
+                    pend &= ~go;
+                    __syncwarp();
+                    continue;
+                }
+                // The first pending row does not fit.
+                const int f = __ffs(pend) - 1;
+                const uint32_t bf = __shfl_sync(FULL, b16, f);
+                if (head + bf > R16) {                // skip the ring's tail
+                    alloc += R16 - head;
+                    head = 0;
+                    continue;
+                }
+                if (oldest == k) {                    // cannot happen: the ring is empty and the row fits
+                    if (lane == 0) atomicOr(status, Q3CU_DEV_TIMEOUT);
+                    ok = false;
+                    break;
+                }
+                if (!reclaim_one()) { ok = false; break; }
             }
-            nxt = __shfl_sync(FULL, nxt, 0);
         }
-        if (ok) {                                  // end of the sequence
-            uint32_t at = 0;
-            if (reserve(0, &at)) {
+        if (ok) {                                     // end of the sequence
+            while (k >= oldest + SMX_NSLOT)
+                if (!reclaim_one()) { ok = false; break; }
+            if (ok) {
                 if (lane == 0) {
                     desc[k % SMX_NSLOT].len = -1;
                     mbar_arrive(&full[k % SMX_NSLOT]);
                 }
                 ++k;
-            } else {
-                ok = false;
             }
         }
         if (!ok) {
             // After a failure, no copy may still be landing when the CTA exits:
             // bounded wait for every slot not yet reclaimed.
             if (lane == 0)
-                for (uint32_t s = oldest; s < k; ++s)
-                    mbar_wait(&full[s % SMX_NSLOT], (s / SMX_NSLOT) & 1u, nullptr);
+                for (uint32_t q = oldest; q < k; ++q)
+                    mbar_wait(&full[q % SMX_NSLOT], (q / SMX_NSLOT) & 1u, nullptr);
         }
         // The last CTA to finish resets the counter pair for the next launch.
         if (lane == 0) {
@@ -353,16 +399,17 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
         const SmxDesc &d = desc[s];
         const int len = d.len;
         if (len < 0) break;
-        bool ok = true;
+        bool ok = true, wrote = true;
         if (len <= SMX_WMAX) {
-            if (int(wc % SMX_CW) == warp) smx_row<32, 4, true>(x, ring, d, lane, s_tab, nullptr, 0, nullptr, nullptr, status);
+            wrote = int(wc % SMX_CW) == warp;
+            if (wrote) smx_row<32, 4, true>(x, ring, d, lane, s_tab, nullptr, 0, nullptr, nullptr, status);
             ++wc;
         } else {
             ok = d.sidx >= 0 ? smx_row<SMX_CT, 2, true>(x, ring, d, tid, s_tab, red, cc & 1u, red_f, red_d, status)
                              : smx_row<SMX_CT, 1, false>(x, ring, d, tid, s_tab, red, cc & 1u, red_f, red_d, status);
             ++cc;
         }
-        fence_proxy_async_smem();
+        if (wrote) fence_proxy_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[s]);
         if (!ok) {
