@@ -7,9 +7,10 @@
 //     for i: x[i] /= sum;
 // The max is order-independent and exact.  Softmax owes the reference 1e-5
 // relative, not its bits, so each exponential of d = x - max in [-80, 0] is
-// exp_m80_0 (binary32 Cody-Waite reduction + ex2.approx, ~2^-22 relative); d
-// below -80 or NaN takes the libm-identical expf, so the reference's underflow
-// (a row entirely below -104 is 0/0 = NaN) is reproduced.  Each float4's four
+// exp_m80_0 (2^(d*log2 e) from ex2.approx with the product's rounding error
+// restored, ~2^-22 relative); a float4 with any d below -80 takes the
+// libm-identical expf, so subnormal results and the reference's underflow (a
+// row entirely below -104 is 0/0 = NaN) are reproduced.  Each float4's four
 // exponentials are added in binary32 and the partial sums accumulated in
 // binary64 (per thread, then a fixed tree): closer to the exact sum than the
 // reference's sequential binary32 sum, and deterministic.  The tests bound the
@@ -17,29 +18,33 @@
 // oracle than the oracle is from it).
 //
 // One launch for every row length.  A persistent CTA per SM streams whole rows
-// through a 224 KB shared-memory ring, so HBM sees each score read once and
+// through a 220 KB shared-memory ring, so HBM sees each score read once and
 // written once, with up to the whole ring in flight per SM:
 //
 //   producer warp   takes units of `unit` consecutive rows from a device
-//                   counter (dynamic balance across SMs), and for each row of
-//                   positive length reserves ring space in order, fills a slot
-//                   descriptor (offset, length, the up-to-six scalars outside
-//                   the row's 16-byte-aligned body) and bulk-copies the body
-//                   (cp.async.bulk, completing on the slot's mbarrier);
-//   15 consumer     walk the slots in order.  A row of <= SMX_WMAX scores
-//   warps           belongs to one warp (round-robin); a longer row is shared
-//                   by all 15, whose two reductions meet on mbarriers (bounded
-//                   waits, no unbounded bar.sync).  A row too long for the ring
-//                   is read from and written to global memory in three passes.
-//                   Max, then exp written back over the staged scores with the
-//                   sum, then the scaled scores stored straight to HBM.  Every
-//                   warp arrives once per slot on its `empty` barrier.
+//                   counter (dynamic balance across SMs) and cuts them into
+//                   batches: one long row (> SMX_WMAX scores), or a run of
+//                   short rows of at most 48 KB.  For each batch it reserves
+//                   ring space and row descriptors in order, fills the
+//                   descriptors (offset, length, ring position, the up-to-six
+//                   scalars outside the row's 16-byte-aligned body) and bulk-
+//                   copies the bodies (cp.async.bulk, completing on the batch's
+//                   mbarrier);
+//   15 consumer     walk the batches in order.  A short row belongs to one warp
+//   warps           (round-robin); a long row is shared by all 15, whose two
+//                   reductions meet on mbarriers (bounded waits, no unbounded
+//                   bar.sync).  A row too long for the ring is read from and
+//                   written to global memory in three passes.  Max, then exp
+//                   written back over the staged scores with the sum, then the
+//                   scaled scores stored straight to HBM.  Every warp arrives
+//                   once per batch on its `empty` barrier.
 //
-// The ring is reclaimed in order (the producer waits for the oldest slot's
-// release), so slot k's buffer is reused only after all 15 warps are done
-// with it; the parity waits stay exact because every consumer warp waits on
-// every slot in sequence.  The counter pair {next unit, finished CTAs} is reset
-// by the last CTA to finish, so it is zero for the next launch on that pair.
+// Batches are reclaimed in order (the producer waits for the oldest batch's
+// release), so a batch's ring bytes and descriptors are reused only after all
+// 15 warps are done with it; the parity waits stay exact because every
+// consumer warp waits on every batch in sequence.  The counter pair {next unit,
+// finished CTAs} is reset by the last CTA to finish, so it is zero for the next
+// launch on that pair.
 #include "q3cu_internal.h"
 
 namespace q3 {
@@ -47,8 +52,10 @@ namespace q3 {
 constexpr int SMX_CW = 15;                       // consumer warps (16 warps in all: 128 registers each)
 constexpr int SMX_CT = SMX_CW * 32;              // consumer threads
 constexpr int SMX_THREADS = SMX_CT + 32;         // + the producer warp
-constexpr int SMX_NSLOT = 32;                    // slots (rows staged or queued) per CTA
-constexpr uint32_t SMX_RING = 224u * 1024u;      // ring bytes: rows of up to 57344 scores are staged
+constexpr int SMX_NB = 16;                       // batch slots per CTA
+constexpr int SMX_NDESC = 128;                   // row descriptors per CTA
+constexpr uint32_t SMX_RING = 220u * 1024u;      // ring bytes: rows of up to 56320 scores are staged
+constexpr uint32_t SMX_BATCH16 = 3072;           // a batch of short rows holds at most 48 KB (in float4)
 constexpr int SMX_WMAX = 4096;                   // rows up to this length: one warp
 constexpr int SMX_UNIT_MAX = 32;                 // rows per unit taken from the counter (lanes of the producer)
 
@@ -70,7 +77,7 @@ __device__ __forceinline__ RowSplit split_row(const float *row, int len) {
 
 struct SmxDesc {
     int64_t off;      // first score of the row in x
-    int32_t len;      // < 0: end of the sequence
+    int32_t len;
     int32_t sidx;     // float4 index of the staged body in the ring; -1: not staged (global)
     int32_t nb;       // float4 body count
     int16_t a, tl;    // leading / trailing scalar counts (<= 3 each)
@@ -78,16 +85,25 @@ struct SmxDesc {
 };
 static_assert(sizeof(SmxDesc) == 48, "descriptor layout");
 
-// exp(v - m) of four scores: exp_m80_0 for d = v - m in [-80, 0] (every d once
-// the max is known, except far-below-max scores and NaN).  Returns false if any
-// d is outside that range, in which case the caller recomputes the four with
-// smx_exp4_exact (the libm-identical expf: subnormal results and NaN as the
-// reference has them), a branch that is cold in practice and kept out of the
-// hot loop's register allocation.
+// A batch: one long row (all consumer warps), or a run of short rows (one
+// warp each), or the end of the sequence.
+enum : uint16_t { SMX_SHORT = 0, SMX_LONG = 1, SMX_END = 2 };
+struct SmxBatch {
+    uint32_t d0;      // first descriptor (monotonic; slot d0 % SMX_NDESC)
+    uint16_t n;       // rows
+    uint16_t kind;
+};
+
+// exp(v - m) of four scores: exp_m80_0 when every d = v - m is in [-80, 0]
+// (RN(min v - m) is the smallest d; NaN scores are skipped by the min and come
+// out NaN).  Returns false otherwise (a score far below the max, or -inf), and
+// the caller recomputes the four with smx_exp4_exact (the libm-identical expf
+// below -80), a branch that is cold in practice and kept out of the hot loop's
+// register allocation.
 __device__ __forceinline__ bool smx_exp4(float4 &v, float m) {
-    const float d0 = __fsub_rn(v.x, m), d1 = __fsub_rn(v.y, m), d2 = __fsub_rn(v.z, m), d3 = __fsub_rn(v.w, m);
-    const bool ok = (d0 >= -80.0f) & (d1 >= -80.0f) & (d2 >= -80.0f) & (d3 >= -80.0f);
-    v = make_float4(exp_m80_0(d0), exp_m80_0(d1), exp_m80_0(d2), exp_m80_0(d3));
+    const bool ok = __fsub_rn(fminf(fminf(v.x, v.y), fminf(v.z, v.w)), m) >= -80.0f;
+    v = make_float4(exp_m80_0(__fsub_rn(v.x, m)), exp_m80_0(__fsub_rn(v.y, m)), exp_m80_0(__fsub_rn(v.z, m)),
+                    exp_m80_0(__fsub_rn(v.w, m)));
     return ok;
 }
 static __device__ __noinline__ float smx_exp_slow(float d, const ExpTab *tab) { return expf_host(d, *tab); }
@@ -104,8 +120,12 @@ __device__ __forceinline__ double sum4(float4 v) {
 __device__ __forceinline__ float max4(float m, float4 v) {
     return fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
 }
-__device__ __forceinline__ float4 scale4(float4 v, float inv) {
-    return make_float4(__fmul_rn(v.x, inv), __fmul_rn(v.y, inv), __fmul_rn(v.z, inv), __fmul_rn(v.w, inv));
+__device__ __forceinline__ float4 scale4(float4 v, float inv) {      // packed f32x2 products
+    const f2 s = pk2(inv, inv);
+    float4 r;
+    up2(mul2(pk2(v.x, v.y), s), r.x, r.y);
+    up2(mul2(pk2(v.z, v.w), s), r.z, r.w);
+    return r;
 }
 // Orders this thread's earlier generic-proxy shared-memory writes before the
 // bulk copies the producer issues into the same bytes after the release.
@@ -209,9 +229,10 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
                     int unit, uint32_t *sched, uint32_t *status) {
     extern __shared__ __align__(128) float4 ring[];
     __shared__ ExpTab s_tab;
-    __shared__ __align__(8) uint64_t full[SMX_NSLOT], empty[SMX_NSLOT], red[2];
-    __shared__ SmxDesc desc[SMX_NSLOT];
-    __shared__ uint32_t s_end[SMX_NSLOT];        // ring position (16-byte units) just past each slot's bytes
+    __shared__ __align__(8) uint64_t full[SMX_NB], empty[SMX_NB], red[2];
+    __shared__ SmxBatch hdr[SMX_NB];
+    __shared__ uint32_t s_end[SMX_NB], s_dend[SMX_NB];   // ring (float4) and descriptor ends of each batch
+    __shared__ SmxDesc desc[SMX_NDESC];
     __shared__ float red_f[SMX_CW];
     __shared__ double red_d[SMX_CW];
     __shared__ int fail_sh;
@@ -219,7 +240,7 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
 
     load_exp_table(s_tab);
     if (tid == 0) {
-        for (int i = 0; i < SMX_NSLOT; ++i) {
+        for (int i = 0; i < SMX_NB; ++i) {
             mbar_init(&full[i], 1);
             mbar_init(&empty[i], SMX_CW);
         }
@@ -232,34 +253,38 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
 
     // ---- producer warp -----------------------------------------------------
     // Ring positions count 16-byte units (float4): `alloc` (monotonic) is the
-    // end of the newest region, `head` its offset in the ring, `freed` the end
-    // of the newest reclaimed region; [freed, alloc) spans every live byte
-    // (plus the tail skipped when a region would cross the ring's end).
-    // Slots are reclaimed in sequence order.  A unit's rows are reserved
-    // together: an exclusive scan of their sizes places every row that fits
-    // (slot free, space free, not crossing the end) and those lanes issue at
-    // once; the rest wait for reclaims.
+    // end of the newest batch's bytes, `head` its offset in the ring, `freed`
+    // the end of the newest reclaimed batch; [freed, alloc) spans every live
+    // byte (plus a tail skipped when a batch would cross the ring's end).
+    // Descriptors likewise ([dfreed, dalloc)).  Batches are reclaimed in
+    // sequence order.  A batch is the first pending row of the unit if it is
+    // long, else the run of short rows that follows it: an exclusive scan of
+    // their sizes places every row that fits (slot, descriptor and ring space
+    // free, no crossing, at most SMX_BATCH16 after the first) and those lanes
+    // write their descriptors and issue their copies together.
     if (warp == SMX_CW) {
         constexpr uint32_t R16 = SMX_RING / 16u;
         const uint64_t units = (uint64_t(rows) + unit - 1) / unit;
         const uint32_t lt = (1u << lane) - 1u;       // lanes below this one
-        uint32_t alloc = 0, head = 0, freed = 0;
-        uint32_t k = 0, oldest = 0;                   // next sequence number; oldest not yet reclaimed
+        uint32_t alloc = 0, head = 0, freed = 0, dalloc = 0, dfreed = 0;
+        uint32_t k = 0, oldest = 0;                   // next batch; oldest not yet reclaimed
         bool ok = true;
-        auto reclaim_ready = [&]() {                  // every released slot, without waiting (warp-uniform)
-            while (oldest != k && __all_sync(FULL, mbar_test_wait(&empty[oldest % SMX_NSLOT], (oldest / SMX_NSLOT) & 1u))) {
-                freed = s_end[oldest % SMX_NSLOT];
-                ++oldest;
-            }
+        auto take = [&]() {
+            freed = s_end[oldest % SMX_NB];
+            dfreed = s_dend[oldest % SMX_NB];
+            ++oldest;
+        };
+        auto reclaim_ready = [&]() {                  // every released batch, without waiting (warp-uniform)
+            while (oldest != k && __all_sync(FULL, mbar_test_wait(&empty[oldest % SMX_NB], (oldest / SMX_NB) & 1u)))
+                take();
             if (oldest == k) freed = alloc;           // nothing live: a skipped tail is free too
         };
-        auto reclaim_one = [&]() -> bool {            // the oldest slot, bounded wait
+        auto reclaim_one = [&]() -> bool {            // the oldest batch, bounded wait
             if (__any_sync(FULL, fail_sh != 0)) return false;
-            if (!__all_sync(FULL, mbar_wait(&empty[oldest % SMX_NSLOT], (oldest / SMX_NSLOT) & 1u,
+            if (!__all_sync(FULL, mbar_wait(&empty[oldest % SMX_NB], (oldest / SMX_NB) & 1u,
                                             lane == 0 ? status : nullptr)))
                 return false;
-            freed = s_end[oldest % SMX_NSLOT];
-            ++oldest;
+            take();
             return true;
         };
         uint8_t *ring_b = reinterpret_cast<uint8_t *>(ring);
@@ -282,7 +307,8 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
             float *row = x + off;
             RowSplit sp{0, 0, 0};
             if (len > 0) sp = split_row(row, len);
-            const bool staged = len > 0 && (len <= SMX_WMAX || uint32_t(sp.nb) <= R16);
+            const bool is_long = len > SMX_WMAX;
+            const bool staged = len > 0 && (!is_long || uint32_t(sp.nb) <= R16);
             const uint32_t b16 = staged ? uint32_t(sp.nb) : 0u;
             float sc[6];
 #pragma unroll
@@ -296,25 +322,37 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
             load_unit(cur);                           // the next unit's lengths and offsets, in flight meanwhile
 
             uint32_t pend = __ballot_sync(FULL, my_len > 0);
+            const uint32_t longs = __ballot_sync(FULL, my_len > 0 && is_long);
             while (pend) {
                 reclaim_ready();
-                const bool mine = (pend >> lane) & 1u;
-                // inclusive scan of the pending rows' sizes, in lane order
-                uint32_t incl = mine ? b16 : 0u;
+                const int f = __ffs(pend) - 1;
+                uint32_t cand;
+                if ((longs >> f) & 1u) {
+                    cand = 1u << f;
+                } else {
+                    const uint32_t lb = longs & pend;             // long rows after f end the run
+                    cand = lb ? pend & ((1u << (__ffs(lb) - 1)) - 1u) : pend;
+                }
+                const bool in_c = (cand >> lane) & 1u;
+                uint32_t incl = in_c ? b16 : 0u;                  // inclusive scan, lane order
 #pragma unroll
                 for (int o = 1; o < 32; o <<= 1) {
                     const uint32_t v = __shfl_up_sync(FULL, incl, o);
                     if (lane >= o) incl += v;
                 }
-                const uint32_t rank = __popc(pend & lt);
-                const bool fits = k + rank < oldest + SMX_NSLOT && head + incl <= R16 && alloc + incl - freed <= R16;
-                const uint32_t bad = __ballot_sync(FULL, mine && !fits);
-                const uint32_t go = bad ? pend & ((1u << (__ffs(bad) - 1)) - 1u) : pend;
+                const uint32_t rank = __popc(cand & lt);
+                const bool fits = k < oldest + SMX_NB && head + incl <= R16 && alloc + incl - freed <= R16 &&
+                                  (rank == 0 || incl <= SMX_BATCH16) && dalloc + rank + 1 - dfreed <= SMX_NDESC;
+                const uint32_t bad = __ballot_sync(FULL, in_c && !fits);
+                const uint32_t go = bad ? cand & ((1u << (__ffs(bad) - 1)) - 1u) : cand;
                 if (go) {
-                    if ((go >> lane) & 1u) {
-                        const uint32_t seq = k + rank, sl = seq % SMX_NSLOT;
-                        const uint32_t at = head + incl - b16;              // float4 index in the ring
-                        SmxDesc &d = desc[sl];
+                    const int n = __popc(go);
+                    const uint32_t used = __shfl_sync(FULL, incl, 31 - __clz(go));
+                    const uint32_t sl = k % SMX_NB;
+                    const bool mine = (go >> lane) & 1u;
+                    const uint32_t at = head + incl - b16;        // float4 index in the ring
+                    if (mine) {
+                        SmxDesc &d = desc[(dalloc + rank) % SMX_NDESC];
                         d.off = my_off;
                         d.len = my_len;
                         d.sidx = staged ? int32_t(at) : -1;
@@ -323,33 +361,35 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
                         d.tl = int16_t(sp.tl);
 #pragma unroll
                         for (int i = 0; i < 6; ++i) d.sc[i] = sc[i];
-                        s_end[sl] = alloc + incl;
-                        if (b16) {
-                            mbar_arrive_expect_tx(&full[sl], b16 * 16u);
-                            bulk_g2s(ring_b + size_t(at) * 16u, row + sp.a, b16 * 16u, &full[sl]);
-                        } else {
-                            mbar_arrive(&full[sl]);
-                        }
                     }
-                    const int last = 31 - __clz(go);
-                    const uint32_t used = __shfl_sync(FULL, incl, last);
-                    k += __popc(go);
+                    if (lane == 0) {
+                        hdr[sl].d0 = dalloc;
+                        hdr[sl].n = uint16_t(n);
+                        hdr[sl].kind = ((longs >> f) & 1u) ? SMX_LONG : SMX_SHORT;
+                        s_end[sl] = alloc + used;
+                        s_dend[sl] = dalloc + uint32_t(n);
+                        if (used) mbar_expect_tx(&full[sl], used * 16u);
+                    }
+                    __syncwarp();
+                    if (mine && b16) bulk_g2s(ring_b + size_t(at) * 16u, row + sp.a, b16 * 16u, &full[sl]);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&full[sl]);        // descriptors and header published
+                    ++k;
                     alloc += used;
                     head += used;
                     if (head == R16) head = 0;
+                    dalloc += uint32_t(n);
                     pend &= ~go;
-                    __syncwarp();
                     continue;
                 }
-                // The first pending row does not fit.
-                const int f = __ffs(pend) - 1;
+                // The first row of the batch does not fit.
                 const uint32_t bf = __shfl_sync(FULL, b16, f);
                 if (head + bf > R16) {                // skip the ring's tail
                     alloc += R16 - head;
                     head = 0;
                     continue;
                 }
-                if (oldest == k) {                    // cannot happen: the ring is empty and the row fits
+                if (oldest == k) {                    // cannot happen: nothing is live and the row fits
                     if (lane == 0) atomicOr(status, Q3CU_DEV_TIMEOUT);
                     ok = false;
                     break;
@@ -358,22 +398,23 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
             }
         }
         if (ok) {                                     // end of the sequence
-            while (k >= oldest + SMX_NSLOT)
+            while (k >= oldest + SMX_NB)
                 if (!reclaim_one()) { ok = false; break; }
             if (ok) {
                 if (lane == 0) {
-                    desc[k % SMX_NSLOT].len = -1;
-                    mbar_arrive(&full[k % SMX_NSLOT]);
+                    hdr[k % SMX_NB].kind = SMX_END;
+                    hdr[k % SMX_NB].n = 0;
+                    mbar_arrive(&full[k % SMX_NB]);
                 }
                 ++k;
             }
         }
         if (!ok) {
             // After a failure, no copy may still be landing when the CTA exits:
-            // bounded wait for every slot not yet reclaimed.
+            // bounded wait for every batch not yet reclaimed.
             if (lane == 0)
                 for (uint32_t q = oldest; q < k; ++q)
-                    mbar_wait(&full[q % SMX_NSLOT], (q / SMX_NSLOT) & 1u, nullptr);
+                    mbar_wait(&full[q % SMX_NB], (q / SMX_NB) & 1u, nullptr);
         }
         // The last CTA to finish resets the counter pair for the next launch.
         if (lane == 0) {
@@ -388,26 +429,33 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
     }
 
     // ---- consumer warps ----------------------------------------------------
-    uint32_t wc = 0, cc = 0;                      // rows seen of one warp / of all warps
+    // Every warp waits on every batch in order and arrives once on its
+    // `empty` barrier.  Short rows: row i of a batch goes to warp
+    // (rot + i) % SMX_CW, rot counting the short rows of earlier batches.
+    uint32_t rot = 0, cc = 0;
     for (uint32_t k = 0;; ++k) {
-        const int s = int(k % SMX_NSLOT);
+        const int s = int(k % SMX_NB);
         if (__any_sync(FULL, fail_sh != 0)) break;
-        if (!__all_sync(FULL, mbar_wait(&full[s], (k / SMX_NSLOT) & 1u, lane == 0 ? status : nullptr))) {
+        if (!__all_sync(FULL, mbar_wait(&full[s], (k / SMX_NB) & 1u, lane == 0 ? status : nullptr))) {
             fail_sh = 1;
             break;
         }
-        const SmxDesc &d = desc[s];
-        const int len = d.len;
-        if (len < 0) break;
-        bool ok = true, wrote = true;
-        if (len <= SMX_WMAX) {
-            wrote = int(wc % SMX_CW) == warp;
-            if (wrote) smx_row<32, 4, true>(x, ring, d, lane, s_tab, nullptr, 0, nullptr, nullptr, status);
-            ++wc;
-        } else {
+        const SmxBatch h = hdr[s];
+        if (h.kind == SMX_END) break;
+        bool ok = true, wrote = false;
+        if (h.kind == SMX_LONG) {
+            const SmxDesc &d = desc[h.d0 % SMX_NDESC];
             ok = d.sidx >= 0 ? smx_row<SMX_CT, 2, true>(x, ring, d, tid, s_tab, red, cc & 1u, red_f, red_d, status)
                              : smx_row<SMX_CT, 1, false>(x, ring, d, tid, s_tab, red, cc & 1u, red_f, red_d, status);
             ++cc;
+            wrote = true;
+        } else {
+            for (int i = (warp + SMX_CW - int(rot % SMX_CW)) % SMX_CW; i < h.n; i += SMX_CW) {
+                smx_row<32, 4, true>(x, ring, desc[(h.d0 + i) % SMX_NDESC], lane, s_tab, nullptr, 0, nullptr, nullptr,
+                                     status);
+                wrote = true;
+            }
+            rot += h.n;
         }
         if (wrote) fence_proxy_async_smem();
         __syncwarp();

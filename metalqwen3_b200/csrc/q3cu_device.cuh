@@ -360,29 +360,28 @@ __device__ __forceinline__ float expf_host(float x, const ExpTab &t) { return q3
 __device__ __forceinline__ float expf_core(float x, const ExpTab &t) { return q3_expf_core(x, t.hi, t.lo); }
 
 // exp(d) for -80 <= d <= 0, where only accuracy is required (softmax: 1e-5
-// relative), in binary32 without the binary64 core.  Cody & Waite's argument
-// reduction (Software Manual for the Elementary Functions, 1980): k = rint(d/ln2)
-// and r = d - k*ln2 with ln2 split as 355/512 (so k*C1 is exact for |k| < 2^15)
-// plus RN(ln2 - 355/512), |r| <= ln2/2; then 2^(r/ln2) from ex2.approx (an
-// argument in [-0.5, 0.5], result in [0.7, 1.42]) and the factor 2^k added to the
-// exponent field (d >= -80 keeps the result a normal number).  Relative error
-// about 2^-22 over the whole range (tests/test_device_math.py sweeps every
-// binary32 d in [-80, 0] against the libm-identical expf).
+// relative), in binary32 without the binary64 core: exp(d) = 2^t, t = d*log2(e).
+// t is carried as th + tl: th = RN(d*L) with L = RN(log2 e), and tl = the
+// product's rounding error, exact by fused multiply-add (the TwoProduct of
+// Ogita, Rump & Oishi, "Accurate sum and dot product", 2005), plus d*(log2 e - L).
+// Then 2^th from ex2.approx (th in [-115.5, 0]: a normal result) and the factor
+// 2^tl = 1 + tl*ln2 to first order (|tl| < 6e-6, so the dropped term is below
+// 2^-36).  Relative error about 2^-22 over the whole range
+// (tests/test_device_math.py sweeps every binary32 d in [-80, 0] against the
+// binary64 exp).  NaN gives NaN; d = -inf does not belong here (tl is NaN).
 __device__ __forceinline__ float ex2_approx_ftz(float x) {
     float r;
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
 __device__ __forceinline__ float exp_m80_0(float d) {
-    constexpr float LOG2E = 1.44269504088896341f;       // RN(1/ln2)
-    constexpr float C1 = 0.693359375f;                   // 355/512
-    constexpr float C2 = -2.12194440054690583e-4f;       // RN(ln2 - 355/512)
-    const float tm = __fadd_rn(__fmul_rn(d, LOG2E), 12582912.0f);   // k + 1.5*2^23 (round to nearest)
-    const float k = __fsub_rn(tm, 12582912.0f);
-    const float r = __fmaf_rn(-k, C2, __fmaf_rn(-k, C1, d));
-    const float e = ex2_approx_ftz(__fmul_rn(r, LOG2E));
-    const uint32_t scale = uint32_t(__float_as_int(tm) - 0x4B400000) << 23;   // k in the exponent field
-    return __uint_as_float(__float_as_uint(e) + scale);
+    constexpr float L = 1.44269502162933349609375f;      // RN(log2 e)
+    constexpr float L_LO = 1.925963033500011079e-8f;     // RN(log2 e - L)
+    constexpr float LN2 = 0.693147182464599609375f;      // RN(ln 2)
+    const float th = __fmul_rn(d, L);
+    const float tl = __fmaf_rn(d, L_LO, __fmaf_rn(d, L, -th));
+    const float e = ex2_approx_ftz(th);
+    return __fmaf_rn(__fmul_rn(e, LN2), tl, e);
 }
 
 // ---------------------------------------------------------------------------
@@ -400,6 +399,10 @@ __device__ __forceinline__ void mbar_init_fence() {
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;"
                  :: "r"(smem_addr(bar)), "r"(bytes) : "memory");
+}
+// Raises the barrier's expected transaction bytes without arriving.
+__device__ __forceinline__ void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" :: "r"(smem_addr(bar)), "r"(bytes) : "memory");
 }
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_addr(bar)) : "memory");
