@@ -470,11 +470,12 @@ def measured_hbm_peak():
         return 6650.0, "fallback"
 
 
-def profiled_traffic(workload, kernel, units=None):
+def profiled_traffic(workload, kernel, alg_bytes=None):
     """Per-launch DRAM bytes of `kernel` from the committed ncu summary, or None.
 
-    A capture taken on a smaller batch (its entry names the units it processed)
-    is scaled to `units` in proportion."""
+    A capture taken on a smaller case of the same kernel is scaled to this
+    launch by the ratio of algorithmic bytes (the kernel's traffic grows in
+    proportion: every input read once, every output written once)."""
     p = os.path.join(ROOT, "profiles", "traffic.json")
     try:
         with open(p) as f:
@@ -482,8 +483,8 @@ def profiled_traffic(workload, kernel, units=None):
     except Exception:
         return None
     b = e["dram_bytes_per_launch"]
-    if "units" in e and units is not None and units != e["units"]:
-        b = round(b * units / e["units"])
+    if alg_bytes is not None and e.get("algorithmic_bytes") and alg_bytes != e["algorithmic_bytes"]:
+        b = round(b * alg_bytes / e["algorithmic_bytes"])
     return b
 
 
@@ -733,7 +734,7 @@ def main():
             "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": peak,
                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
                          else "fallback 6650 GB/s", "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": profiled_traffic(wl.name, dom_name, wl.tokens),
+                         "traffic": profiled_traffic(wl.name, dom_name, dom_bytes),
                          "algorithmic_bytes_per_launch": dom_bytes},
             "e2e": {"value": round(world * e2e_bytes * args.e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
