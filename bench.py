@@ -552,6 +552,64 @@ def run_reference(args, wl):
     return 0
 
 
+# The CPU implementation's row functions, by the kernel they stand for.
+CPU_KERNEL = {"rows_rmsnorm_q8": "rmsnorm_q8", "rows_qk_norm_rope": "qk_norm_rope", "rows_swiglu_q8": "swiglu_q8",
+              "rows_softmax": "softmax_rows", "rows_embed": "embed_gather"}
+
+
+class _TimedImpl:
+    """Wraps the CPU implementation and adds up the wall time of each row function."""
+
+    def __init__(self, impl):
+        self._impl, self.seconds = impl, {}
+
+    def __getattr__(self, name):
+        f = getattr(self._impl, name)
+        if name not in CPU_KERNEL:
+            return f
+
+        def timed(*a, **kw):
+            t0 = time.perf_counter()
+            r = f(*a, **kw)
+            k = CPU_KERNEL[name]
+            self.seconds[k] = self.seconds.get(k, 0.0) + time.perf_counter() - t0
+            return r
+        return timed
+
+
+def cpu_kernels(args, wl):
+    """Per-kernel GB/s of the reference's CPU code on this host, on one core and
+    on all cores (OpenMP over rows), on a token sample of the workload; one JSON
+    line."""
+    import numpy as np
+    impl, kind = cpu_impl()
+    cores = os.cpu_count() or 1
+    sample = 128
+    if hasattr(wl, "kernel_bytes"):
+        kb = dict(wl.kernel_bytes(wl.sample_pos(sample)))
+    else:
+        kb = {n: b * sample / wl.tokens for n, b in wl.kernels()}
+    out, passes = {}, {}
+    for threads in (1, cores):
+        timed = _TimedImpl(impl)
+        rng = np.random.default_rng(0)
+        wl.cpu_step(impl, np, sample, threads, rng)              # builds the sample; warm-up
+        t0, n = time.perf_counter(), 0
+        while True:
+            wl.cpu_step(timed, np, sample, threads, rng)
+            n += 1
+            if time.perf_counter() - t0 >= args.cpu_seconds:
+                break
+        passes[str(threads)] = n
+        for k, sec in timed.seconds.items():
+            out.setdefault(k, {})[str(threads)] = round(kb[k] * n / sec / 1e9, 3)
+    print(json.dumps({"cpu_kernels": out, "unit": "GB/s (algorithmic bytes of the workload's kernels)",
+                      "workload": wl.name, "threads": [1, cores], "kind": kind,
+                      "sample": f"{sample} tokens per pass; passes per thread count {passes}", "note": CPU_NOTE[kind]}),
+          flush=True)
+    return 0
+
+
 CPU_NOTE = {
     "reference": "src/cpu/qwen3_original.c compiled unmodified (rmsnorm, softmax, quantize, dequantize); its "
                  "inline RoPE and SwiGLU loops restated in oracle/ref_rows.c",
@@ -574,12 +632,16 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-kernels", action="store_true",
+                    help="time each kernel of the workload on the reference's CPU code (1 core and all cores) and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     wl = WORKLOADS[args.workload](tokens=args.tokens) if args.tokens else WORKLOADS[args.workload]()
 
     if args.impl == "reference":
         return run_reference(args, wl)
+    if args.cpu_kernels:
+        return cpu_kernels(args, wl)
 
     import torch
     import torch.distributed as dist
