@@ -168,22 +168,33 @@ __global__ void __launch_bounds__(RMS_THREADS, 1) rmsnorm_kernel(const T *x, con
     // rises now and falls when they land), and after a CTA barrier thread 0
     // makes the item's one arrival.
     const int first_items = total < RMS_NS ? total : RMS_NS;
-    for (int it = 0; it < first_items; ++it) {
+    auto copy_item = [&](int it, int t0, int nthr) {
         const int kb = it / per_block, j = it % per_block, c = j < nch ? j : j - nch, st = it % RMS_NS;
         int64_t r0; int rv;
         block_rows(kb, r0, rv);
         const int vpr = chunk_bytes(c) / 16;            // 16-byte vectors per row
         const uint8_t *src = reinterpret_cast<const uint8_t *>(x) + r0 * row_bytes + int64_t(c) * RMS_CB;
         uint8_t *dst = stage + size_t(st) * RMS_MAXR * RMS_ROWB;
-        for (int f = tid; f < rv * vpr; f += RMS_THREADS) {
+        for (int f = t0; f < rv * vpr; f += nthr) {
             const int r = f / vpr, v = f - (f / vpr) * vpr;
             cp_async16(dst + r * RMS_ROWB + v * 16, src + r * row_bytes + v * 16);
         }
         cp_async_track(&bar[st]);
-    }
+    };
+    // Item 0 by every thread, published as soon as every piece is attached.
+    // Items 1.. by the compute warps other than the chain warp (an SM keeps
+    // only ~50 KB of cp.async in flight, so issuing them stalls their issuers
+    // until earlier pieces land; the chain warp starts on item 0 meanwhile).
+    copy_item(0, tid, RMS_THREADS);
     __syncthreads();
-    if (tid == 0)
-        for (int it = 0; it < first_items; ++it) mbar_arrive(&bar[it]);
+    if (tid == 0) mbar_arrive(&bar[0]);
+    if (first_items > 1 && warp < RMS_CWARPS && warp != RMS_CHAIN) {
+        const int ft = tid - (warp > RMS_CHAIN ? 32 : 0);        // 0 .. RMS_CTHREADS - 33
+        for (int it = 1; it < first_items; ++it) copy_item(it, ft, RMS_CTHREADS - 32);
+        named_sync(2, RMS_CTHREADS - 32);
+        if (ft == 0)
+            for (int it = 1; it < first_items; ++it) mbar_arrive(&bar[it]);
+    }
     // Later items: the producer warp, one bulk copy per row (lane r copies row
     // r's piece); the expect-tx arrival is the item's one arrival.  Bulk copies
     // do not count against the SM's cap on outstanding cp.async bytes (~50 KB),
