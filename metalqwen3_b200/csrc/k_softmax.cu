@@ -11,9 +11,10 @@
 // restored, ~2^-22 relative); a float4 with any d below -80 takes the
 // libm-identical expf, so subnormal results and the reference's underflow (a
 // row entirely below -104 is 0/0 = NaN) are reproduced.  Each float4's four
-// exponentials are added in binary32 and the partial sums accumulated in
-// binary64 (per thread, then a fixed tree): closer to the exact sum than the
-// reference's sequential binary32 sum, and deterministic.  The tests bound the
+// exponentials are added in binary32 (at most 4*U of them per thread and
+// step) and the partial sums accumulated in binary64 (per thread, then a
+// fixed tree): closer to the exact sum than the reference's sequential
+// binary32 sum, and deterministic.  The tests bound the
 // outputs (1e-5 rel / 1e-6 abs of a binary64 softmax, and no further from the
 // oracle than the oracle is from it).
 //
@@ -102,8 +103,9 @@ struct SmxBatch {
 // register allocation.
 __device__ __forceinline__ bool smx_exp4(float4 &v, float m) {
     const bool ok = __fsub_rn(fminf(fminf(v.x, v.y), fminf(v.z, v.w)), m) >= -80.0f;
-    v = make_float4(exp_m80_0(__fsub_rn(v.x, m)), exp_m80_0(__fsub_rn(v.y, m)), exp_m80_0(__fsub_rn(v.z, m)),
-                    exp_m80_0(__fsub_rn(v.w, m)));
+    const f2 mm = pk2(m, m);
+    up2(exp2_m80_0(sub2(pk2(v.x, v.y), mm)), v.x, v.y);
+    up2(exp2_m80_0(sub2(pk2(v.z, v.w), mm)), v.z, v.w);
     return ok;
 }
 static __device__ __noinline__ float smx_exp_slow(float d, const ExpTab *tab) { return expf_host(d, *tab); }
@@ -114,9 +116,7 @@ __device__ __forceinline__ float4 smx_exp4_exact(float4 v, float m, const ExpTab
     return make_float4(smx_exp1(__fsub_rn(v.x, m), tab), smx_exp1(__fsub_rn(v.y, m), tab),
                        smx_exp1(__fsub_rn(v.z, m), tab), smx_exp1(__fsub_rn(v.w, m), tab));
 }
-__device__ __forceinline__ double sum4(float4 v) {
-    return double(__fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w)));
-}
+
 __device__ __forceinline__ float max4(float m, float4 v) {
     return fmaxf(m, fmaxf(fmaxf(v.x, v.y), fmaxf(v.z, v.w)));
 }
@@ -192,15 +192,19 @@ __device__ __forceinline__ bool smx_row(float *x, float4 *ring, const SmxDesc &d
 #pragma unroll
             for (int u = 0; u < U; ++u) e[u] = smx_exp4_exact(v[u], m, tab);
         }
+        f2 part = pk2(0.0f, 0.0f);                    // this step's exponentials, binary32 pairs
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int j = j0 + u * NT;
             if (j < nb) {
                 if constexpr (STAGED) sb[j] = e[u];
                 else *reinterpret_cast<uint4 *>(gb + j) = f4_as_u4(e[u]);
-                s += sum4(e[u]);
+                part = add2(part, add2(pk2(e[u].x, e[u].y), pk2(e[u].z, e[u].w)));
             }
         }
+        float p0, p1;
+        up2(part, p0, p1);
+        s += double(__fadd_rn(p0, p1));
     }
     if (si >= 0) { xs = smx_exp1(__fsub_rn(xs, m), tab); s += double(xs); }
     s = warp_sum_d(s);

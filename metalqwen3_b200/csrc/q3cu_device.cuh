@@ -374,14 +374,25 @@ __device__ __forceinline__ float ex2_approx_ftz(float x) {
     asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
+constexpr float EXP_L = 1.44269502162933349609375f;      // RN(log2 e)
+constexpr float EXP_L_LO = 1.925963033500011079e-8f;     // RN(log2 e - EXP_L)
+constexpr float EXP_LN2 = 0.693147182464599609375f;      // RN(ln 2)
 __device__ __forceinline__ float exp_m80_0(float d) {
-    constexpr float L = 1.44269502162933349609375f;      // RN(log2 e)
-    constexpr float L_LO = 1.925963033500011079e-8f;     // RN(log2 e - L)
-    constexpr float LN2 = 0.693147182464599609375f;      // RN(ln 2)
-    const float th = __fmul_rn(d, L);
-    const float tl = __fmaf_rn(d, L_LO, __fmaf_rn(d, L, -th));
+    const float th = __fmul_rn(d, EXP_L);
+    const float tl = __fmaf_rn(d, EXP_L_LO, __fmaf_rn(d, EXP_L, -th));
     const float e = ex2_approx_ftz(th);
-    return __fmaf_rn(__fmul_rn(e, LN2), tl, e);
+    return __fmaf_rn(__fmul_rn(e, EXP_LN2), tl, e);
+}
+// exp_m80_0 of an element pair in packed f32x2 arithmetic, the same roundings in
+// the same order (bit-identical: -th = RN(d*(-L)) is the exact negation of
+// RN(d*L), round-to-nearest being symmetric).
+__device__ __forceinline__ f2 exp2_m80_0(f2 d) {
+    const f2 nth = mul2(d, pk2(-EXP_L, -EXP_L));
+    const f2 tl = fma2(d, pk2(EXP_L_LO, EXP_L_LO), fma2(d, pk2(EXP_L, EXP_L), nth));
+    float n0, n1;
+    up2(nth, n0, n1);
+    const f2 e = pk2(ex2_approx_ftz(-n0), ex2_approx_ftz(-n1));
+    return fma2(mul2(e, pk2(EXP_LN2, EXP_LN2)), tl, e);
 }
 
 // ---------------------------------------------------------------------------

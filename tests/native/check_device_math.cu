@@ -1,6 +1,6 @@
 // Exhaustive / sweeping checks of the fast device arithmetic in
 // metalqwen3_b200/csrc/q3cu_device.cuh against the exact forms it replaces.
-// Built and run by tests/test_device_math.py; prints three mismatch counts.
+// Built and run by tests/test_device_math.py; prints the counts and the bound.
 #include <cstdio>
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -47,6 +47,21 @@ __global__ void check_exp80(unsigned long long *worst) {
     atomicMax(worst, w);
 }
 
+// (1d) the packed pair form exp2_m80_0 returns exp_m80_0's bits, on every
+//      binary32 d in [-80, 0] (each d paired with its neighbour)
+__global__ void check_exp80_pair(unsigned long long *bad) {
+    unsigned long long n = 0;
+    const uint32_t lo = 0x80000000u, hi = 0xc2a00000u;
+    for (uint64_t u = lo + uint64_t(blockIdx.x) * blockDim.x + threadIdx.x; u <= hi;
+         u += uint64_t(gridDim.x) * blockDim.x) {
+        const float d0 = __uint_as_float(uint32_t(u)), d1 = __uint_as_float(uint32_t(u == hi ? u : u + 1));
+        float r0, r1;
+        up2(exp2_m80_0(pk2(d0, d1)), r0, r1);
+        if (__float_as_uint(r0) != __float_as_uint(exp_m80_0(d0)) || __float_as_uint(r1) != __float_as_uint(exp_m80_0(d1))) ++n;
+    }
+    if (n) atomicAdd(bad, n);
+}
+
 // (2) scale and codes of the fast path == the exact path
 //     q8_scale (IEEE m/127) and q8_code (IEEE division + round half away)
 __device__ __forceinline__ uint32_t hash32(uint32_t x) {
@@ -87,16 +102,17 @@ __global__ void check_q8(uint32_t nm, unsigned long long *bad_scale, unsigned lo
 
 int main() {
     unsigned long long *d;
-    cudaMalloc(&d, 5 * sizeof(unsigned long long));
-    cudaMemset(d, 0, 5 * sizeof(unsigned long long));
+    cudaMalloc(&d, 6 * sizeof(unsigned long long));
+    cudaMemset(d, 0, 6 * sizeof(unsigned long long));
     check_rcp<<<148 * 16, 256>>>(0x3f800000u, 0x7f800001u, d);           // [1, +inf]
     check_q8<<<148 * 8, 128>>>(1u << 20, d + 1, d + 2);
     check_rcp1<<<148 * 16, 256>>>(0x3f800000u, 0x7b800000u, d + 3);     // [1, 2^120)
     check_exp80<<<148 * 16, 256>>>(d + 4);                                 // [-80, 0]
+    check_exp80_pair<<<148 * 16, 256>>>(d + 5);
     cudaError_t e = cudaDeviceSynchronize();
-    unsigned long long h[5] = {~0ull, ~0ull, ~0ull, ~0ull, ~0ull};
+    unsigned long long h[6] = {~0ull, ~0ull, ~0ull, ~0ull, ~0ull, ~0ull};
     cudaMemcpy(h, d, sizeof(h), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) { printf("cuda error %s\n", cudaGetErrorString(e)); return 1; }
-    printf("%llu %llu %llu %llu %llu\n", h[0], h[1], h[2], h[3], h[4]);
+    printf("%llu %llu %llu %llu %llu %llu\n", h[0], h[1], h[2], h[3], h[4], h[5]);
     return 0;
 }

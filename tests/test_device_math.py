@@ -5,7 +5,8 @@
 * on the GPU (tests/native/check_device_math.cu, built with nvcc):
   the Markstein reciprocal == __frcp_rn for every binary32 d >= 1 (two
   steps) and every d in [1, 2^120) (one step); softmax's binary32 exp within
-  1e-6 relative of exp on every binary32 d in [-80, 0]; and the
+  1e-6 relative of exp on every binary32 d in [-80, 0], and its packed pair
+  form bit-identical to it on the same range; and the
   multiply-by-reciprocal code path == the IEEE-division path on 2^20 random
   scales x values placed on and around every rounding tie.
 """
@@ -61,7 +62,8 @@ def test_fast_device_math_on_gpu():
                         "-I", CSRC, "-I", os.path.join(ROOT, "include"),
                         os.path.join(ROOT, "tests", "native", "check_device_math.cu"), "-o", exe], check=True)
         out = subprocess.run([exe], check=True, capture_output=True, text=True, timeout=300).stdout.split()
-    bad_rcp, bad_scale, bad_code, bad_rcp1, exp80_e12 = map(int, out[:5])
+    bad_rcp, bad_scale, bad_code, bad_rcp1, exp80_e12, bad_pair = map(int, out[:6])
+    assert bad_pair == 0, f"{bad_pair} d in [-80, 0] where the packed exp differs from the scalar one"
     assert exp80_e12 < 1_000_000, f"softmax exp: relative error {exp80_e12 * 1e-12:.3g} on [-80, 0] (bound 1e-6)"
     assert bad_rcp == 0, f"{bad_rcp} binary32 d >= 1 where the Markstein reciprocal != __frcp_rn"
     assert bad_rcp1 == 0, f"{bad_rcp1} binary32 d in [1, 2^120) where the one-step reciprocal != __frcp_rn"
