@@ -11,11 +11,14 @@
 // q [T][n_heads][128] and k [T][n_kv][128] are flat lists of 128-element head
 // rows.  A warp owns a tile of 32 consecutive head rows of one tensor, one row
 // per lane:
-//   * the warp copies the tile (one contiguous 16 KB / 8 KB range) into 32
-//     padded shared-memory row slots with 16-byte cp.async copies, 512 bytes per
-//     instruction; two buffers per warp, so the next tile streams in while this
-//     one is processed.  (A bulk copy per 512-byte row costs ~30 ns of
-//     copy-engine time per row per SM, more than the HBM time of the row.)
+//   * a copy warp per CTA copies every compute warp's tiles (one contiguous
+//     16 KB / 8 KB range each) into 32 padded shared-memory row slots with
+//     16-byte cp.async copies, 512 bytes per instruction; two buffers per
+//     compute warp with full/empty mbarriers (bounded waits), so the next tile
+//     streams in while this one is processed and the issue stalls of cp.async
+//     (an SM keeps only ~50 KB in flight) fall on the copy warp.  (A bulk copy
+//     per 512-byte row costs ~30 ns of copy-engine time per row per SM, more
+//     than the HBM time of the row.)
 //   * lane i runs row i's sum of squares in index order (the reference's
 //     rounding sequence, so the normalised values are bit-exact);
 //   * the warp fills a table with cos/sin of every token the tile touches
@@ -78,9 +81,9 @@ __device__ __forceinline__ void rotate_row(uint8_t *row, const float *w, const f
 }
 
 template <typename T>
-__global__ void __launch_bounds__(rope_warps<T>() * 32, 1) qk_norm_rope_kernel(
+__global__ void __launch_bounds__((rope_warps<T>() + 1) * 32, 1) qk_norm_rope_kernel(
     T *q, T *k, const int32_t *__restrict__ pos, int64_t q_rows, int64_t k_rows, int n_heads, int n_kv,
-    const float *__restrict__ q_norm, const float *__restrict__ k_norm, InvFreq invf, float eps) {
+    const float *__restrict__ q_norm, const float *__restrict__ k_norm, InvFreq invf, float eps, uint32_t *status) {
     constexpr int ESZ = sizeof(T);
     constexpr int RW = rope_warps<T>();
     constexpr int ROWBYTES = HD * ESZ;
@@ -89,20 +92,29 @@ __global__ void __launch_bounds__(rope_warps<T>() * 32, 1) qk_norm_rope_kernel(
     constexpr int V = Vec<T>::N;
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(16) float wsh[2][HD];          // q_norm, k_norm
+    __shared__ __align__(8) uint64_t full[RW][2];       // a compute warp's buffer holds its next tile
+    __shared__ __align__(8) uint64_t empty[RW][2];      // ... and was written back
+    __shared__ int fail_sh;
 
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    uint8_t *buf0 = smem + size_t(wid) * rope_warp_bytes<T>();
-    uint8_t *tab = buf0 + 2 * ROPE_TILE * ROWB;
     for (int i = threadIdx.x; i < HD; i += blockDim.x) {
         wsh[0][i] = q_norm[i];
         wsh[1][i] = k_norm[i];
+    }
+    if (threadIdx.x == 0) {
+        for (int w = 0; w < RW; ++w)
+            for (int b = 0; b < 2; ++b) {
+                mbar_init(&full[w][b], 1);
+                mbar_init(&empty[w][b], 1);
+            }
+        fail_sh = 0;
+        mbar_init_fence();
     }
     __syncthreads();
 
     const int64_t q_tiles = (q_rows + ROPE_TILE - 1) / ROPE_TILE;
     const int64_t k_tiles = (k_rows + ROPE_TILE - 1) / ROPE_TILE;
     const int64_t ntiles = q_tiles + k_tiles;
-    const int64_t gw = int64_t(blockIdx.x) * RW + wid;
     const int64_t GW = int64_t(gridDim.x) * RW;
 
     // per-lane frequencies for j = 2*lane, 2*lane+1
@@ -116,27 +128,52 @@ __global__ void __launch_bounds__(rope_warps<T>() * 32, 1) qk_norm_rope_kernel(
         nvalid = left < ROPE_TILE ? int(left) : ROPE_TILE;
         heads = isq ? n_heads : n_kv;
     };
-    // Copies tile t into buffer b and commits them as one group (an empty group
-    // when t is past the end, so every lane's group count stays in step).
-    auto load_tile = [&](int64_t t, int b) {
-        if (t < ntiles) {
-            T *base; int64_t row0; int nvalid, heads;
-            tile_info(t, base, row0, nvalid, heads);
-            const uint8_t *src = reinterpret_cast<const uint8_t *>(base + row0 * HD);
-            uint8_t *dst = buf0 + size_t(b) * ROPE_TILE * ROWB;
-            for (int c = lane; c < nvalid * CPR; c += 32)
-                cp_async16(dst + (c / CPR) * ROWB + (c % CPR) * 16, src + size_t(c) * 16);
+    // Compute warp w's tiles are t = blockIdx.x * RW + w + kk * GW, kk = 0, 1, ...,
+    // in buffer kk & 1.  The copy warp (wid == RW) copies them all, in kk order,
+    // with 16-byte cp.async pieces: an SM keeps only ~50 KB of cp.async in
+    // flight and issuing beyond that stalls the issuing warp, so the stalls
+    // fall on a warp with nothing else to do.  Each piece is attached to the
+    // buffer's `full` barrier (balanced arrival) and one plain arrival follows;
+    // the compute warp releases the buffer on `empty` after its write-back.
+    if (wid == RW) {
+        for (int64_t kk = 0;; ++kk) {
+            bool any = false, ok = true;
+            for (int w = 0; w < RW && ok; ++w) {
+                const int64_t t = int64_t(blockIdx.x) * RW + w + kk * GW;
+                if (t >= ntiles) continue;
+                any = true;
+                const int b = int(kk & 1);
+                if (kk >= 2 && !__all_sync(FULL, mbar_wait(&empty[w][b], uint32_t(((kk >> 1) - 1) & 1),
+                                                           lane == 0 ? status : nullptr))) {
+                    ok = false;
+                    break;
+                }
+                T *base; int64_t row0; int nvalid, heads;
+                tile_info(t, base, row0, nvalid, heads);
+                const uint8_t *src = reinterpret_cast<const uint8_t *>(base + row0 * HD);
+                uint8_t *dst = smem + size_t(w) * rope_warp_bytes<T>() + size_t(b) * ROPE_TILE * ROWB;
+                for (int c = lane; c < nvalid * CPR; c += 32)
+                    cp_async16(dst + (c / CPR) * ROWB + (c % CPR) * 16, src + size_t(c) * 16);
+                cp_async_track(&full[w][b]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&full[w][b]);
+            }
+            if (!any || !ok || __any_sync(FULL, fail_sh != 0)) break;
         }
-        cp_async_commit();
-    };
+        cp_async_wait<0>();    // no copy may still be landing when the CTA exits
+        return;
+    }
 
-    load_tile(gw, 0);
-    int64_t kk = 0;
-    for (int64_t t = gw; t < ntiles; t += GW, ++kk) {
+    uint8_t *buf0 = smem + size_t(wid) * rope_warp_bytes<T>();
+    uint8_t *tab = buf0 + 2 * ROPE_TILE * ROWB;
+    for (int64_t kk = 0;; ++kk) {
+        const int64_t t = int64_t(blockIdx.x) * RW + wid + kk * GW;
+        if (t >= ntiles) break;
         const int b = int(kk & 1);
-        load_tile(t + GW, b ^ 1);
-        cp_async_wait<1>();                        // this lane's copies of tile t have landed
-        __syncwarp();                              // ... and every other lane's
+        if (!__all_sync(FULL, mbar_wait(&full[wid][b], uint32_t((kk >> 1) & 1), lane == 0 ? status : nullptr))) {
+            fail_sh = 1;
+            break;
+        }
         T *base; int64_t row0; int nvalid, heads;
         tile_info(t, base, row0, nvalid, heads);
         const float *w = wsh[t < q_tiles ? 0 : 1];
@@ -183,8 +220,8 @@ __global__ void __launch_bounds__(rope_warps<T>() * 32, 1) qk_norm_rope_kernel(
         for (int c = lane; c < nvalid * CPR; c += 32)
             st_cs_v4(dst + size_t(c) * 16, *reinterpret_cast<const uint4 *>(tb + (c / CPR) * ROWB + (c % CPR) * 16));
         __syncwarp();          // all reads of buffer b done before it is refilled
+        if (lane == 0) mbar_arrive(&empty[wid][b]);
     }
-    cp_async_wait<0>();        // no copy may still be landing when the CTA exits
 }
 
 template <typename T>
@@ -200,9 +237,8 @@ static cudaError_t launch_rope_t(T *q, T *k, const int32_t *pos, int64_t rows, i
     const int64_t tiles = (qr + ROPE_TILE - 1) / ROPE_TILE + (kr + ROPE_TILE - 1) / ROPE_TILE;
     int64_t blocks = (tiles + RW - 1) / RW;                      // one CTA per SM (shared memory)
     if (blocks > sms) blocks = sms;
-    (void)status;                                                // no polling waits: nothing to report
-    qk_norm_rope_kernel<T><<<unsigned(blocks), RW * 32, SMEM, stream>>>(q, k, pos, qr, kr, nh, nkv, qn, kn, invf,
-                                                                      eps);
+    qk_norm_rope_kernel<T><<<unsigned(blocks), (RW + 1) * 32, SMEM, stream>>>(q, k, pos, qr, kr, nh, nkv, qn, kn,
+                                                                            invf, eps, status);
     return cudaGetLastError();
 }
 
