@@ -2,7 +2,9 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--workload NAME]
 
-Workloads: prefill4b (default: the headline line), decode8b, embed, prefill14b.
+Workloads: prefill4b (default: the headline line), decode8b, embed, prefill14b,
+decode06b (one Qwen3-0.6B decode token through 28 layers of the path's ops,
+timed eagerly and as CUDA graphs: microseconds per op and per layer).
 
 A step is one pass of the layer's memory-bound kernels over one batch of
 token rows already resident in HBM.  Default workload `prefill4b`: the
@@ -403,7 +405,178 @@ class Embed(Workload):
         return self.total_bytes() * n / self.tokens
 
 
-WORKLOADS = {"prefill4b": Prefill4B, "decode8b": Decode8B, "embed": Embed, "prefill14b": Prefill14B}
+class Decode06B(Workload):
+    """Qwen3-0.6B decode step through the path's ops: T token rows (1: one
+    decode token) at position 37, the embedding row, then 28 layers of
+    attention RMSNorm+Q8_0 (1024), QK-norm+RoPE (16 + 8 heads of 128), the 16
+    score rows of 38 (zero KV cache), the attention-output quantize (2048),
+    FFN RMSNorm+Q8_0 and SwiGLU+Q8_0 (3072), and the final RMSNorm+Q8_0 -- in
+    layer order, each op on its own layer's inputs.  Latency-bound: read as
+    microseconds per op and per layer (the `graph` key: the same op sequence
+    captured in a CUDA graph and replayed, per op type and for the whole step),
+    not as a roofline fraction."""
+    name = "decode06b"
+    dtype = "f32"
+
+    def __init__(self, tokens=1, dim=1024, nh=16, nkv=8, hd=128, hidden=3072, layers=28, pos=37, vocab=151936):
+        self.tokens, self.dim, self.nh, self.nkv, self.hd = tokens, dim, nh, nkv, hd
+        self.hidden, self.layers, self.pos, self.vocab = hidden, layers, pos, vocab
+
+    def op_bytes(self):
+        T, D, H, A, n = self.tokens, self.dim, self.hidden, self.nh * self.hd, self.pos + 1
+        return {
+            "embed_gather": T * (4 + D + D // 16 + 4 * D),
+            "rmsnorm_q8": T * (4 * D + D + D // 16 * 4) + 4 * D,
+            "qk_norm_rope": 2 * T * (self.nh + self.nkv) * self.hd * 4 + T * 4 + 2 * self.hd * 4,
+            "softmax_rows": 8 * T * self.nh * n + 12 * T * self.nh,
+            "quantize_q8": T * (4 * A + A + A // 16 * 4),
+            "swiglu_q8": T * (2 * 4 * H + H + H // 16 * 4),
+        }
+
+    def op_counts(self):
+        L = self.layers
+        return {"embed_gather": 1, "rmsnorm_q8": 2 * L + 1, "qk_norm_rope": L, "softmax_rows": L,
+                "quantize_q8": L, "swiglu_q8": L}
+
+    def kernels(self):
+        b, c = self.op_bytes(), self.op_counts()
+        return [("decode_step_ops", sum(b[k] * c[k] for k in b))]
+
+    def config(self):
+        return {"workload": "Qwen3-0.6B decode step through the path's ops (28 layers; the Q8_0 matmuls are not "
+                            "on the path)", "tokens_per_gpu": self.tokens, "dim": self.dim, "n_heads": self.nh,
+                "n_kv_heads": self.nkv, "head_dim": self.hd, "hidden": self.hidden, "layers": self.layers,
+                "position": self.pos, "vocab": self.vocab, "input_dtype": "f32"}
+
+    def make(self, torch, dev, seed):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        L, T, D, H, A = self.layers, self.tokens, self.dim, self.hidden, self.nh * self.hd
+        n = self.pos + 1
+        r = lambda *shape: torch.randn(*shape, device=dev, generator=g)
+        rows = T * self.nh
+        d = {
+            "xa": r(L, T, D), "xf": r(L, T, D), "xfin": r(T, D),
+            "wa": 1 + 0.1 * r(L, D), "wf": 1 + 0.1 * r(L, D), "wfin": 1 + 0.1 * r(D),
+            "q": r(L, T, self.nh, self.hd), "k": r(L, T, self.nkv, self.hd),
+            "qn": 1 + 0.1 * r(L, self.hd), "kn": 1 + 0.1 * r(L, self.hd),
+            "pos": torch.full((T,), self.pos, dtype=torch.int32, device=dev),
+            "sc": 2.0 * r(L, rows * n), "off": torch.arange(rows, device=dev, dtype=torch.int64) * n,
+            "len": torch.full((rows,), n, dtype=torch.int32, device=dev),
+            "ao": r(L, T, A), "hb": r(L, T, H), "hb2": r(L, T, H),
+            "tq": torch.randint(-127, 128, (self.vocab, D), dtype=torch.int8, device=dev, generator=g),
+            "ts": (0.01 * r(self.vocab, D // GS)).abs(),
+            "ids": torch.randint(0, self.vocab, (T,), dtype=torch.int32, device=dev, generator=g),
+            "emb": torch.empty(T, D, device=dev),
+            "xq": torch.empty(T, D, dtype=torch.int8, device=dev), "xs": torch.empty(T, D // GS, device=dev),
+            "aq": torch.empty(T, A, dtype=torch.int8, device=dev), "as": torch.empty(T, A // GS, device=dev),
+            "hq": torch.empty(T, H, dtype=torch.int8, device=dev), "hs": torch.empty(T, H // GS, device=dev),
+        }
+        return d
+
+    def _ops(self, q3, d, stream):
+        """(op type, launch) in layer order; per-layer views are taken here once."""
+        ops = [("embed_gather", lambda: q3.embed_gather(d["tq"], d["ts"], d["ids"], want_q8=False, out=d["emb"],
+                                                         stream=stream))]
+        for l in range(self.layers):
+            xa, xf, wa, wf = d["xa"][l], d["xf"][l], d["wa"][l], d["wf"][l]
+            q, k, qn, kn, sc = d["q"][l], d["k"][l], d["qn"][l], d["kn"][l], d["sc"][l]
+            ao, hb, hb2 = d["ao"][l], d["hb"][l], d["hb2"][l]
+            ops += [
+                ("rmsnorm_q8", lambda xa=xa, wa=wa: q3.rmsnorm_q8(xa, wa, q=d["xq"], s=d["xs"], stream=stream)),
+                ("qk_norm_rope", lambda q=q, k=k, qn=qn, kn=kn: q3.qk_norm_rope(q, k, d["pos"], qn, kn,
+                                                                                stream=stream)),
+                ("softmax_rows", lambda sc=sc: q3.softmax_rows(sc, d["off"], d["len"], stream=stream)),
+                ("quantize_q8", lambda ao=ao: q3.quantize_q8(ao, q=d["aq"], s=d["as"], stream=stream)),
+                ("rmsnorm_q8", lambda xf=xf, wf=wf: q3.rmsnorm_q8(xf, wf, q=d["xq"], s=d["xs"], stream=stream)),
+                ("swiglu_q8", lambda hb=hb, hb2=hb2: q3.swiglu_q8(hb, hb2, q=d["hq"], s=d["hs"], stream=stream)),
+            ]
+        ops.append(("rmsnorm_q8", lambda: q3.rmsnorm_q8(d["xfin"], d["wfin"], q=d["xq"], s=d["xs"], stream=stream)))
+        return ops
+
+    def launch(self, q3, d, stream, events=None):
+        if not hasattr(self, "_opl") or self._opl[0] is not d or self._opl[1] is not stream:
+            self._opl = (d, stream, self._ops(q3, d, stream))
+        ops = self._opl[2]
+        if events is not None:
+            events[0][0].record(stream)
+        for _, op in ops:
+            op()
+        if events is not None:
+            events[0][1].record(stream)
+        return len(ops)
+
+    def graph_report(self, torch, q3, d, stream, reps=20):
+        """The step's ops captured in CUDA graphs and replayed: the whole step
+        in layer order, and each op type's launches alone; device microseconds."""
+        ops = self._ops(q3, d, stream)
+        groups = {"step": ops}
+        for name in self.op_counts():
+            groups[name] = [o for o in ops if o[0] == name]
+        out = {}
+        for name, lst in groups.items():
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for _, op in lst:
+                    op()
+            for _ in range(3):
+                gr.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with torch.cuda.stream(stream):
+                e0.record(stream)
+                for _ in range(reps):
+                    gr.replay()
+                e1.record(stream)
+            stream.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / reps
+            out[name] = {"us_per_replay": round(us, 2), "launches": len(lst), "us_per_op": round(us / len(lst), 2)}
+            del gr
+        out["us_per_layer"] = round((out["step"]["us_per_replay"] - out["embed_gather"]["us_per_replay"]) /
+                                    self.layers, 2)
+        return out
+
+    h2d_keys = ("xa", "xf", "xfin", "q", "k", "sc", "ao", "hb", "hb2", "ids")
+    d2h_keys = ("emb", "xq", "xs", "aq", "as", "hq", "hs")
+
+    def cpu_step(self, oracle, np, sample, threads, rng):
+        """One decode token of the reference's CPU code, on one core (the
+        reference runs these ops serially per token)."""
+        if not hasattr(self, "_cpu"):
+            D, H, A, n = self.dim, self.hidden, self.nh * self.hd, self.pos + 1
+            f = lambda *shape: rng.standard_normal(shape, dtype=np.float32)
+            self._cpu = dict(x=f(1, D), w=(1 + 0.1 * f(D)).astype(np.float32), q=f(1, self.nh, self.hd),
+                             k=f(1, self.nkv, self.hd), pos=np.array([self.pos], np.int32),
+                             qn=(1 + 0.1 * f(self.hd)).astype(np.float32), kn=(1 + 0.1 * f(self.hd)).astype(np.float32),
+                             sc=(2.0 * f(self.nh * n)).astype(np.float32),
+                             off=(np.arange(self.nh) * n).astype(np.int64), lens=np.full(self.nh, n, np.int32),
+                             ao=f(1, A), hb=f(1, H), hb2=f(1, H),
+                             tq=rng.integers(-127, 128, size=(1024, D), dtype=np.int8),
+                             ts=np.abs(0.01 * f(1024, D // GS)).astype(np.float32),
+                             ids=np.array([7], np.int32))
+        c = self._cpu
+        if hasattr(oracle, "decode_ops"):           # the reference's code, the whole sequence in C
+            oracle.decode_ops(c["tq"], c["ts"], int(c["ids"][0]), c["x"], c["w"], c["q"], c["k"], self.pos, c["qn"],
+                              c["kn"], c["sc"], c["ao"], c["hb"], c["hb2"], self.layers)
+            return
+        oracle.rows_embed(c["tq"], c["ts"], c["ids"], want_q8=False, threads=1)
+        for _ in range(self.layers):
+            oracle.rows_rmsnorm_q8(c["x"], c["w"], threads=1)
+            oracle.rows_qk_norm_rope(c["q"], c["k"], c["pos"], c["qn"], c["kn"], threads=1)
+            oracle.rows_softmax(c["sc"], c["off"], c["lens"], threads=1)
+            oracle.rows_quantize(c["ao"], threads=1)
+            oracle.rows_rmsnorm_q8(c["x"], c["w"], threads=1)
+            oracle.rows_swiglu_q8(c["hb"], c["hb2"], threads=1)
+        oracle.rows_rmsnorm_q8(c["x"], c["w"], threads=1)
+
+    cpu_tokens = 1                      # cpu_step runs one decode token whatever the sample
+    cpu_threads = 1                     # ... on one core
+
+    def bytes_for_tokens(self, n):
+        return self.total_bytes()
+
+
+WORKLOADS = {"prefill4b": Prefill4B, "decode8b": Decode8B, "embed": Embed, "prefill14b": Prefill14B,
+             "decode06b": Decode06B}
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -491,7 +664,7 @@ def profiled_traffic(workload, kernel, alg_bytes=None):
 def cpu_baseline(workload, seconds=10.0):
     import numpy as np
     impl, kind = cpu_impl()
-    threads = os.cpu_count() or 1
+    threads = getattr(workload, "cpu_threads", os.cpu_count() or 1)
     sample = 128
     rng = np.random.default_rng(0)
     workload.cpu_step(impl, np, sample, threads, rng)          # warm up (allocations, page faults)
@@ -505,9 +678,9 @@ def cpu_baseline(workload, seconds=10.0):
             break
     gbs = workload.bytes_for_tokens(sample) * n / el / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
-            "sample": f"{n} passes over {sample} tokens of the same step ({el:.1f} s), OpenMP over rows; "
-                      + CPU_NOTE[kind],
-            "tokens_per_s": round(sample * n / el, 1)}
+            "sample": f"{n} passes over {getattr(workload, 'cpu_tokens', sample)} tokens of the same step "
+                      f"({el:.1f} s), OpenMP over rows; " + CPU_NOTE[kind],
+            "tokens_per_s": round(getattr(workload, "cpu_tokens", sample) * n / el, 1)}
 
 
 # ---------------------------------------------------------------------------- reference arm
@@ -527,7 +700,7 @@ def run_reference(args, wl):
         return 0
     import numpy as np
     impl, kind = cpu_impl()
-    threads = os.cpu_count() or 1
+    threads = getattr(wl, "cpu_threads", os.cpu_count() or 1)
     sample = 32
     rng = np.random.default_rng(0)
     for _ in range(args.warmup):
@@ -542,9 +715,10 @@ def run_reference(args, wl):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
         "config": dict(wl.config(), sample_tokens_per_step=sample),
-        "tokens_per_s": round(sample * args.steps / el, 2),
+        "tokens_per_s": round(getattr(wl, "cpu_tokens", sample) * args.steps / el, 2),
         "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": kind,
-                         "sample": f"{sample} tokens per step of the same workload, {threads} host threads "
+                         "sample": f"{getattr(wl, 'cpu_tokens', sample)} tokens per step of the same workload, "
+                                   f"{threads} host threads "
                                    f"(OpenMP over rows); " + CPU_NOTE[kind]},
         "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
@@ -554,7 +728,7 @@ def run_reference(args, wl):
 
 # The CPU implementation's row functions, by the kernel they stand for.
 CPU_KERNEL = {"rows_rmsnorm_q8": "rmsnorm_q8", "rows_qk_norm_rope": "qk_norm_rope", "rows_swiglu_q8": "swiglu_q8",
-              "rows_softmax": "softmax_rows", "rows_embed": "embed_gather"}
+              "rows_softmax": "softmax_rows", "rows_embed": "embed_gather", "rows_quantize": "quantize_q8"}
 
 
 class _TimedImpl:
@@ -585,7 +759,9 @@ def cpu_kernels(args, wl):
     impl, kind = cpu_impl()
     cores = os.cpu_count() or 1
     sample = 128
-    if hasattr(wl, "kernel_bytes"):
+    if hasattr(wl, "op_bytes"):
+        kb = {k: b * wl.op_counts()[k] for k, b in wl.op_bytes().items()}
+    elif hasattr(wl, "kernel_bytes"):
         kb = dict(wl.kernel_bytes(wl.sample_pos(sample)))
     else:
         kb = {n: b * sample / wl.tokens for n, b in wl.kernels()}
@@ -708,6 +884,9 @@ def main():
     if q3.device_status(stream) != 0:
         raise RuntimeError("device status set during the timed region")
 
+    # ---- CUDA graphs of the step's ops (latency-bound workloads) -----------
+    graph = wl.graph_report(torch, q3, d, stream) if hasattr(wl, "graph_report") else None
+
     # ---- end to end: host buffers, copies inside the timed region ----------
     hin = {k: d[k].detach().to("cpu").pin_memory() for k in wl.h2d_keys}
     hout = {k: torch.empty(d[k].shape, dtype=d[k].dtype).pin_memory() for k in wl.d2h_keys}
@@ -812,6 +991,8 @@ def main():
             "gpu_launches": launches,
             "clocks": clk,
         }
+        if graph is not None:
+            line["graph"] = graph
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
         print(json.dumps(line), flush=True)

@@ -317,10 +317,13 @@ class ReferenceRows:
         vp, i32, i64 = C.c_void_p, C.c_int, C.c_int64
         for name, args in (
             ("ref_rows_rmsnorm_q8", [vp, vp, i64, i32, vp, vp, i32]),
+            ("ref_rows_quantize", [vp, i64, i32, vp, vp, i32]),
             ("ref_rows_qk_norm_rope", [vp, vp, vp, i64, i32, i32, i32, vp, vp, i32]),
             ("ref_rows_swiglu_q8", [vp, vp, i64, i32, vp, vp, i32]),
             ("ref_rows_softmax", [vp, vp, vp, i64, i32]),
             ("ref_rows_embed", [vp, vp, i32, i32, vp, i64, vp, vp, vp, i32]),
+            ("ref_decode_ops", [vp, vp, i32, i32, vp, vp, vp, vp, vp, i32, i32, i32, i32, vp, vp, vp, vp, vp, vp,
+                                i32, i32, vp, vp]),
         ):
             fn = getattr(self.lib, name)
             fn.restype = None
@@ -331,6 +334,13 @@ class ReferenceRows:
         q = np.empty((rows, dim), np.int8)
         s = np.empty((rows, dim // GS), np.float32)
         self.lib.ref_rows_rmsnorm_q8(_p(x), _p(w), rows, dim, _p(q), _p(s), threads)
+        return q, s
+
+    def rows_quantize(self, x, threads=1):
+        rows, n = x.shape
+        q = np.empty((rows, n), np.int8)
+        s = np.empty((rows, n // GS), np.float32)
+        self.lib.ref_rows_quantize(_p(np.ascontiguousarray(x, np.float32)), rows, n, _p(q), _p(s), threads)
         return q, s
 
     def rows_qk_norm_rope(self, q, k, pos, q_norm, k_norm, theta=1e6, threads=1):
@@ -364,6 +374,21 @@ class ReferenceRows:
         os_ = np.zeros((n, dim // GS), np.float32) if want_q8 else None
         self.lib.ref_rows_embed(_p(tq), _p(ts), vocab, dim, _p(ids), n, _p(out), _p(oq), _p(os_), threads)
         return out, oq, os_
+
+    def decode_ops(self, tq, ts, token, x, w, q, k, pos, qn, kn, sc, ao, hb, hb2, layers):
+        """One decode token through the path's ops (ref_decode_ops); q, k and sc
+        in place."""
+        dim = x.size
+        n_heads, head_dim = q.shape[-2], q.shape[-1]
+        n_kv = k.shape[-2]
+        big = max(dim, hb.size, n_heads * head_dim)
+        emb = np.empty(dim, np.float32)
+        q8 = np.empty(big, np.int8)
+        s8 = np.empty(big // GS, np.float32)
+        self.lib.ref_decode_ops(_p(tq), _p(ts), dim, int(token), _p(emb), _p(x), _p(w), _p(q), _p(k), n_heads,
+                                n_kv, head_dim, int(pos), _p(qn), _p(kn), _p(sc), _p(ao), _p(hb), _p(hb2), hb.size,
+                                layers, _p(q8), _p(s8))
+        return emb
 
 
 class OracleModel:

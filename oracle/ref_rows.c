@@ -42,6 +42,15 @@ void ref_rows_rmsnorm_q8(const float *x, const float *w, int64_t rows, int dim, 
     }
 }
 
+void ref_rows_quantize(const float *x, int64_t rows, int n, int8_t *q, float *s, int threads) {
+    GS = 64;
+    #pragma omp parallel for schedule(static) num_threads(NT(threads))
+    for (int64_t r = 0; r < rows; r++) {
+        QuantizedTensor qt = {q + r * n, s + r * (n / 64)};
+        quantize(&qt, (float *)(x + r * n), n);
+    }
+}
+
 void ref_rows_qk_norm_rope(float *q, float *k, const int32_t *pos, int64_t rows, int n_heads, int n_kv,
                            int head_dim, const float *q_norm, const float *k_norm, int threads) {
     GS = 64;
@@ -105,4 +114,39 @@ void ref_rows_embed(const int8_t *tq, const float *ts, int vocab, int dim, const
             quantize(&dst, row, dim);
         }
     }
+}
+
+/* One decode token through the path's ops, in the order of forward()
+ * (qwen3_original.c:333-468 without its matmuls and attention dot products):
+ * the embedding row, then per layer RMSNorm + quantize (:353-356), the QK-norm
+ * + RoPE loop (:361-393), softmax of the n_heads score rows of pos+1 (:416),
+ * quantize of the attention output (:431), RMSNorm + quantize (:439-443),
+ * SwiGLU + quantize (:449-453); then the final RMSNorm + quantize (:462-465).
+ * Every layer reuses the same inputs (the matmuls that would produce fresh ones
+ * are not on the path); q, k and the scores are updated in place. */
+void ref_decode_ops(const int8_t *tq, const float *ts, int dim, int token, float *emb, const float *x,
+                    const float *w, float *q, float *k, int n_heads, int n_kv, int head_dim, int pos,
+                    const float *qn, const float *kn, float *sc, const float *ao, const float *hb,
+                    const float *hb2, int hidden, int layers, int8_t *q8, float *s8) {
+    GS = 64;
+    const int ahd = n_heads * head_dim, n = pos + 1;
+    const int big = dim > hidden ? dim : hidden;
+    float *o = malloc((size_t)(big > ahd ? big : ahd) * 4);
+    QuantizedTensor row = {(int8_t *)tq + (int64_t)token * dim, (float *)ts + (int64_t)token * (dim / 64)};
+    dequantize(&row, emb, dim);
+    QuantizedTensor out = {q8, s8};
+    for (int l = 0; l < layers; l++) {
+        rmsnorm(o, (float *)x, (float *)w, dim);
+        quantize(&out, o, dim);
+        ref_rows_qk_norm_rope(q, k, &pos, 1, n_heads, n_kv, head_dim, qn, kn, 1);
+        for (int h = 0; h < n_heads; h++) softmax(sc + (int64_t)h * n, n);
+        quantize(&out, (float *)ao, ahd);
+        rmsnorm(o, (float *)x, (float *)w, dim);
+        quantize(&out, o, dim);
+        for (int i = 0; i < hidden; i++) o[i] = hb[i] * (hb2[i] * (1.0f / (1.0f + expf(-hb[i]))));
+        quantize(&out, o, hidden);
+    }
+    rmsnorm(o, (float *)x, (float *)w, dim);
+    quantize(&out, o, dim);
+    free(o);
 }
