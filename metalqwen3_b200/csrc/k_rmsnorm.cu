@@ -387,6 +387,92 @@ __global__ void __launch_bounds__(RMS_THREADS, 1) rmsnorm_kernel(const T *x, con
     }
 }
 
+// ---------------------------------------------------------------------------
+// Few rows (decode): one CTA of 256 threads per row.  Every thread copies its
+// 16-byte pieces of the row into shared memory with cp.async, attaching each
+// to the barrier of its 2 KB chunk; lane 0 of warp 0 folds the chunks into the
+// chain as they land (the same fold, in index order, as the persistent
+// kernel); then all threads normalise and quantize from shared memory, a lane
+// per 8 consecutive elements, 8 lanes per Q8_0 group.  No producer warp, ring
+// or block loop: the latency is the first chunk, the chain, and one pass.
+constexpr int RSM_THREADS = 256;
+constexpr int RSM_CB = 2048;                     // chunk bytes
+constexpr int RSM_MAXCH = 32;                    // rows of up to 64 KB
+constexpr int RSM_PPC = RSM_CB / 16;             // 16-byte pieces per chunk
+
+template <typename T, bool Q8>
+__global__ void __launch_bounds__(RSM_THREADS) rmsnorm_row_kernel(const T *x, const float *__restrict__ w, int dim,
+                                                                 int n_div, float eps, T *out,
+                                                                 int8_t *__restrict__ q, float *__restrict__ s,
+                                                                 uint32_t *status) {
+    constexpr int ESZ = sizeof(T);
+    extern __shared__ __align__(128) uint8_t rbuf[];
+    __shared__ __align__(8) uint64_t bar[RSM_MAXCH];
+    __shared__ float ss_sh;
+    const int tid = threadIdx.x;
+    const int64_t row = blockIdx.x;
+    const int row_bytes = dim * ESZ;
+    const int nch = (row_bytes + RSM_CB - 1) / RSM_CB;
+    const uint8_t *src = reinterpret_cast<const uint8_t *>(x) + row * int64_t(row_bytes);
+    if (tid == 0) {
+        for (int c = 0; c < nch; ++c) mbar_init(&bar[c], 1);
+        mbar_init_fence();
+    }
+    __syncthreads();
+    for (int f = tid; f < row_bytes / 16; f += RSM_THREADS) {
+        cp_async16(rbuf + f * 16, src + f * 16);
+        cp_async_track(&bar[f / RSM_PPC]);
+    }
+    __syncthreads();                              // every piece attached before the arrivals
+    if (tid == 0)
+        for (int c = 0; c < nch; ++c) mbar_arrive(&bar[c]);
+    if (tid < 32) {
+        float acc = 0.0f;
+        bool ok = true;
+        for (int c = 0; c < nch && ok; ++c) {
+            ok = __all_sync(FULL, mbar_wait(&bar[c], 0, tid == 0 ? status : nullptr));
+            if (ok && tid == 0) {
+                const int cb = row_bytes - c * RSM_CB < RSM_CB ? row_bytes - c * RSM_CB : RSM_CB;
+                acc = cb == RSM_CB ? chain_full<T>(acc, rbuf + c * RSM_CB) : chain_sum<T>(acc, rbuf + c * RSM_CB, cb / ESZ);
+            }
+            __syncwarp();
+        }
+        if (tid == 0) ss_sh = ok ? __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, float(n_div)), eps)))
+                                 : __int_as_float(0x7fc00000);
+    }
+    __syncthreads();
+    const float ss = ss_sh;
+    const f2 ss2 = pk2(ss, ss);
+    const int64_t e0 = row * int64_t(dim);
+    for (int u = tid; u * 8 < dim; u += RSM_THREADS) {   // 8 elements per lane; dim % 8 == 0 (host)
+        float xv[8], wv[8], o[8];
+        if constexpr (ESZ == 4) {
+            Vec<float>::widen(*reinterpret_cast<const uint4 *>(rbuf + u * 32), xv);
+            Vec<float>::widen(*reinterpret_cast<const uint4 *>(rbuf + u * 32 + 16), xv + 4);
+        } else {
+            Vec<T>::widen(*reinterpret_cast<const uint4 *>(rbuf + u * 16), xv);
+        }
+        Vec<float>::widen(ld_l1_v4(w + u * 8), wv);
+        Vec<float>::widen(ld_l1_v4(w + u * 8 + 4), wv + 4);
+#pragma unroll
+        for (int i = 0; i < 8; i += 2)
+            up2(mul2(pk2(wv[i], wv[i + 1]), mul2(ss2, pk2(xv[i], xv[i + 1]))), o[i], o[i + 1]);
+        if constexpr (Q8) {
+            uint32_t codes[2];
+            const float scale = q8_encode_lane<8, 8>(o, codes);
+            st_cs_u32(q + e0 + u * 8, codes[0]);
+            st_cs_u32(q + e0 + u * 8 + 4, codes[1]);
+            if ((tid & 7) == 0) st_cs_f32(s + ((e0 + u * 8) >> 6), scale);
+        } else if constexpr (ESZ == 4) {
+            st_cs_v4(out + e0 + u * 8, Vec<float>::narrow(o));
+            st_cs_v4(out + e0 + u * 8 + 4, Vec<float>::narrow(o + 4));
+        } else {
+            st_cs_v4(out + e0 + u * 8, Vec<T>::narrow(o));
+        }
+    }
+    cp_async_wait<0>();                           // (all landed already; no copy outlives the CTA)
+}
+
 template <typename T, bool Q8>
 static cudaError_t launch_rms_t(const T *x, const float *w, int64_t rows, int dim, int n_div, float eps, T *out,
                                 int8_t *q, float *s, uint32_t *status, cudaStream_t stream, int sms) {
@@ -396,6 +482,16 @@ static cudaError_t launch_rms_t(const T *x, const float *w, int64_t rows, int di
     const int R = int((rows_per_sm + bps - 1) / bps);
     const int64_t nblocks = (rows + R - 1) / R;
     const unsigned grid = unsigned(nblocks < sms ? nblocks : sms);
+    const int64_t row_bytes = int64_t(dim) * sizeof(T);
+    if (rows <= int64_t(sms) * 4 && row_bytes <= int64_t(RSM_CB) * RSM_MAXCH && dim % 8 == 0) {
+        const int rslot = 12 + (sizeof(T) == 4 ? 0 : 2) + (Q8 ? 1 : 0);
+        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(rmsnorm_row_kernel<T, Q8>),
+                                         size_t(RSM_CB) * RSM_MAXCH, rslot);
+        if (e != cudaSuccess) return e;
+        rmsnorm_row_kernel<T, Q8><<<unsigned(rows), RSM_THREADS, size_t(row_bytes), stream>>>(x, w, dim, n_div, eps,
+                                                                                          out, q, s, status);
+        return cudaGetLastError();
+    }
     const int slot = 2 + (sizeof(T) == 4 ? 0 : 2) + (Q8 ? 1 : 0);
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(rmsnorm_kernel<T, Q8>), RMS_SMEM, slot);
     if (e != cudaSuccess) return e;
