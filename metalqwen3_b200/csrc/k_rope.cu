@@ -97,10 +97,6 @@ __global__ void __launch_bounds__((rope_warps<T>() + 1) * 32, 1) qk_norm_rope_ke
     __shared__ int fail_sh;
 
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
-    for (int i = threadIdx.x; i < HD; i += blockDim.x) {
-        wsh[0][i] = q_norm[i];
-        wsh[1][i] = k_norm[i];
-    }
     if (threadIdx.x == 0) {
         for (int w = 0; w < RW; ++w)
             for (int b = 0; b < 2; ++b) {
@@ -164,12 +160,26 @@ __global__ void __launch_bounds__((rope_warps<T>() + 1) * 32, 1) qk_norm_rope_ke
         return;
     }
 
+    // The compute warps load the norm weights while the copy warp starts.
+    for (int i = threadIdx.x; i < HD; i += RW * 32) {
+        wsh[0][i] = q_norm[i];
+        wsh[1][i] = k_norm[i];
+    }
+    named_sync(1, RW * 32);
     uint8_t *buf0 = smem + size_t(wid) * rope_warp_bytes<T>();
     uint8_t *tab = buf0 + 2 * ROPE_TILE * ROWB;
     for (int64_t kk = 0;; ++kk) {
         const int64_t t = int64_t(blockIdx.x) * RW + wid + kk * GW;
         if (t >= ntiles) break;
         const int b = int(kk & 1);
+        // positions of the tile's tokens (lane l: token tok0 + l), loaded while the tile lands
+        int pv = 0;
+        {
+            T *pb; int64_t pr0; int pnv, phe;
+            tile_info(t, pb, pr0, pnv, phe);
+            const int64_t ptok0 = pr0 / phe;
+            if (lane <= int((pr0 + pnv - 1) / phe - ptok0)) pv = __ldg(pos + ptok0 + lane);
+        }
         if (!__all_sync(FULL, mbar_wait(&full[wid][b], uint32_t((kk >> 1) & 1), lane == 0 ? status : nullptr))) {
             fail_sh = 1;
             break;
@@ -201,7 +211,7 @@ __global__ void __launch_bounds__((rope_warps<T>() + 1) * 32, 1) qk_norm_rope_ke
         for (int tt0 = 0; tt0 < ntok; tt0 += ROPE_TOKS) {
             const int nt = ntok - tt0 < ROPE_TOKS ? ntok - tt0 : ROPE_TOKS;
             for (int tt = 0; tt < nt; ++tt) {
-                const float p = float(__ldg(pos + tok0 + tt0 + tt));
+                const float p = float(__shfl_sync(FULL, pv, tt0 + tt));   // a tile spans <= 32 tokens
                 float c0, s0, c1, s1;
                 sincosf(__fmul_rn(p, f0), &s0, &c0);
                 sincosf(__fmul_rn(p, f1), &s1, &c1);

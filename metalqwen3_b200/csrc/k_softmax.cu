@@ -471,11 +471,108 @@ softmax_ring_kernel(float *x, const int64_t *__restrict__ offs, const int32_t *_
     }
 }
 
+// ---- few rows (a decode token's heads) -------------------------------------
+// One CTA of SMS_THREADS per row, no ring: a row of at most SMS_THREADS * 16
+// scores is held in registers (one read, one write); a longer row takes three
+// passes over global memory (max; exponentials in place + sum; scale).  Same
+// arithmetic as the ring kernel: max from 0, exp_m80_0 with the exact expf
+// below -80, binary32 float4 partials summed in binary64 over a fixed tree.
+constexpr int SMS_THREADS = 256;
+constexpr int SMS_REG = 4;                       // float4 per thread held in registers
+
+__device__ __forceinline__ float sms_block_max(float v, float *sh) {
+    v = warp_max(v);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    __syncthreads();                              // sh free from the previous reduction
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    return warp_max(lane < SMS_THREADS / 32 ? sh[lane] : 0.0f);
+}
+__device__ __forceinline__ double sms_block_sum(double v, double *sh) {
+    v = warp_sum_d(v);
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+    __syncthreads();
+    if (lane == 0) sh[w] = v;
+    __syncthreads();
+    return warp_sum_d(lane < SMS_THREADS / 32 ? sh[lane] : 0.0);
+}
+
+__global__ void __launch_bounds__(SMS_THREADS) softmax_small_kernel(float *x, const int64_t *__restrict__ offs,
+                                                                    const int32_t *__restrict__ lens) {
+    __shared__ ExpTab s_tab;
+    __shared__ float sh_f[SMS_THREADS / 32];
+    __shared__ double sh_d[SMS_THREADS / 32];
+    load_exp_table(s_tab);
+    const int t = threadIdx.x;
+    const int len = __ldg(lens + blockIdx.x);
+    float *row = x + __ldg(offs + blockIdx.x);
+    __syncthreads();
+    if (len <= 0) return;                         // block-uniform
+    const RowSplit sp = split_row(row, len);
+    float4 *gb = reinterpret_cast<float4 *>(row + sp.a);
+    const int si = t < sp.a ? t : (t - sp.a < sp.tl ? sp.a + 4 * sp.nb + (t - sp.a) : -1);
+    float xs = si >= 0 ? row[si] : 0.0f;
+    if (sp.nb <= SMS_THREADS * SMS_REG) {
+        float4 v[SMS_REG];
+        float m = 0.0f;                           // the reference's max starts at 0
+#pragma unroll
+        for (int u = 0; u < SMS_REG; ++u) {
+            const int j = t + u * SMS_THREADS;
+            if (j < sp.nb) { v[u] = u4_as_f4(ld_v4(gb + j)); m = max4(m, v[u]); }
+        }
+        if (si >= 0) m = fmaxf(m, xs);
+        m = sms_block_max(m, sh_f);
+        double s = 0.0;
+        f2 part = pk2(0.0f, 0.0f);
+#pragma unroll
+        for (int u = 0; u < SMS_REG; ++u) {
+            if (t + u * SMS_THREADS < sp.nb) {
+                const float4 v0 = v[u];
+                if (!smx_exp4(v[u], m)) v[u] = smx_exp4_exact(v0, m, s_tab);
+                part = add2(part, add2(pk2(v[u].x, v[u].y), pk2(v[u].z, v[u].w)));
+            }
+        }
+        float p0, p1;
+        up2(part, p0, p1);
+        s = double(__fadd_rn(p0, p1));
+        if (si >= 0) { xs = smx_exp1(__fsub_rn(xs, m), s_tab); s += double(xs); }
+        const float inv = float(1.0 / sms_block_sum(s, sh_d));
+#pragma unroll
+        for (int u = 0; u < SMS_REG; ++u) {
+            const int j = t + u * SMS_THREADS;
+            if (j < sp.nb) st_cs_v4(gb + j, f4_as_u4(scale4(v[u], inv)));
+        }
+        if (si >= 0) row[si] = __fmul_rn(xs, inv);
+        return;
+    }
+    float m = 0.0f;
+    for (int j = t; j < sp.nb; j += SMS_THREADS) m = max4(m, u4_as_f4(ld_v4(gb + j)));
+    if (si >= 0) m = fmaxf(m, xs);
+    m = sms_block_max(m, sh_f);
+    double s = 0.0;
+    for (int j = t; j < sp.nb; j += SMS_THREADS) {
+        float4 v = u4_as_f4(ld_v4(gb + j));
+        const float4 v0 = v;
+        if (!smx_exp4(v, m)) v = smx_exp4_exact(v0, m, s_tab);
+        *reinterpret_cast<uint4 *>(gb + j) = f4_as_u4(v);
+        s += double(__fadd_rn(__fadd_rn(v.x, v.y), __fadd_rn(v.z, v.w)));
+    }
+    if (si >= 0) { xs = smx_exp1(__fsub_rn(xs, m), s_tab); s += double(xs); }
+    const float inv = float(1.0 / sms_block_sum(s, sh_d));
+    for (int j = t; j < sp.nb; j += SMS_THREADS)
+        st_cs_v4(gb + j, f4_as_u4(scale4(u4_as_f4(ld_v4(gb + j)), inv)));
+    if (si >= 0) row[si] = __fmul_rn(xs, inv);
+}
+
 constexpr int SMX_SMEM_SLOT = 8;
 
 cudaError_t launch_softmax_rows(float *x, const int64_t *off, const int32_t *len, int64_t rows, uint32_t *sched,
                                 uint32_t *status, cudaStream_t stream, int sms) {
     if (rows <= 0) return cudaSuccess;
+    if (rows <= int64_t(sms) * 2) {               // a decode token's heads: one CTA per row
+        softmax_small_kernel<<<unsigned(rows), SMS_THREADS, 0, stream>>>(x, off, len);
+        return cudaGetLastError();
+    }
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(softmax_ring_kernel), SMX_RING, SMX_SMEM_SLOT);
     if (e != cudaSuccess) return e;
     // Units small enough that every SM takes about 16 of them (balance), at

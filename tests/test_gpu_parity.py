@@ -379,14 +379,18 @@ def _check_ragged(g, x, o, off, lens):
     assert np.array_equal(bits(g[~inrow]), bits(x[~inrow]))
 
 
-def test_softmax_row_classes(q3, oracle):
-    """Every path of the kernel in one call: rows of one warp (<= 4096), rows
-    shared by the CTA and staged in shared memory (<= 57344 after the leading
-    scalars), rows longer than the ring (global memory), empty and negative
-    lengths; some rows hold scores far below their max (the exact-exp branch:
-    subnormal and zero exponentials) and one holds a NaN."""
+@pytest.mark.parametrize("extra", [0, 400])
+def test_softmax_row_classes(q3, oracle, extra):
+    """Every path in one call.  With few rows (extra = 0) the one-CTA-per-row
+    kernel: register rows (<= 16384 scores) and three-pass rows.  With 400
+    extra short rows the ring kernel: rows of one warp (<= 4096), rows shared
+    by the CTA and staged in shared memory, rows longer than the ring (global
+    memory).  Empty and negative lengths; some rows hold scores far below
+    their max (the exact-exp branch: subnormal and zero exponentials) and one
+    holds a NaN."""
     rng = np.random.default_rng(7)
     lens = [0, 3, 4096, 4097, -5, 57340, 57344, 57345, 57347, 60000, 131072, 1, 9000, 20000]
+    lens = lens + list(rng.integers(1, 9, extra))
     x, off, lens = _ragged_case(rng, lens)
     for r, n in ((3, 4097), (9, 60000), (12, 9000), (1, 3)):     # far-below-max scores
         idx = off[r] + rng.choice(n, min(n, 40), replace=False)
