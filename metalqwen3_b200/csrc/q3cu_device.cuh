@@ -139,9 +139,15 @@ __device__ __forceinline__ uint32_t q8_code(float v, float scale) {
 
 __device__ __forceinline__ float q8_scale(float wmax) { return __fdiv_rn(wmax, 127.0f); }
 
+// 1/x within 1 ulp, for x whose reciprocal is a normal binary32 number (every
+// caller: 1 <= x < 2^120, or a Q8_0 scale in [2^-97, 2^93]; a group outside
+// that range takes the exact path and ignores this value).  The .ftz form is
+// the bare hardware approximation; without .ftz the compiler wraps it in a
+// subnormal rescaling (compare, two selects, two multiplies per call) that
+// these operands never need.
 __device__ __forceinline__ float rcp_approx(float x) {
     float r;
-    asm("rcp.approx.f32 %0, %1;" : "=f"(r) : "f"(x));   // max error 1 ulp
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
     return r;
 }
 
