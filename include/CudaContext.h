@@ -43,10 +43,15 @@ public:
     // the engine's CPU quantize (MetalQwen3.cpp:308-329) and embedding copy (:228)
     void executeQuantize(int8_t *q, float *s, const float *x, int n);
     void executeEmbedding(float *out, const int8_t *q, const float *s, int token, int dim);
+    // MetalContext::executeQuantizedMatMul (src/metal/MetalContext.h:81-82).
+    void executeQuantizedMatMul(float *output, const int8_t *x_q, const float *x_s, const int8_t *w_q,
+                                const float *w_s, int n, int d, int group_size);
 
     // batched device-pointer path (asynchronous on `stream`)
     void rmsnormQ8(const void *x, q3cu_dtype dt, const float *w, int64_t rows, int dim, int8_t *q, float *s,
                    q3cu_stream stream, float eps = 1e-6f);
+    void matmulQ8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n, int d,
+                  float *out, q3cu_stream stream);
     void rmsnorm(const void *x, q3cu_dtype dt, const float *w, int64_t rows, int dim, void *out,
                  q3cu_stream stream, float eps = 1e-6f);
     void qkNormRope(void *q, void *k, q3cu_dtype dt, const int32_t *pos, int64_t rows, int n_heads, int n_kv,

@@ -155,6 +155,17 @@ q3cu_status q3cu_embed_gather(q3cu_ctx *ctx, const int8_t *tq, const float *ts, 
                               int dim, const int32_t *ids, int64_t n, float *out_f32,
                               int8_t *out_q, float *out_s, q3cu_stream stream);
 
+/* Q8_0 x Q8_0 matrix products for B token rows (qwen3_original.c:310-331
+ * `matmul`, applied to each row; engine src/metal/MetalQwen3.cpp:530-533,
+ * shaders/quantized_matmul.metal): out[b][i] = sum over the 64-groups j of row
+ * i, in order, of RN(RN((float) dot(xq[b] group j, wq[i] group j) * ws[i][j])
+ * * xs[b][j]) -- the reference's bits.  xq [B][n], xs [B][n/64]; wq [d][n],
+ * ws [d][n/64] (row-major [out][in]); out [B][d].  n % 64 == 0; xq and wq
+ * 32-byte aligned.  W is streamed once per block of up to 4 token rows. */
+q3cu_status q3cu_matmul_q8(q3cu_ctx *ctx, const int8_t *xq, const float *xs, int B,
+                           const int8_t *wq, const float *ws, int n, int d, float *out,
+                           q3cu_stream stream);
+
 /* ---- host-pointer drop-in (synchronous), MetalContext signatures -------- */
 
 /* MetalContext::executeRMSNorm (src/metal/MetalContext.h:79). */
@@ -171,6 +182,12 @@ q3cu_status q3cu_execute_rope(q3cu_ctx *ctx, float *q, float *k, int head_dim, i
                               const float *k_norm_weights);
 /* The engine's CPU quantize (src/metal/MetalQwen3.cpp:308-329). */
 q3cu_status q3cu_execute_quantize(q3cu_ctx *ctx, int8_t *q, float *s, const float *x, int n);
+/* MetalContext::executeQuantizedMatMul (src/metal/MetalContext.h:81-82): one
+ * token, W (d,n) @ x (n,) -> output (d,), all host pointers (copied in per
+ * call, as the Metal path does).  group_size must be 64. */
+q3cu_status q3cu_execute_quantized_matmul(q3cu_ctx *ctx, float *output, const int8_t *x_q,
+                                          const float *x_s, const int8_t *w_q, const float *w_s,
+                                          int n, int d, int group_size);
 /* The engine's embedding row copy (src/metal/MetalQwen3.cpp:228) from a Q8_0
  * table row instead of a dequantized fp32 table. */
 q3cu_status q3cu_execute_embedding(q3cu_ctx *ctx, float *out, const int8_t *q, const float *s,

@@ -49,6 +49,14 @@ void CudaContext::executeEmbedding(float *out, const int8_t *q, const float *s, 
     check(q3cu_execute_embedding(ctx_, out, q, s, token, dim), "executeEmbedding");
 }
 
+void CudaContext::executeQuantizedMatMul(float *output, const int8_t *x_q, const float *x_s, const int8_t *w_q,
+                                         const float *w_s, int n, int d, int group_size) {
+    check(q3cu_execute_quantized_matmul(ctx_, output, x_q, x_s, w_q, w_s, n, d, group_size), "executeQuantizedMatMul");
+}
+void CudaContext::matmulQ8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n, int d,
+                           float *out, q3cu_stream stream) {
+    check(q3cu_matmul_q8(ctx_, xq, xs, B, wq, ws, n, d, out, stream), "matmulQ8");
+}
 void CudaContext::rmsnormQ8(const void *x, q3cu_dtype dt, const float *w, int64_t rows, int dim, int8_t *q, float *s,
                             q3cu_stream stream, float eps) {
     check(q3cu_rmsnorm_q8(ctx_, x, dt, w, rows, dim, eps, q, s, stream), "rmsnormQ8");

@@ -1,0 +1,162 @@
+// k_matmul.cu -- Q8_0 x Q8_0 matrix-vector products, bit-exact with the
+// reference's matmul, for a few token rows at a time (decode).
+//
+// Reference: src/cpu/qwen3_original.c:310-331, W (d,n) @ x (n,) -> xout (d,):
+//     for i < d:  val = 0
+//                 for each 64-group j (in order):
+//                     ival = sum_k x.q[j+k] * w.q[i*n+j+k]          (int32, exact)
+//                     val += ((float) ival) * w.s[(i*n+j)/64] * x.s[j/64]
+//                 xout[i] = val
+// Built without FMA contraction, the group term is RN(RN(float(ival) * ws) * xs)
+// and val is a sequential binary32 sum over the groups, in group order.
+//
+// Layout: W codes [d][n] int8 and scales [d][n/64] f32 (row-major [out][in],
+// as the reference stores them); x codes [B][n] and scales [B][n/64]; out
+// [B][d] f32.  The int8 dot products are exact in any order, so they are
+// spread over lanes: a warp job is a tile of RB output rows x TB tokens, and
+// in each pass over 32 consecutive groups lane g takes group g of every row of
+// the tile -- two 32-byte loads of the row's codes per lane, so the warp reads
+// 2 KB of the row contiguously -- and forms the TB group terms with dp4a.  The
+// terms go to a padded shared-memory transpose, and lane s = (row, token) then
+// adds its 32 terms to its running val in group order: the reference's
+// accumulation, so the outputs are its bits.  The codes of the lane's group for
+// the TB tokens stay in registers across the rows of the tile.
+//
+// Cost: W is read once per block of TB tokens (TB <= 4), so for one to four
+// tokens the kernel streams W at HBM speed; larger batches re-read W per block
+// (a tensor-core path for prefill-sized batches is not part of this file).
+#include "q3cu_internal.h"
+
+namespace q3 {
+
+constexpr int MM_WARPS = 8;
+constexpr int MM_THREADS = MM_WARPS * 32;
+
+__device__ __forceinline__ int dot64(const U8 &a0, const U8 &a1, const U8 &b0, const U8 &b1) {
+    int acc = 0;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc = __dp4a(int(a0.w[k]), int(b0.w[k]), acc);
+#pragma unroll
+    for (int k = 0; k < 8; ++k) acc = __dp4a(int(a1.w[k]), int(b1.w[k]), acc);
+    return acc;
+}
+
+template <int TB>
+__global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__restrict__ xq,
+                                                               const float *__restrict__ xs, int B,
+                                                               const int8_t *__restrict__ wq,
+                                                               const float *__restrict__ ws, int n, int d, int RB,
+                                                               float *__restrict__ out) {
+    __shared__ float terms[MM_WARPS][32][33];      // [slot = row * TB + token][group], padded
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int G = n / GS;                           // groups per row
+    const int tiles = (d + RB - 1) / RB;
+    const int ntb = (B + TB - 1) / TB;
+    const int64_t jobs = int64_t(tiles) * ntb;
+    const int slots = RB * TB;                      // (row, token) pairs of a tile, <= 32
+    float(*tw)[33] = terms[warp];
+
+    for (int64_t job = int64_t(blockIdx.x) * MM_WARPS + warp; job < jobs; job += int64_t(gridDim.x) * MM_WARPS) {
+        const int tile = int(job % tiles), tb = int(job / tiles);
+        const int i0 = tile * RB, t0 = tb * TB;
+        float val = 0.0f;                           // lane s < slots: row i0 + s / TB, token t0 + s % TB
+        for (int g0 = 0; g0 < G; g0 += 32) {
+            const int g = g0 + lane;
+            const bool gl = g < G;
+            U8 xa[TB], xb[TB];
+            float xsc[TB];
+#pragma unroll
+            for (int t = 0; t < TB; ++t) {
+                const bool tl = gl && t0 + t < B;
+                const int8_t *xp = xq + int64_t(t0 + t) * n + int64_t(g) * GS;
+                if (tl) {
+                    xa[t] = ld_nc_v8(xp);
+                    xb[t] = ld_nc_v8(xp + 32);
+                    xsc[t] = xs[int64_t(t0 + t) * G + g];
+                } else {
+#pragma unroll
+                    for (int k = 0; k < 8; ++k) xa[t].w[k] = xb[t].w[k] = 0u;
+                    xsc[t] = 0.0f;
+                }
+            }
+            const int rmax = d - i0 < RB ? d - i0 : RB;
+            int r = 0;
+            for (; r + 1 < rmax; r += 2) {         // two rows' loads in flight
+                U8 wa[2], wb[2];
+                float wsc[2];
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const int64_t row = i0 + r + u;
+                    if (gl) {
+                        wa[u] = ld_nc_v8(wq + row * n + int64_t(g) * GS);
+                        wb[u] = ld_nc_v8(wq + row * n + int64_t(g) * GS + 32);
+                        wsc[u] = ws[row * G + g];
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 2; ++u)
+#pragma unroll
+                    for (int t = 0; t < TB; ++t) {
+                        float f = 0.0f;
+                        if (gl) f = __fmul_rn(__fmul_rn(__int2float_rn(dot64(wa[u], wb[u], xa[t], xb[t])), wsc[u]), xsc[t]);
+                        tw[(r + u) * TB + t][lane] = f;
+                    }
+            }
+            if (r < rmax) {
+                const int64_t row = i0 + r;
+                U8 wa, wb;
+                float wsc = 0.0f;
+                if (gl) {
+                    wa = ld_nc_v8(wq + row * n + int64_t(g) * GS);
+                    wb = ld_nc_v8(wq + row * n + int64_t(g) * GS + 32);
+                    wsc = ws[row * G + g];
+                }
+#pragma unroll
+                for (int t = 0; t < TB; ++t) {
+                    float f = 0.0f;
+                    if (gl) f = __fmul_rn(__fmul_rn(__int2float_rn(dot64(wa, wb, xa[t], xb[t])), wsc), xsc[t]);
+                    tw[r * TB + t][lane] = f;
+                }
+            }
+            __syncwarp();
+            if (lane < slots) {
+                const int gc = G - g0 < 32 ? G - g0 : 32;
+                const float *row = tw[lane];
+#pragma unroll 8
+                for (int j = 0; j < gc; ++j) val = __fadd_rn(val, row[j]);   // group order
+            }
+            __syncwarp();
+        }
+        if (lane < slots) {
+            const int i = i0 + lane / TB, t = t0 + lane % TB;
+            if (i < d && t < B) out[int64_t(t) * d + i] = val;
+        }
+    }
+}
+
+template <int TB>
+static cudaError_t launch_mm_t(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
+                               int d, float *out, cudaStream_t stream, int sms) {
+    const int ntb = (B + TB - 1) / TB;
+    // Rows per tile: enough jobs for ~16 warps per SM, at most 32 / TB (one lane per (row, token)).
+    const int64_t want = int64_t(sms) * 16;
+    int64_t rb = (int64_t(d) * ntb + want - 1) / want;
+    if (rb < 1) rb = 1;
+    if (rb > 32 / TB) rb = 32 / TB;
+    const int RB = int(rb);
+    const int64_t jobs = int64_t((d + RB - 1) / RB) * ntb;
+    int64_t grid = (jobs + MM_WARPS - 1) / MM_WARPS;
+    if (grid > int64_t(sms) * 8) grid = int64_t(sms) * 8;
+    matmul_q8_kernel<TB><<<unsigned(grid), MM_THREADS, 0, stream>>>(xq, xs, B, wq, ws, n, d, RB, out);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
+                             int d, float *out, cudaStream_t stream, int sms) {
+    if (B == 0 || d == 0) return cudaSuccess;
+    if (B == 1) return launch_mm_t<1>(xq, xs, B, wq, ws, n, d, out, stream, sms);
+    if (B == 2) return launch_mm_t<2>(xq, xs, B, wq, ws, n, d, out, stream, sms);
+    return launch_mm_t<4>(xq, xs, B, wq, ws, n, d, out, stream, sms);
+}
+
+}  // namespace q3

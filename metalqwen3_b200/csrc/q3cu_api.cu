@@ -134,6 +134,7 @@ q3cu_status grow_scratch(q3cu_ctx *ctx, size_t bytes) {
 }
 
 size_t up16(size_t b) { return (b + 15) & ~size_t(15); }
+size_t up32(size_t b) { return (b + 31) & ~size_t(31); }
 
 }  // namespace
 
@@ -414,6 +415,19 @@ q3cu_status q3cu_embed_gather(q3cu_ctx *ctx, const int8_t *tq, const float *ts, 
                     "embed_gather launch");
 }
 
+q3cu_status q3cu_matmul_q8(q3cu_ctx *ctx, const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws,
+                           int n, int d, float *out, q3cu_stream stream) {
+    CHECK_CTX(ctx);
+    if (B < 0 || n <= 0 || d < 0) return fail(Q3CU_ERR_INVALID, "B=%d n=%d d=%d", B, n, d);
+    if (n % Q3CU_GROUP_SIZE) return fail(Q3CU_ERR_GROUP, "n %d is not a multiple of 64", n);
+    if (B > 0 && d > 0 && (!xq || !xs || !wq || !ws || !out)) return fail(Q3CU_ERR_INVALID, "NULL pointer");
+    if (!aligned(xq, 32) || !aligned(wq, 32) || !aligned(xs, 4) || !aligned(ws, 4) || !aligned(out, 4))
+        return fail(Q3CU_ERR_ALIGN, "xq and wq must be 32-byte aligned, xs, ws and out 4-byte aligned");
+    if (q3cu_status st = use_device(ctx)) return st;
+    return launched(q3::launch_matmul_q8(xq, xs, B, wq, ws, n, d, out, static_cast<cudaStream_t>(stream), ctx->sms),
+                    "matmul_q8 launch");
+}
+
 // ---------------------------------------------------------------------------
 // host-pointer drop-in wrappers (synchronous)
 // ---------------------------------------------------------------------------
@@ -533,6 +547,34 @@ q3cu_status q3cu_execute_quantize(q3cu_ctx *ctx, int8_t *q, float *s, const floa
     TRY_CUDA(q3::launch_quantize_q8(dx, Q3CU_F32, m, dq, ds, ctx->stream, ctx->sms), "quantize");
     TRY_CUDA(cudaMemcpyAsync(q, dq, size_t(m), cudaMemcpyDeviceToHost, ctx->stream), "D2H");
     TRY_CUDA(cudaMemcpyAsync(s, ds, size_t(groups) * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
+    return finish(ctx);
+}
+
+q3cu_status q3cu_execute_quantized_matmul(q3cu_ctx *ctx, float *output, const int8_t *x_q, const float *x_s,
+                                          const int8_t *w_q, const float *w_s, int n, int d, int group_size) {
+    CHECK_CTX(ctx);
+    if (!output || !x_q || !x_s || !w_q || !w_s || n <= 0 || d < 0)
+        return fail(Q3CU_ERR_INVALID, "executeQuantizedMatMul: bad argument");
+    if (group_size != Q3CU_GROUP_SIZE || n % Q3CU_GROUP_SIZE)
+        return fail(Q3CU_ERR_GROUP, "group_size %d / n %d: only 64-element groups are supported", group_size, n);
+    if (d == 0) return Q3CU_OK;
+    if (q3cu_status st = use_device(ctx)) return st;
+    const int g = n / Q3CU_GROUP_SIZE;
+    const size_t xqb = up32(size_t(n)), xsb = up32(size_t(g) * 4), wqb = up32(size_t(d) * n),
+                 wsb = up32(size_t(d) * g * 4);
+    if (q3cu_status st = grow_scratch(ctx, xqb + xsb + wqb + wsb + size_t(d) * 4)) return st;
+    auto *p = static_cast<uint8_t *>(ctx->d_scratch);
+    int8_t *dxq = reinterpret_cast<int8_t *>(p);
+    float *dxs = reinterpret_cast<float *>(p + xqb);
+    int8_t *dwq = reinterpret_cast<int8_t *>(p + xqb + xsb);
+    float *dws = reinterpret_cast<float *>(p + xqb + xsb + wqb);
+    float *dout = reinterpret_cast<float *>(p + xqb + xsb + wqb + wsb);
+    TRY_CUDA(cudaMemcpyAsync(dxq, x_q, size_t(n), cudaMemcpyHostToDevice, ctx->stream), "H2D");
+    TRY_CUDA(cudaMemcpyAsync(dxs, x_s, size_t(g) * 4, cudaMemcpyHostToDevice, ctx->stream), "H2D");
+    TRY_CUDA(cudaMemcpyAsync(dwq, w_q, size_t(d) * n, cudaMemcpyHostToDevice, ctx->stream), "H2D");
+    TRY_CUDA(cudaMemcpyAsync(dws, w_s, size_t(d) * g * 4, cudaMemcpyHostToDevice, ctx->stream), "H2D");
+    TRY_CUDA(q3::launch_matmul_q8(dxq, dxs, 1, dwq, dws, n, d, dout, ctx->stream, ctx->sms), "matmul");
+    TRY_CUDA(cudaMemcpyAsync(output, dout, size_t(d) * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
     return finish(ctx);
 }
 

@@ -34,6 +34,9 @@ cudaError_t launch_qk_norm_rope(void *q, void *k, q3cu_dtype dt, const int32_t *
                                 int n_kv, const float *q_norm, const float *k_norm, const InvFreq &inv_freq,
                                 float eps, uint32_t *status, cudaStream_t stream, int sms);
 
+cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
+                             int d, float *out, cudaStream_t stream, int sms);
+
 cudaError_t launch_swiglu(const void *hb, const void *hb2, q3cu_dtype dt, int64_t elems, void *out, int8_t *q,
                           float *s, cudaStream_t stream, int sms);
 

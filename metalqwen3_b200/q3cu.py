@@ -64,6 +64,8 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
                 "q3cu_quantize_q8": (st, [vp, vp, i32, i64, i32, vp, vp, vp]),
                 "q3cu_dequantize_q8": (st, [vp, vp, vp, i64, vp, vp]),
                 "q3cu_embed_gather": (st, [vp, vp, vp, i32, i32, vp, i64, vp, vp, vp, vp]),
+                "q3cu_matmul_q8": (st, [vp, vp, vp, i32, vp, vp, i32, i32, vp, vp]),
+                "q3cu_execute_quantized_matmul": (st, [vp, vp, vp, vp, vp, vp, i32, i32, i32]),
                 "q3cu_execute_rmsnorm": (st, [vp, vp, vp, vp, i32]),
                 "q3cu_execute_softmax": (st, [vp, vp, i32]),
                 "q3cu_execute_swiglu": (st, [vp, vp, vp, i32]),
@@ -210,6 +212,17 @@ class Q3CU:
                     "q3cu_embed_gather")
         return out, oq, os_
 
+    def matmul_q8(self, xq, xs, wq, ws, out=None, stream=None):
+        """out[b] = W @ x[b] for Q8_0 x (xq [B][n], xs [B][n/64]) and W (wq [d][n], ws [d][n/64])."""
+        B, n = xq.shape
+        d = wq.shape[0]
+        if wq.shape[1] != n:
+            raise ValueError(f"W is {tuple(wq.shape)}, x rows have {n} elements")
+        out = self.torch.empty((B, d), dtype=self.torch.float32, device=xq.device) if out is None else out
+        self._check(self.lib.q3cu_matmul_q8(self.ctx, _ptr(xq), _ptr(xs), B, _ptr(wq), _ptr(ws), n, d, _ptr(out),
+                                            self._stream(stream)), "q3cu_matmul_q8")
+        return out
+
     # -- host-pointer drop-in (numpy arrays, synchronous) -----------------------
     def execute_rmsnorm(self, out, inp, w):
         self._check(self.lib.q3cu_execute_rmsnorm(self.ctx, _ptr(out), _ptr(inp), _ptr(w), inp.size), "executeRMSNorm")
@@ -226,6 +239,10 @@ class Q3CU:
 
     def execute_quantize(self, q, s, x):
         self._check(self.lib.q3cu_execute_quantize(self.ctx, _ptr(q), _ptr(s), _ptr(x), x.size), "executeQuantize")
+
+    def execute_quantized_matmul(self, out, xq, xs, wq, ws, n, d, group_size=GS):
+        self._check(self.lib.q3cu_execute_quantized_matmul(self.ctx, _ptr(out), _ptr(xq), _ptr(xs), _ptr(wq), _ptr(ws),
+                                                           n, d, group_size), "executeQuantizedMatMul")
 
     def execute_embedding(self, out, tq, ts, token, dim):
         self._check(self.lib.q3cu_execute_embedding(self.ctx, _ptr(out), _ptr(tq), _ptr(ts), token, dim),

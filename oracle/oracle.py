@@ -115,6 +115,19 @@ class Oracle:
         self.lib.q3o_swiglu(_p(hb), _p(np.ascontiguousarray(hb2, np.float32)), hb.size)
         return hb
 
+    def matmul(self, xq, xs, wq, ws):
+        """qwen3_original.c:310-331 for each row of x: xq [B][n], xs [B][n/64]; wq [d][n], ws [d][n/64] -> [B][d]."""
+        xq = np.ascontiguousarray(np.atleast_2d(xq), np.int8)
+        xs = np.ascontiguousarray(np.atleast_2d(xs), np.float32)
+        wq = np.ascontiguousarray(wq, np.int8)
+        ws = np.ascontiguousarray(ws, np.float32)
+        B, n = xq.shape
+        d = wq.shape[0]
+        out = np.empty((B, d), np.float32)
+        for b in range(B):
+            self.lib.q3o_matmul(_p(out[b]), _p(xq[b]), _p(xs[b]), _p(wq), _p(ws), n, d)
+        return out
+
     # ---- row-batched forms ------------------------------------------------
     @staticmethod
     def _dt(a):
@@ -258,6 +271,21 @@ class Reference:
         qt = _QT(q.ctypes.data, s.ctypes.data)
         self.lib.dequantize(C.byref(qt), _p(x), q.size)
         return x
+
+    def matmul(self, xq, xs, wq, ws):
+        """The reference's own `matmul` (OpenMP over output rows) for each row of x."""
+        xq = np.ascontiguousarray(np.atleast_2d(xq), np.int8)
+        xs = np.ascontiguousarray(np.atleast_2d(xs), np.float32)
+        wq = np.ascontiguousarray(wq, np.int8)
+        ws = np.ascontiguousarray(ws, np.float32)
+        B, n = xq.shape
+        d = wq.shape[0]
+        out = np.empty((B, d), np.float32)
+        wt = _QT(wq.ctypes.data, ws.ctypes.data)
+        for b in range(B):
+            xt = _QT(xq[b].ctypes.data, xs[b].ctypes.data)
+            self.lib.matmul(_p(out[b]), C.byref(xt), C.byref(wt), n, d)
+        return out
 
     # ---- whole decode step --------------------------------------------------
     def create(self, checkpoint_path: str, ctx_length: int = 0):

@@ -9,6 +9,9 @@ and stores inputs and outputs:
   primitives.npz    vectors of length 64..10240 (incl. the Q8_0 edge cases:
                     denormal groups, wrapped codes, inf/NaN, -0, exact .5
                     quotients) -> rmsnorm / softmax / quantize / dequantize
+  matmul.npz        Q8_0 x Q8_0 matrix-vector products (`matmul`) on seeded
+                    codes/scales, incl. extreme codes (-128, +-127), zero and
+                    huge scales (inf outputs) and n = 64..1024
   forward_tiny.npz  a seeded 2-layer checkpoint (oracle/checkpoint.py, sha256
                     recorded) run for 8 positions: logits, and the RunState the
                     reference leaves behind (rotated q, SwiGLU output, softmax
@@ -72,6 +75,23 @@ def main():
             out[f"deq{i}"] = ref.dequantize(q, s)
     out["count"] = np.array(len(vecs))
     np.savez_compressed(os.path.join(HERE, "primitives.npz"), **out)
+
+    mm = {}
+    cases = [(64, 5), (128, 64), (1024, 96), (576, 33)]
+    for i, (n, d) in enumerate(cases):
+        xq = rng.integers(-127, 128, n, dtype=np.int8)
+        xs = np.abs(0.05 * rng.standard_normal(n // 64)).astype(np.float32)
+        wq = rng.integers(-127, 128, (d, n), dtype=np.int8)
+        ws = np.abs(0.01 * rng.standard_normal((d, n // 64))).astype(np.float32)
+        if i == 3:                                           # extremes
+            xq[:64], wq[0, :64], wq[1, :64] = -128, -128, 127
+            ws[2, :] = 0.0
+            ws[3, 0], xs[0] = 3e38, 3e38                     # overflows to inf
+        mm[f"xq{i}"], mm[f"xs{i}"], mm[f"wq{i}"], mm[f"ws{i}"] = xq, xs, wq, ws
+        with np.errstate(all="ignore"):
+            mm[f"out{i}"] = ref.matmul(xq, xs, wq, ws)[0]
+    mm["count"] = np.array(len(cases))
+    np.savez_compressed(os.path.join(HERE, "matmul.npz"), **mm)
 
     fw = {}
     with tempfile.TemporaryDirectory() as d:

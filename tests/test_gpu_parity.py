@@ -523,3 +523,66 @@ def test_execute_dropin(q3, oracle):
     out = np.empty(1024, np.float32)
     q3.execute_embedding(out, tq, ts, 17, 1024)
     assert np.array_equal(bits(out), bits(oracle.dequantize(tq[17], ts[17])))
+
+
+# --------------------------------------------------------------------------- Q8_0 matmul
+def same_bits(a, b):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    na, nb = np.isnan(a), np.isnan(b)
+    return a.shape == b.shape and np.array_equal(na, nb) and np.array_equal(bits(a[~na]), bits(b[~nb]))
+
+
+def q8_operands(rng, B, n, d, extremes=False):
+    """x codes / scales in the range quantize produces, W codes uniform in
+    [-127, 127] with |N(0, 0.01)| group scales (the exporter's range)."""
+    xq = rng.integers(-127, 128, (B, n), dtype=np.int8)
+    xs = np.abs(0.05 * rng.standard_normal((B, n // 64))).astype(np.float32)
+    wq = rng.integers(-127, 128, (d, n), dtype=np.int8)
+    ws = np.abs(0.01 * rng.standard_normal((d, n // 64))).astype(np.float32)
+    if extremes:
+        xq[:, :64], wq[0, :64], wq[1, :64] = -128, -128, 127
+        ws[2, :] = 0.0
+        ws[3, 0], xs[:, 0] = 3e38, 3e38
+        ws[4, 1], xs[:, 1] = np.inf, 0.0
+    return xq, xs, wq, ws
+
+
+# Qwen3-0.6B's matmul shapes (wq, wk/wv, wo, w1/w3, w2), an 8B-sized square one,
+# odd row counts, 1..7 token rows (ragged blocks of 4), n from one group up.
+@pytest.mark.parametrize("B,n,d", [(1, 1024, 2048), (1, 1024, 1024), (1, 2048, 1024), (1, 1024, 3072),
+                                   (1, 3072, 1024), (2, 4096, 4096), (3, 2560, 9728), (4, 64, 5),
+                                   (5, 1088, 333), (7, 9728, 77)])
+def test_matmul_q8(q3, oracle, B, n, d):
+    xq, xs, wq, ws = q8_operands(np.random.default_rng(B * 7 + n + d), B, n, d)
+    g = host(q3.matmul_q8(dev(xq), dev(xs), dev(wq), dev(ws)))
+    assert same_bits(g, oracle.matmul(xq, xs, wq, ws))
+
+
+def test_matmul_q8_extremes_and_golden(q3, oracle):
+    xq, xs, wq, ws = q8_operands(np.random.default_rng(5), 3, 576, 40, extremes=True)
+    with np.errstate(all="ignore"):
+        assert same_bits(host(q3.matmul_q8(dev(xq), dev(xs), dev(wq), dev(ws))), oracle.matmul(xq, xs, wq, ws))
+    import os
+    g = np.load(os.path.join(os.path.dirname(__file__), "golden", "matmul.npz"))
+    for i in range(int(g["count"])):
+        out = host(q3.matmul_q8(dev(g[f"xq{i}"][None]), dev(g[f"xs{i}"][None]), dev(g[f"wq{i}"]), dev(g[f"ws{i}"])))
+        assert same_bits(out[0], g[f"out{i}"]), f"golden case {i}"
+
+
+def test_matmul_q8_classifier(q3, oracle):
+    """The 0.6B classifier: 151,936 x 1024 (155 MB of codes), one token."""
+    xq, xs, wq, ws = q8_operands(np.random.default_rng(11), 1, 1024, 151936)
+    g = host(q3.matmul_q8(dev(xq), dev(xs), dev(wq), dev(ws)))
+    assert same_bits(g, oracle.matmul(xq, xs, wq, ws))
+
+
+def test_execute_quantized_matmul(q3, oracle):
+    """MetalContext::executeQuantizedMatMul drop-in (host pointers)."""
+    xq, xs, wq, ws = q8_operands(np.random.default_rng(12), 1, 2048, 1024)
+    out = np.empty(1024, np.float32)
+    q3.execute_quantized_matmul(out, xq[0], xs[0], wq, ws, 2048, 1024)
+    assert same_bits(out, oracle.matmul(xq, xs, wq, ws)[0])
+    from metalqwen3_b200.q3cu import Q3Error
+    with pytest.raises(Q3Error) as e:
+        q3.execute_quantized_matmul(out, xq[0], xs[0], wq, ws, 2048, 1024, group_size=32)
+    assert e.value.status == 3                       # ERR_GROUP

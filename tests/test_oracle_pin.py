@@ -61,6 +61,34 @@ def test_quantize_edge_cases_vs_reference(oracle, reference):
     assert (qb[192:256] == 0).all()                   # scale underflowed to 0 -> x/0 -> 0
 
 
+def same_bits(a, b):
+    """Bit-identical, except that any two NaNs compare equal (payloads differ between builds)."""
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    na, nb = np.isnan(a), np.isnan(b)
+    return a.shape == b.shape and np.array_equal(na, nb) and np.array_equal(u32(a[~na]), u32(b[~nb]))
+
+
+def matmul_case(rng, B, n, d, extremes=False):
+    xq = rng.integers(-127, 128, (B, n), dtype=np.int8)
+    xs = np.abs(0.05 * rng.standard_normal((B, n // 64))).astype(np.float32)
+    wq = rng.integers(-127, 128, (d, n), dtype=np.int8)
+    ws = np.abs(0.01 * rng.standard_normal((d, n // 64))).astype(np.float32)
+    if extremes:
+        xq[:, :64], wq[0, :64], wq[1, :64] = -128, -128, 127
+        ws[2, :] = 0.0
+        ws[3, 0], xs[:, 0] = 3e38, 3e38                 # inf
+        ws[4, 1], xs[:, 1] = np.inf, 0.0                # inf * 0 = NaN
+    return xq, xs, wq, ws
+
+
+@pytest.mark.parametrize("B,n,d,ext", [(1, 64, 7, False), (2, 1024, 300, False), (1, 3072, 64, False),
+                                       (3, 576, 40, True)])
+def test_matmul_vs_reference(oracle, reference, B, n, d, ext):
+    xq, xs, wq, ws = matmul_case(np.random.default_rng(n + d), B, n, d, ext)
+    with np.errstate(all="ignore"):
+        assert same_bits(oracle.matmul(xq, xs, wq, ws), reference.matmul(xq, xs, wq, ws))
+
+
 def test_softmax_edges_vs_reference(oracle, reference):
     for x in (np.full(40, -3.0, np.float32), np.full(40, -200.0, np.float32), np.array([0.0], np.float32),
               np.array([np.nan, 1.0, 2.0], np.float32), np.array([88.0, 89.0, -1e30], np.float32)):
@@ -122,6 +150,14 @@ def test_golden_primitives(oracle):
         q, s = oracle.quantize(x)
         assert np.array_equal(q, g[f"q{i}"]) and np.array_equal(u32(s), u32(g[f"s{i}"]))
         assert np.array_equal(u32(oracle.dequantize(q, s)), u32(g[f"deq{i}"]))
+
+
+def test_golden_matmul(oracle):
+    g = load_golden("matmul.npz")
+    for i in range(int(g["count"])):
+        with np.errstate(all="ignore"):
+            o = oracle.matmul(g[f"xq{i}"], g[f"xs{i}"], g[f"wq{i}"], g[f"ws{i}"])[0]
+        assert same_bits(o, g[f"out{i}"]), f"case {i}"
 
 
 def test_golden_forward(oracle):
