@@ -87,120 +87,84 @@ __device__ __forceinline__ float swiglu_exact(float a, float b, const ExpTab &ta
     const float ex = expf_host(-a, tab);
     return __fmul_rn(a, __fmul_rn(b, __frcp_rn(__fadd_rn(1.0f, ex))));
 }
-// The same, with the host-identical expf evaluated on the table in constant
-// memory (out of line: the fast path's rare exit).
-static __device__ __noinline__ float swiglu_exact2(float a, float b) {
-    const float ex = q3_expf_tab(-a, c_exp_tab);
-    return __fmul_rn(a, __fmul_rn(b, __frcp_rn(__fadd_rn(1.0f, ex))));
-}
 
 // Main kernel: 32 bytes of hb and hb2 per lane per step (8 f32 / 16 bf16), so a
 // 64-group spans 8 / 4 lanes.  Per element: the expf core (binary64, branch
-// free, one 8-byte table read), then 1/(1+e) by a rcp.approx seed and one
-// Markstein correction step (rcp_rn_1to2p120: correctly rounded for
-// 1 <= d < 2^120, checked against __frcp_rn on every such d), and the two
-// products, element pairs in packed f32x2 arithmetic.  A lane whose largest
-// |a| is >= 83 (or NaN) recomputes its values with swiglu_exact2 before the
-// group reduction; codes come from q8_encode_lane.  Full steps (every lane's
-// elements in range: all but possibly the array's last step) run without
-// per-lane bounds checks.
-template <typename T, bool Q8>
-__device__ __forceinline__ void swiglu_lane(const U8 &ra, const U8 &rb, const ExpTab2 &tab, float (&o)[Wide<T>::N]) {
-    constexpr int N = Wide<T>::N;
-    float a[N], b[N];
-    Wide<T>::widen(ra, a);
-    Wide<T>::widen(rb, b);
-    // |a| < 83 keeps -a off expf's special inputs (|x| >= 88, NaN, inf) and
-    // d = 1 + e^-a inside [1, 2^120), where rcp_rn_1to2p120's one correction
-    // step is exact.  nd = -1 - e is -d exactly (round-to-nearest is
-    // symmetric), so d's negation costs nothing.
-    float amax = 0.0f;                               // NaN if any a is NaN
-    const f2 NEG1 = pk2(-1.0f, -1.0f), ONE = pk2(1.0f, 1.0f);
-#pragma unroll
-    for (int i = 0; i < N; i += 2) {
-        amax = max3_nan(amax, fabsf(a[i]), fabsf(a[i + 1]));
-        const f2 nd = sub2(NEG1, pk2(expf_core2(-a[i], tab), expf_core2(-a[i + 1], tab)));
-        float nd0, nd1;
-        up2(nd, nd0, nd1);
-        const f2 y0 = pk2(rcp_approx(-nd0), rcp_approx(-nd1));
-        const f2 y = fma2(y0, fma2(nd, y0, ONE), y0);      // y0 + y0*(1 - d*y0)
-        up2(mul2(pk2(a[i], a[i + 1]), mul2(pk2(b[i], b[i + 1]), y)), o[i], o[i + 1]);
-    }
-    if (__builtin_expect(!(amax < 83.0f), 0)) {
-#pragma unroll
-        for (int i = 0; i < N; ++i) o[i] = swiglu_exact2(a[i], b[i]);
-    }
-}
-
+// free), then 1/(1+e) by a rcp.approx seed and one Markstein correction step
+// (rcp_rn_1to2p120: correctly rounded for 1 <= d < 2^120, checked against
+// __frcp_rn on every such d), and the two products, element pairs in packed
+// f32x2 arithmetic.  Lanes holding an |a| >= 83 (or NaN) recompute their values
+// with swiglu_exact before the group reduction; codes come from q8_encode_lane.
 template <typename T, int U, bool Q8>
 __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 3 : 2) swiglu_v8_kernel(const T *hb, const T *__restrict__ hb2, int64_t elems,
                                                         T *out, int8_t *__restrict__ q, float *__restrict__ s) {
     constexpr int N = Wide<T>::N;
     constexpr int LPG = GS / N;
     constexpr int STEP = 32 * N;
-    __shared__ ExpTab2 s_tab;
+    __shared__ ExpTab s_tab;
     load_exp_table(s_tab);
     __syncthreads();
 
     const int lane = threadIdx.x & 31;
     const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
     const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
-    const int64_t nfull = elems / STEP;                  // steps with every lane in range
-    const int64_t nsteps = nfull + ((elems % STEP) != 0);
-
-    auto emit = [&](int64_t e, const float (&o)[N], bool ok) {
-        if constexpr (Q8) {
-            uint32_t codes[N / 4];
-            const float scale = q8_encode_lane<N, LPG>(o, codes);   // every lane joins the group shuffles
-            if (ok) {
-                if constexpr (N == 8) st_cs_v2(q + e, make_uint2(codes[0], codes[1]));
-                else st_cs_v4(q + e, make_uint4(codes[0], codes[1], codes[2], codes[3]));
-            }
-            st_cs_f32_if(ok && (lane % LPG) == 0, s + (e >> 6), scale);
-        } else {
-            if (ok) st_cs_v8(out + e, Wide<T>::narrow(o));
-        }
-    };
+    const int64_t nsteps = elems / STEP + ((elems % STEP) != 0);
 
     for (int64_t st0 = warp * U; st0 < nsteps; st0 += nwarps * U) {
         const int64_t e0 = st0 * STEP + lane * N;
         U8 ra[U], rb[U];
-        if (st0 + U <= nfull) {                          // warp-uniform: U full steps
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                ra[u] = ld_v8(hb + e0 + int64_t(u) * STEP);          // coherent: out may alias hb
-                rb[u] = ld_nc_v8(hb2 + e0 + int64_t(u) * STEP);
-            }
-#pragma unroll
-            for (int u = 0; u < U; ++u) {
-                float o[N];
-                swiglu_lane<T, Q8>(ra[u], rb[u], s_tab, o);
-                emit(e0 + int64_t(u) * STEP, o, true);
-            }
-            continue;
-        }
-        // The array's last steps: per-lane bounds.
 #pragma unroll
         for (int u = 0; u < U; ++u) {
             const int64_t e = e0 + int64_t(u) * STEP;
             if (e < elems) {
-                ra[u] = ld_v8(hb + e);
+                ra[u] = ld_v8(hb + e);               // coherent: out may alias hb
                 rb[u] = ld_nc_v8(hb2 + e);
             }
         }
 #pragma unroll
         for (int u = 0; u < U; ++u) {
-            if (st0 + u >= nsteps) break;                // warp-uniform
+            if (st0 + u >= nsteps) break;            // warp-uniform
             const int64_t e = e0 + int64_t(u) * STEP;
             const bool ok = e < elems;
             float o[N];
             if (ok) {
-                swiglu_lane<T, Q8>(ra[u], rb[u], s_tab, o);
+                float a[N], b[N];
+                Wide<T>::widen(ra[u], a);
+                Wide<T>::widen(rb[u], b);
+                // |a| < 83 keeps -a off expf's special inputs (|x| >= 88, NaN, inf) and
+                // d = 1 + e^-a inside [1, 2^120), where rcp_rn_1to2p120's one correction
+                // step is exact.  Pairs use packed f32x2 arithmetic; nd = -1 - e is -d
+                // exactly (round-to-nearest is symmetric), so d's negation costs nothing.
+                bool slow = false;
+                const f2 NEG1 = pk2(-1.0f, -1.0f), ONE = pk2(1.0f, 1.0f);
+#pragma unroll
+                for (int i = 0; i < N; i += 2) {
+                    slow |= !(fabsf(a[i]) < 83.0f) | !(fabsf(a[i + 1]) < 83.0f);
+                    const f2 nd = sub2(NEG1, pk2(expf_core(-a[i], s_tab), expf_core(-a[i + 1], s_tab)));
+                    float nd0, nd1;
+                    up2(nd, nd0, nd1);
+                    const f2 y0 = pk2(rcp_approx(-nd0), rcp_approx(-nd1));
+                    const f2 y = fma2(y0, fma2(nd, y0, ONE), y0);      // y0 + y0*(1 - d*y0)
+                    up2(mul2(pk2(a[i], a[i + 1]), mul2(pk2(b[i], b[i + 1]), y)), o[i], o[i + 1]);
+                }
+                if (__builtin_expect(slow, 0)) {
+#pragma unroll
+                    for (int i = 0; i < N; ++i) o[i] = swiglu_exact(a[i], b[i], s_tab);
+                }
             } else {
 #pragma unroll
                 for (int i = 0; i < N; ++i) o[i] = 0.0f;
             }
-            emit(e, o, ok);
+            if constexpr (Q8) {
+                uint32_t codes[N / 4];
+                const float scale = q8_encode_lane<N, LPG>(o, codes);
+                if (!ok) continue;
+                if constexpr (N == 8) st_cs_v2(q + e, make_uint2(codes[0], codes[1]));
+                else st_cs_v4(q + e, make_uint4(codes[0], codes[1], codes[2], codes[3]));
+                if ((lane % LPG) == 0) st_cs_f32(s + (e >> 6), scale);
+            } else {
+                if (ok) st_cs_v8(out + e, Wide<T>::narrow(o));
+            }
         }
     }
 }

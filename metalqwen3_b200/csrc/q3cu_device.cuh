@@ -70,17 +70,6 @@ __device__ __forceinline__ void st_cs_u32(void *p, uint32_t v) {
 __device__ __forceinline__ void st_cs_f32(float *p, float v) {
     asm volatile("st.global.cs.f32 [%0], %1;" :: "l"(p), "f"(v) : "memory");
 }
-// The same store, made only if `pred` (a predicated instruction, no branch).
-__device__ __forceinline__ void st_cs_f32_if(bool pred, float *p, float v) {
-    asm volatile("{\n\t.reg .pred q;\n\tsetp.ne.u32 q, %2, 0;\n\t@q st.global.cs.f32 [%0], %1;\n\t}"
-                 :: "l"(p), "f"(v), "r"(uint32_t(pred)) : "memory");
-}
-// max(a, b, c) that returns NaN if any operand is NaN (one instruction on sm_100).
-__device__ __forceinline__ float max3_nan(float a, float b, float c) {
-    float r;
-    asm("max.NaN.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
-    return r;
-}
 
 __device__ __forceinline__ float4 u4_as_f4(uint4 u) {
     return make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
@@ -327,7 +316,7 @@ __device__ __forceinline__ float q8_encode_lane(const float *o, uint32_t *codes)
     if (__builtin_expect(exact_group, 0)) scale = q8_scale(m);
     const float inv = rcp_approx(scale);
     const f2 inv2 = pk2(inv, inv), M2 = pk2(12582912.0f, 12582912.0f);
-    float dmax = 0.0f;                       // largest distance to the nearest integer; NaN if any is NaN
+    bool fix = exact_group;
     uint32_t tb[N];
 #pragma unroll
     for (int i = 0; i < N; i += 2) {
@@ -337,11 +326,10 @@ __device__ __forceinline__ float q8_encode_lane(const float *o, uint32_t *codes)
         float d0, d1, t0, t1;
         up2(d, d0, d1);
         up2(t, t0, t1);
-        dmax = max3_nan(dmax, fabsf(d0), fabsf(d1));
+        fix |= !(fabsf(d0) <= 0.49993896484375f) | !(fabsf(d1) <= 0.49993896484375f);
         tb[i] = __float_as_uint(t0);
         tb[i + 1] = __float_as_uint(t1);
     }
-    const bool fix = exact_group || !(dmax <= 0.49993896484375f);
 #pragma unroll
     for (int w = 0; w < N / 4; ++w)
         codes[w] = __byte_perm(__byte_perm(tb[4 * w], tb[4 * w + 1], 0x0040),
@@ -375,35 +363,6 @@ __device__ __forceinline__ void load_exp_table(ExpTab &t) {
     }
 }
 __device__ __forceinline__ float expf_host(float x, const ExpTab &t) { return q3_expf_fast(x, t.hi, t.lo); }
-// The table with each entry as one 8-byte word (low, high): one shared-memory
-// read per exp instead of two.
-struct ExpTab2 {
-    uint2 e[32];
-};
-__device__ __forceinline__ void load_exp_table(ExpTab2 &t) {
-    if (threadIdx.x < 32) {
-        const uint64_t v = c_exp_tab[threadIdx.x];
-        t.e[threadIdx.x] = make_uint2(uint32_t(v), uint32_t(v >> 32));
-    }
-}
-// q3_expf_core (q3_expf.h) operation for operation, with the table entry read
-// as one word: the same binary64 steps, so the same bits (valid where
-// !q3_expf_special(x)).
-__device__ __forceinline__ float expf_core2(float x, const ExpTab2 &t) {
-    const double xd = double(x);
-    double kd = fma(Q3_EXP_INVLN2N, xd, Q3_EXP_SHIFT);
-    const uint32_t ki = uint32_t(__double2loint(kd));
-    kd -= Q3_EXP_SHIFT;
-    const double r = fma(Q3_EXP_INVLN2N, xd, -kd);
-    const uint2 e = t.e[ki & 31u];
-    const double sc = __hiloint2double(int(e.y + (ki << 15)), int(e.x));   // (ki << 47) reaches the high word only
-    const double z = fma(Q3_EXP_C0, r, Q3_EXP_C1);
-    const double r2 = r * r;
-    double y = fma(Q3_EXP_C2, r, 1.0);
-    y = fma(z, r2, y);
-    y = y * sc;
-    return float(y);
-}
 __device__ __forceinline__ float expf_core(float x, const ExpTab &t) { return q3_expf_core(x, t.hi, t.lo); }
 
 // exp(d) for -80 <= d <= 0, where only accuracy is required (softmax: 1e-5
