@@ -4,7 +4,8 @@
 
 Workloads: prefill4b (default: the headline line), decode8b, embed, prefill14b,
 decode06b (one Qwen3-0.6B decode token through 28 layers of the path's ops,
-timed eagerly and as CUDA graphs: microseconds per op and per layer).
+timed eagerly and as CUDA graphs: microseconds per op and per layer), matmul06b
+(one Qwen3-0.6B decode token's Q8_0 matmuls, 113 launches replayed as a graph).
 
 A step is one pass of the layer's memory-bound kernels over one batch of
 token rows already resident in HBM.  Default workload `prefill4b`: the
@@ -575,8 +576,113 @@ class Decode06B(Workload):
         return self.total_bytes()
 
 
+class Matmul06B(Workload):
+    """Qwen3-0.6B decode-token Q8_0 matmuls (qwen3_original.c:357-359, :432,
+    :444-445, :454, :466), T token rows (1: one decode token): per layer the
+    Q/K/V projections as one concatenated [2048+1024+1024][1024] matrix (they
+    share their input), wo [1024][2048], W1|W3 as one [6144][1024], w2
+    [1024][3072]; then the classifier [151936][1024] (the shared token table).
+    28 layers + 1 = 113 launches per step, replayed as one CUDA graph.
+    Weights: codes uniform in [-127, 127], scales |N(0, 0.01)| (the exporter's
+    ranges); each matmul reads its own seeded activation codes.  HBM-bound in
+    principle (633 MB of weights per token), latency-bound per launch at this
+    model size."""
+    name = "matmul06b"
+    dtype = "int8 codes (dp4a, exact int32) -> f32"
+
+    def __init__(self, tokens=1, dim=1024, nh=16, nkv=8, hd=128, hidden=3072, layers=28, vocab=151936):
+        self.tokens, self.dim, self.layers, self.vocab = tokens, dim, layers, vocab
+        A, K = nh * hd, nkv * hd
+        self.shapes = [("qkv", dim, A + 2 * K), ("wo", A, dim), ("w13", dim, 2 * hidden), ("w2", hidden, dim)]
+
+    def _mats(self):
+        return [(f"{nm}{l}", n, d) for l in range(self.layers) for nm, n, d in self.shapes] + \
+               [("cls", self.dim, self.vocab)]
+
+    def kernels(self):
+        B = self.tokens
+        b = sum(d * n + d * n // 16 + B * (n + n // 16) + 4 * B * d for _, n, d in self._mats())
+        return [("matmul_q8", b)]
+
+    def config(self):
+        return {"workload": "Qwen3-0.6B decode-token Q8_0 matmuls (28 layers: QKV, wo, W1|W3, w2; classifier)",
+                "tokens_per_gpu": self.tokens, "dim": self.dim, "layers": self.layers, "vocab": self.vocab,
+                "launches_per_step": len(self._mats()), "weights": "codes uniform [-127,127], scales |N(0,0.01)|",
+                "launch": "one CUDA graph replay per step"}
+
+    def make(self, torch, dev, seed):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        B = self.tokens
+        d = {}
+        for nm, n, m in self._mats():
+            d["wq_" + nm] = torch.randint(-127, 128, (m, n), dtype=torch.int8, device=dev, generator=g)
+            d["ws_" + nm] = (0.01 * torch.randn(m, n // GS, device=dev, generator=g)).abs()
+            d["xq_" + nm] = torch.randint(-127, 128, (B, n), dtype=torch.int8, device=dev, generator=g)
+            d["xs_" + nm] = (0.05 * torch.randn(B, n // GS, device=dev, generator=g)).abs()
+            d["o_" + nm] = torch.empty(B, m, device=dev)
+        self.h2d_keys = tuple(k for k in d if k.startswith(("xq_", "xs_")))
+        self.d2h_keys = tuple(k for k in d if k.startswith("o_"))
+        return d
+
+    def _replay(self, q3, d, stream):
+        import torch
+        key = (id(d), id(stream))
+        if getattr(self, "_gkey", None) != key:
+            mats = self._mats()
+            for nm, _, _ in mats:          # once eagerly (lazy init outside the capture)
+                q3.matmul_q8(d["xq_" + nm], d["xs_" + nm], d["wq_" + nm], d["ws_" + nm], out=d["o_" + nm], stream=stream)
+            stream.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                for nm, _, _ in mats:
+                    q3.matmul_q8(d["xq_" + nm], d["xs_" + nm], d["wq_" + nm], d["ws_" + nm], out=d["o_" + nm],
+                                 stream=stream)
+            self._graph, self._gkey = gr, key
+        self._graph.replay()
+        return len(self._mats())
+
+    def launch(self, q3, d, stream, events=None):
+        if events is not None:
+            n = self._replay(q3, d, stream)            # the graph exists before the first timed step
+            events[0][0].record(stream)
+            self._graph.replay()
+            events[0][1].record(stream)
+            return n
+        return self._replay(q3, d, stream)
+
+    def launch_e2e(self, q3, d, stream):
+        return self._replay(q3, d, stream)
+
+    def cpu_step(self, oracle, np, sample, threads, rng):
+        """One decode token's matmuls by the reference's own `matmul` (OpenMP over
+        output rows, its own pragma), on all host cores."""
+        if not hasattr(self, "_cpu"):
+            from oracle.oracle import Oracle, Reference
+            try:
+                self._mm = Reference().matmul
+            except Exception:
+                self._mm = Oracle().matmul
+            mats = {}
+            for nm, n, m in self.shapes + [("cls", self.dim, self.vocab)]:
+                mats[nm] = (rng.integers(-127, 128, (1, n), dtype=np.int8),
+                            np.abs(0.05 * rng.standard_normal((1, n // GS))).astype(np.float32),
+                            rng.integers(-127, 128, (m, n), dtype=np.int8),
+                            np.abs(0.01 * rng.standard_normal((m, n // GS))).astype(np.float32))
+            self._cpu = mats
+        for _ in range(self.layers):
+            for nm, _, _ in self.shapes:
+                self._mm(*self._cpu[nm])
+        self._mm(*self._cpu["cls"])
+
+    cpu_tokens = 1
+
+    def bytes_for_tokens(self, n):
+        return self.total_bytes() / self.tokens
+
+
 WORKLOADS = {"prefill4b": Prefill4B, "decode8b": Decode8B, "embed": Embed, "prefill14b": Prefill14B,
-             "decode06b": Decode06B}
+             "decode06b": Decode06B, "matmul06b": Matmul06B}
 
 
 # ---------------------------------------------------------------------------- clocks

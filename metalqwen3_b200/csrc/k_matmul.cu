@@ -20,7 +20,10 @@
 // terms go to a padded shared-memory transpose, and lane s = (row, token) then
 // adds its 32 terms to its running val in group order: the reference's
 // accumulation, so the outputs are its bits.  The codes of the lane's group for
-// the TB tokens stay in registers across the rows of the tile.
+// the TB tokens stay in registers across the rows of the tile.  Rows with
+// fewer than 32 groups share a pass: GL lanes per row (the group count
+// rounded up to a power of two), 32 / GL rows side by side, and U rows' loads
+// are in flight per lane.
 //
 // Cost: W is read once per block of TB tokens (TB <= 4), so for one to four
 // tokens the kernel streams W at HBM speed; larger batches re-read W per block
@@ -41,15 +44,20 @@ __device__ __forceinline__ int dot64(const U8 &a0, const U8 &a1, const U8 &b0, c
     return acc;
 }
 
-template <int TB>
+template <int TB, int U>
 __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__restrict__ xq,
                                                                const float *__restrict__ xs, int B,
                                                                const int8_t *__restrict__ wq,
                                                                const float *__restrict__ ws, int n, int d, int RB,
                                                                float *__restrict__ out) {
-    __shared__ float terms[MM_WARPS][32][33];      // [slot = row * TB + token][group], padded
+    __shared__ float terms[MM_WARPS][32][33];      // [slot = row * TB + token][group of the pass], padded
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int G = n / GS;                           // groups per row
+    // A pass covers GL consecutive groups (G rounded up to a power of two, at
+    // most 32) of RP = 32 / GL rows at once: lane = sub * GL + gi.
+    int GL = 1;
+    while (GL < G && GL < 32) GL <<= 1;
+    const int RP = 32 / GL, sub = lane / GL, gi = lane % GL;
     const int tiles = (d + RB - 1) / RB;
     const int ntb = (B + TB - 1) / TB;
     const int64_t jobs = int64_t(tiles) * ntb;
@@ -59,17 +67,17 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
     for (int64_t job = int64_t(blockIdx.x) * MM_WARPS + warp; job < jobs; job += int64_t(gridDim.x) * MM_WARPS) {
         const int tile = int(job % tiles), tb = int(job / tiles);
         const int i0 = tile * RB, t0 = tb * TB;
+        const int rmax = d - i0 < RB ? d - i0 : RB;
         float val = 0.0f;                           // lane s < slots: row i0 + s / TB, token t0 + s % TB
-        for (int g0 = 0; g0 < G; g0 += 32) {
-            const int g = g0 + lane;
+        for (int g0 = 0; g0 < G; g0 += GL) {
+            const int g = g0 + gi;
             const bool gl = g < G;
             U8 xa[TB], xb[TB];
             float xsc[TB];
 #pragma unroll
             for (int t = 0; t < TB; ++t) {
-                const bool tl = gl && t0 + t < B;
                 const int8_t *xp = xq + int64_t(t0 + t) * n + int64_t(g) * GS;
-                if (tl) {
+                if (gl && t0 + t < B) {
                     xa[t] = ld_nc_v8(xp);
                     xb[t] = ld_nc_v8(xp + 32);
                     xsc[t] = xs[int64_t(t0 + t) * G + g];
@@ -79,48 +87,39 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
                     xsc[t] = 0.0f;
                 }
             }
-            const int rmax = d - i0 < RB ? d - i0 : RB;
-            int r = 0;
-            for (; r + 1 < rmax; r += 2) {         // two rows' loads in flight
-                U8 wa[2], wb[2];
-                float wsc[2];
+            for (int r = 0; r < rmax; r += RP * U) {
+                U8 wa[U], wb[U];
+                float wsc[U];
+                bool ok[U];
 #pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const int64_t row = i0 + r + u;
-                    if (gl) {
+                for (int u = 0; u < U; ++u) {        // U rows' loads in flight
+                    const int rr = r + u * RP + sub;
+                    ok[u] = gl && rr < rmax;
+                    if (ok[u]) {
+                        const int64_t row = i0 + rr;
                         wa[u] = ld_nc_v8(wq + row * n + int64_t(g) * GS);
                         wb[u] = ld_nc_v8(wq + row * n + int64_t(g) * GS + 32);
                         wsc[u] = ws[row * G + g];
                     }
                 }
 #pragma unroll
-                for (int u = 0; u < 2; ++u)
+                for (int u = 0; u < U; ++u) {
+                    const int rr = r + u * RP + sub;
+                    if (rr < rmax) {
 #pragma unroll
-                    for (int t = 0; t < TB; ++t) {
-                        float f = 0.0f;
-                        if (gl) f = __fmul_rn(__fmul_rn(__int2float_rn(dot64(wa[u], wb[u], xa[t], xb[t])), wsc[u]), xsc[t]);
-                        tw[(r + u) * TB + t][lane] = f;
+                        for (int t = 0; t < TB; ++t) {
+                            float f = 0.0f;
+                            if (ok[u])
+                                f = __fmul_rn(__fmul_rn(__int2float_rn(dot64(wa[u], wb[u], xa[t], xb[t])), wsc[u]),
+                                              xsc[t]);
+                            tw[rr * TB + t][gi] = f;
+                        }
                     }
-            }
-            if (r < rmax) {
-                const int64_t row = i0 + r;
-                U8 wa, wb;
-                float wsc = 0.0f;
-                if (gl) {
-                    wa = ld_nc_v8(wq + row * n + int64_t(g) * GS);
-                    wb = ld_nc_v8(wq + row * n + int64_t(g) * GS + 32);
-                    wsc = ws[row * G + g];
-                }
-#pragma unroll
-                for (int t = 0; t < TB; ++t) {
-                    float f = 0.0f;
-                    if (gl) f = __fmul_rn(__fmul_rn(__int2float_rn(dot64(wa, wb, xa[t], xb[t])), wsc), xsc[t]);
-                    tw[r * TB + t][lane] = f;
                 }
             }
             __syncwarp();
             if (lane < slots) {
-                const int gc = G - g0 < 32 ? G - g0 : 32;
+                const int gc = G - g0 < GL ? G - g0 : GL;
                 const float *row = tw[lane];
 #pragma unroll 8
                 for (int j = 0; j < gc; ++j) val = __fadd_rn(val, row[j]);   // group order
@@ -147,7 +146,8 @@ static cudaError_t launch_mm_t(const int8_t *xq, const float *xs, int B, const i
     const int64_t jobs = int64_t((d + RB - 1) / RB) * ntb;
     int64_t grid = (jobs + MM_WARPS - 1) / MM_WARPS;
     if (grid > int64_t(sms) * 8) grid = int64_t(sms) * 8;
-    matmul_q8_kernel<TB><<<unsigned(grid), MM_THREADS, 0, stream>>>(xq, xs, B, wq, ws, n, d, RB, out);
+    matmul_q8_kernel<TB, TB == 1 ? 4 : 2><<<unsigned(grid), MM_THREADS, 0, stream>>>(xq, xs, B, wq, ws, n, d, RB,
+                                                                                    out);
     return cudaGetLastError();
 }
 
