@@ -676,13 +676,133 @@ class Matmul06B(Workload):
         self._mm(*self._cpu["cls"])
 
     cpu_tokens = 1
+    cpu_note = ("the reference's own matmul (src/cpu/qwen3_original.c:310-331, compiled unmodified, its "
+                "#pragma omp parallel for over output rows), one decode token per pass")
 
     def bytes_for_tokens(self, n):
         return self.total_bytes() / self.tokens
 
 
+class Forward06B(Workload):
+    """One Qwen3-0.6B decode token through the whole model on the device
+    (q3cu_model_load + q3cu_model_forward: qwen3_original.c:333-468), at
+    position `pos` (attention over pos + 1 KV rows): the embedding row, 28
+    layers of RMSNorm+Q8_0, Q/K/V matmuls, QK-norm+RoPE, attention, quantize,
+    wo + residual, RMSNorm+Q8_0, W1|W3, SwiGLU+Q8_0, w2 + residual, then the
+    final RMSNorm+Q8_0 and the classifier -- 339 launches, replayed as one CUDA
+    graph per timed step.  The checkpoint is a seeded synthetic image in the
+    reference's file format (codes uniform in [-127, 127], scales
+    |N(0, 0.01)|, norm weights 1 + N(0, 0.1)); the reference arm runs its own
+    qwen3_forward on the same file."""
+    name = "forward06b"
+    dtype = "f32 activations, Q8_0 weights (int8 dp4a, exact int32)"
+
+    def __init__(self, tokens=1, pos=511, layers=28, dim=1024, hidden=3072, nh=16, nkv=8, hd=128, vocab=151936):
+        self.tokens, self.pos, self.layers, self.dim, self.hidden = 1, pos, layers, dim, hidden
+        self.nh, self.nkv, self.hd, self.vocab = nh, nkv, hd, vocab
+
+    def _bytes(self):
+        D, H, L, V = self.dim, self.hidden, self.layers, self.vocab
+        A, K = self.nh * self.hd, self.nkv * self.hd
+        codes = V * D + L * (A * D + 2 * K * D + D * A + 3 * H * D)
+        norms = 4 * (2 * L * D + D + 2 * L * self.hd)
+        kv = 2 * L * (self.pos + 1) * K * 4 + 2 * L * K * 4      # cache rows read, this position's rows written
+        return codes + codes // 16 + norms + kv + 4 * V
+
+    def kernels(self):
+        return [("decode_step", self._bytes())]
+
+    def config(self):
+        return {"workload": "Qwen3-0.6B decode token through the whole model on the device (28 layers, classifier)",
+                "tokens_per_gpu": 1, "position": self.pos, "dim": self.dim, "hidden": self.hidden,
+                "layers": self.layers, "n_heads": self.nh, "n_kv_heads": self.nkv, "head_dim": self.hd,
+                "vocab": self.vocab, "launches_per_step": 2 + 12 * self.layers + 1,
+                "weights": "seeded synthetic checkpoint, codes uniform [-127,127], scales |N(0,0.01)|",
+                "launch": "one CUDA graph replay per step; e2e: the q3cu_model_forward call with logits to the host"}
+
+    def image(self, seed=0):
+        """The checkpoint bytes (the reference's format), as a numpy uint8 array."""
+        import struct
+        import numpy as np
+        rng = np.random.default_rng(seed)
+        D, H, L, V, hd = self.dim, self.hidden, self.layers, self.vocab, self.hd
+        A, K = self.nh * hd, self.nkv * hd
+        parts = [struct.pack("I", 0x616A6331) + struct.pack("i", 1) +
+                 struct.pack("10i", D, H, L, self.nh, self.nkv, V, self.pos + 1, hd, 1, GS), bytes(256 - 48)]
+        norm = lambda n: (1.0 + 0.1 * rng.standard_normal(n, dtype=np.float32)).astype(np.float32).tobytes()
+        parts += [norm(L * D), norm(L * D), norm(D), norm(L * hd), norm(L * hd)]
+
+        def q8(rows, cols):
+            n = rows * cols
+            return (rng.integers(-127, 128, n, dtype=np.int8).tobytes() +
+                    np.abs(0.01 * rng.standard_normal(n // GS, dtype=np.float32)).astype(np.float32).tobytes())
+        parts.append(q8(V, D))
+        for shape in [(A, D)] * L + [(K, D)] * L + [(K, D)] * L + [(D, A)] * L + [(H, D)] * L + [(D, H)] * L + \
+                [(H, D)] * L:
+            parts.append(q8(*shape))
+        return np.frombuffer(b"".join(parts), np.uint8)
+
+    def make(self, torch, dev, seed):
+        return {"img": self.image(seed)}
+
+    def _model(self, q3, d):
+        if "model" not in d:
+            from metalqwen3_b200.q3cu import Q3Model
+            d["model"] = Q3Model(q3, d.pop("img"))
+        return d["model"]
+
+    def _replay(self, q3, d, stream):
+        import torch
+        m = self._model(q3, d)
+        if getattr(self, "_gkey", None) != (id(d), id(stream)):
+            m.forward(7, self.pos, stream=stream, to_host=False)         # eager once, outside the capture
+            stream.synchronize()
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr, stream=stream):
+                m.forward(7, self.pos, stream=stream, to_host=False)
+            self._graph, self._gkey = gr, (id(d), id(stream))
+        return self._graph
+
+    def launch(self, q3, d, stream, events=None):
+        gr = self._replay(q3, d, stream)
+        if events is not None:
+            events[0][0].record(stream)
+        gr.replay()
+        if events is not None:
+            events[0][1].record(stream)
+        return 2 + 12 * self.layers + 1
+
+    def launch_e2e(self, q3, d, stream):
+        self._model(q3, d).forward(7, self.pos, stream=stream, to_host=True)
+        return 2 + 12 * self.layers + 1
+
+    h2d_keys = ()
+    d2h_keys = ()
+    e2e_note = ("the token id goes in by value and the logits come back to the host inside the call "
+                f"(607,744 bytes); no graph")
+
+    def cpu_step(self, oracle, np, sample, threads, rng):
+        """One decode token by the reference's own qwen3_forward on the same checkpoint file."""
+        if not hasattr(self, "_ref"):
+            import tempfile
+            from oracle.oracle import Reference
+            self._dir = tempfile.TemporaryDirectory()
+            path = os.path.join(self._dir.name, "m.bin")
+            self.image(1234).tofile(path)
+            self._ref = Reference()
+            self._t = self._ref.create(path, self.pos + 1)
+        self._ref.forward(self._t, 7, self.pos)
+
+    cpu_tokens = 1
+    cpu_note = ("the reference's own qwen3_transformer_create + qwen3_forward (src/cpu/qwen3_original.c compiled "
+                "unmodified, OpenMP in its matmul and attention), one decode token per pass")
+
+    def bytes_for_tokens(self, n):
+        return self.total_bytes()
+
+
 WORKLOADS = {"prefill4b": Prefill4B, "decode8b": Decode8B, "embed": Embed, "prefill14b": Prefill14B,
-             "decode06b": Decode06B, "matmul06b": Matmul06B}
+             "decode06b": Decode06B, "matmul06b": Matmul06B, "forward06b": Forward06B}
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -785,7 +905,7 @@ def cpu_baseline(workload, seconds=10.0):
     gbs = workload.bytes_for_tokens(sample) * n / el / 1e9
     return {"value": round(gbs, 3), "unit": "GB/s", "cores": threads, "kind": kind,
             "sample": f"{n} passes over {getattr(workload, 'cpu_tokens', sample)} tokens of the same step "
-                      f"({el:.1f} s), OpenMP over rows; " + CPU_NOTE[kind],
+                      f"({el:.1f} s), OpenMP over rows; " + getattr(workload, "cpu_note", CPU_NOTE[kind]),
             "tokens_per_s": round(getattr(workload, "cpu_tokens", sample) * n / el, 1)}
 
 
@@ -825,7 +945,7 @@ def run_reference(args, wl):
         "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": kind,
                          "sample": f"{getattr(wl, 'cpu_tokens', sample)} tokens per step of the same workload, "
                                    f"{threads} host threads "
-                                   f"(OpenMP over rows); " + CPU_NOTE[kind]},
+                                   f"(OpenMP over rows); " + getattr(wl, "cpu_note", CPU_NOTE[kind])},
         "e2e": {"value": round(val, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)

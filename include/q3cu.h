@@ -166,6 +166,30 @@ q3cu_status q3cu_matmul_q8(q3cu_ctx *ctx, const int8_t *xq, const float *xs, int
                            const int8_t *wq, const float *ws, int n, int d, float *out,
                            q3cu_stream stream);
 
+/* ---- a checkpoint on the device and its decode step --------------------- */
+typedef struct q3cu_model q3cu_model;
+
+/* Loads a checkpoint image -- the file's bytes: 256-byte header, fp32 norms,
+ * Q8_0 tensors (qwen3_original.c:185-248 read_checkpoint/memory_map_weights,
+ * written by scripts/export.py:108-170) -- into device memory on ctx's device,
+ * with a zeroed KV cache of seq_len positions (ctx_length > 0 caps seq_len as
+ * :240-241 does).  The token table stays Q8_0: rows are dequantized on lookup
+ * instead of keeping the reference's fp32 copy (:203-205).  head_dim must be
+ * 128.  One device allocation, made here; a short image is Q3CU_ERR_FORMAT. */
+q3cu_status q3cu_model_load(q3cu_ctx *ctx, const void *checkpoint, size_t bytes, int ctx_length,
+                            q3cu_model **out);
+q3cu_status q3cu_model_config(const q3cu_model *m, q3cu_config *out);
+/* One decode step, `forward(token, pos)` (qwen3_original.c:333-468; the
+ * library entry qwen3_forward, :1062): the token at `pos` attends to the KV
+ * rows 0..pos written by earlier calls.  The logits [vocab] stay on the device
+ * (q3cu_model_logits); with logits_host set they are also copied there and the
+ * call synchronises `stream`.  Same bits as the reference.  Allocates nothing;
+ * an out-of-range token or pos is Q3CU_ERR_INDEX. */
+q3cu_status q3cu_model_forward(q3cu_model *m, int token, int pos, float *logits_host,
+                               q3cu_stream stream);
+const float *q3cu_model_logits(const q3cu_model *m);
+q3cu_status q3cu_model_destroy(q3cu_model *m);
+
 /* ---- host-pointer drop-in (synchronous), MetalContext signatures -------- */
 
 /* MetalContext::executeRMSNorm (src/metal/MetalContext.h:79). */

@@ -25,6 +25,10 @@
 // rounded up to a power of two), 32 / GL rows side by side, and U rows' loads
 // are in flight per lane.
 //
+// With `add` set, out = RN(add + val): the residual update that follows the
+// wo and w2 matmuls in the forward pass (x[i] += xb[i], :434 and :457), one
+// rounding as there; out may equal add.
+//
 // Cost: W is read once per block of TB tokens (TB <= 4), so for one to four
 // tokens the kernel streams W at HBM speed; larger batches re-read W per block
 // (a tensor-core path for prefill-sized batches is not part of this file).
@@ -49,7 +53,7 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
                                                                const float *__restrict__ xs, int B,
                                                                const int8_t *__restrict__ wq,
                                                                const float *__restrict__ ws, int n, int d, int RB,
-                                                               float *__restrict__ out) {
+                                                               const float *add, float *out) {
     __shared__ float terms[MM_WARPS][32][33];      // [slot = row * TB + token][group of the pass], padded
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int G = n / GS;                           // groups per row
@@ -128,14 +132,17 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
         }
         if (lane < slots) {
             const int i = i0 + lane / TB, t = t0 + lane % TB;
-            if (i < d && t < B) out[int64_t(t) * d + i] = val;
+            if (i < d && t < B) {
+                const int64_t o = int64_t(t) * d + i;
+                out[o] = add ? __fadd_rn(add[o], val) : val;      // residual: x[i] += xb[i] (:434, :457)
+            }
         }
     }
 }
 
 template <int TB>
 static cudaError_t launch_mm_t(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
-                               int d, float *out, cudaStream_t stream, int sms) {
+                               int d, const float *add, float *out, cudaStream_t stream, int sms) {
     const int ntb = (B + TB - 1) / TB;
     // Rows per tile: enough jobs for ~16 warps per SM, at most 32 / TB (one lane per (row, token)).
     const int64_t want = int64_t(sms) * 16;
@@ -147,16 +154,16 @@ static cudaError_t launch_mm_t(const int8_t *xq, const float *xs, int B, const i
     int64_t grid = (jobs + MM_WARPS - 1) / MM_WARPS;
     if (grid > int64_t(sms) * 8) grid = int64_t(sms) * 8;
     matmul_q8_kernel<TB, TB == 1 ? 4 : 2><<<unsigned(grid), MM_THREADS, 0, stream>>>(xq, xs, B, wq, ws, n, d, RB,
-                                                                                    out);
+                                                                                    add, out);
     return cudaGetLastError();
 }
 
 cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
-                             int d, float *out, cudaStream_t stream, int sms) {
+                             int d, float *out, cudaStream_t stream, int sms, const float *add) {
     if (B == 0 || d == 0) return cudaSuccess;
-    if (B == 1) return launch_mm_t<1>(xq, xs, B, wq, ws, n, d, out, stream, sms);
-    if (B == 2) return launch_mm_t<2>(xq, xs, B, wq, ws, n, d, out, stream, sms);
-    return launch_mm_t<4>(xq, xs, B, wq, ws, n, d, out, stream, sms);
+    if (B == 1) return launch_mm_t<1>(xq, xs, B, wq, ws, n, d, add, out, stream, sms);
+    if (B == 2) return launch_mm_t<2>(xq, xs, B, wq, ws, n, d, add, out, stream, sms);
+    return launch_mm_t<4>(xq, xs, B, wq, ws, n, d, add, out, stream, sms);
 }
 
 }  // namespace q3

@@ -151,6 +151,11 @@ cudaError_t ensure_smem_attr(const void *kernel, size_t bytes, int slot) {
     if (e == cudaSuccess) done[dev].fetch_or(bit, std::memory_order_release);
     return e;
 }
+
+q3cu_status set_error(q3cu_status s, const char *msg) { return fail(s, "%s", msg); }
+bool ctx_alive(const q3cu_ctx *ctx) { return ctx && ctx->alive; }
+q3cu_status ctx_use_device(q3cu_ctx *ctx) { return use_device(ctx); }
+int ctx_sms(const q3cu_ctx *ctx) { return ctx->sms; }
 }  // namespace q3
 
 extern "C" {

@@ -9,6 +9,12 @@
 
 namespace q3 {
 
+// Context internals for the other translation units of the library.
+q3cu_status set_error(q3cu_status s, const char *msg);   // records msg for q3cu_last_error_string
+bool ctx_alive(const q3cu_ctx *ctx);
+q3cu_status ctx_use_device(q3cu_ctx *ctx);                // makes the context's device current
+int ctx_sms(const q3cu_ctx *ctx);
+
 // Raises a kernel's dynamic shared-memory limit once per (device, slot):
 // `slot` (< 32) names the kernel instantiation.
 cudaError_t ensure_smem_attr(const void *kernel, size_t bytes, int slot);
@@ -34,8 +40,23 @@ cudaError_t launch_qk_norm_rope(void *q, void *k, q3cu_dtype dt, const int32_t *
                                 int n_kv, const float *q_norm, const float *k_norm, const InvFreq &inv_freq,
                                 float eps, uint32_t *status, cudaStream_t stream, int sms);
 
+// out = W @ x for each token row; with `add`, out = add + W @ x (one rounding).
 cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
-                             int d, float *out, cudaStream_t stream, int sms);
+                             int d, float *out, cudaStream_t stream, int sms, const float *add = nullptr);
+
+// Decode attention of one token at `pos` (head_dim 128): q [n_heads][128],
+// kc / vc the layer's caches [seq_len][kv_dim], att [n_heads][seq_len] scratch,
+// xb [n_heads][128] out.
+cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, float *xb, int pos,
+                               int n_heads, int kv_dim, int kv_mul, int seq_len, cudaStream_t stream);
+// Q/K RMSNorm + RoPE of one token, head_dim 128, in place; tab holds
+// cos/sin(pos * freq_j) for j < 64, computed by the caller.
+struct RopeTab {
+    float c[64], s[64];
+};
+cudaError_t launch_qk_norm_rope_tab(float *q, float *k, int n_heads, int n_kv, const float *qn, const float *kn,
+                                    const RopeTab &tab, float eps, cudaStream_t stream);
+
 
 cudaError_t launch_swiglu(const void *hb, const void *hb2, q3cu_dtype dt, int64_t elems, void *out, int8_t *q,
                           float *s, cudaStream_t stream, int sms);

@@ -1,0 +1,298 @@
+// q3cu_model.cu -- a Qwen3 checkpoint resident on the device, and the
+// reference's decode step (forward) run on it with the library's kernels.
+//
+// Reference: src/cpu/qwen3_original.c
+//   read_checkpoint / memory_map_weights (:185-248): 256-byte header, fp32
+//   norms (rms_att[L][dim], rms_ffn[L][dim], rms_final[dim], q_norm[L][hd],
+//   k_norm[L][hd]), then Q8_0 tensors, each as int8 codes then f32 scales:
+//   token table, wq[L], wk[L], wv[L], wo[L], w1[L], w2[L], w3[L] (and the
+//   classifier unless shared_classifier).  ctx_length caps seq_len (:240-241).
+//   forward (:333-468): the op sequence reproduced in q3cu_model_forward.
+//
+// Every step keeps the reference's roundings, so the logits are its bits:
+// the embedding row is dequantized on lookup (the reference dequantizes the
+// whole table at load, :203-205; same product per element); RMSNorm+Q8_0,
+// quantize, SwiGLU+Q8_0 are the library's bit-exact kernels; QK-norm+RoPE takes
+// its cos/sin from the host's libm for the step's position (as the reference
+// computes them) instead of the device's sincosf; the
+// matmuls keep the group order (k_matmul.cu) and fuse the residual add
+// (x += W x, one rounding as in :434/:457); attention keeps its three orders
+// (k_attn.cu).  W1 and W3 share their input and are stored as one [2H][dim]
+// matrix, so one launch produces hb and hb2.  Weights, KV cache and run state
+// live in one device allocation made at load; forward allocates nothing.
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <vector>
+
+#include "q3cu_internal.h"
+
+struct q3cu_model {
+    q3cu_ctx *ctx = nullptr;
+    q3cu_config cfg{};
+    int kv_dim = 0, ahd = 0, kv_mul = 0, sms = 0;
+    void *arena = nullptr;
+    float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr, *q_norm = nullptr, *k_norm = nullptr;
+    int8_t *tok_q = nullptr, *cls_q = nullptr;
+    float *tok_s = nullptr, *cls_s = nullptr;
+    std::vector<int8_t *> wq, wk, wv, wo, w13, w2;
+    std::vector<float *> sq, sk, sv, so, s13, s2;
+    float *kc = nullptr, *vc = nullptr, *x = nullptr, *q = nullptr, *att = nullptr, *xb = nullptr, *hb = nullptr,
+          *logits = nullptr, *xs = nullptr;
+    int8_t *xq = nullptr;
+};
+
+namespace {
+
+q3cu_status err(q3cu_status s, const char *fmt, ...) {
+    char buf[400];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof(buf), fmt, ap);
+    va_end(ap);
+    return q3::set_error(s, buf);
+}
+
+q3cu_status cuda_err(cudaError_t e, const char *what) {
+    return err(e == cudaErrorMemoryAllocation ? Q3CU_ERR_OOM : Q3CU_ERR_CUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+#define MTRY(expr, what)                                     \
+    do {                                                     \
+        cudaError_t e_ = (expr);                             \
+        if (e_ != cudaSuccess) return cuda_err(e_, what);    \
+    } while (0)
+#define MCHK(expr)                                           \
+    do {                                                     \
+        q3cu_status s_ = (expr);                             \
+        if (s_ != Q3CU_OK) return s_;                        \
+    } while (0)
+
+size_t up256(size_t b) { return (b + 255) & ~size_t(255); }
+
+// Bump allocator over the arena: first pass sizes it, second hands out pointers.
+struct Layout {
+    uint8_t *base = nullptr;
+    size_t off = 0;
+    template <typename T> T *take(size_t count) {
+        T *p = base ? reinterpret_cast<T *>(base + off) : nullptr;
+        off += up256(count * sizeof(T));
+        return p;
+    }
+};
+
+// Reads the checkpoint image in file order.
+struct Reader {
+    const uint8_t *p, *end;
+    bool ok = true;
+    const uint8_t *take(size_t n) {
+        if (size_t(end - p) < n) {
+            ok = false;
+            return nullptr;
+        }
+        const uint8_t *r = p;
+        p += n;
+        return r;
+    }
+};
+
+}  // namespace
+
+static void place(q3cu_model *m, Layout &L) {
+    const q3cu_config &c = m->cfg;
+    const size_t D = c.dim, H = c.hidden_dim, V = c.vocab_size, S = c.seq_len, hd = c.head_dim;
+    const int nl = c.n_layers;
+    m->rms_att = L.take<float>(size_t(nl) * D);
+    m->rms_ffn = L.take<float>(size_t(nl) * D);
+    m->rms_final = L.take<float>(D);
+    m->q_norm = L.take<float>(size_t(nl) * hd);
+    m->k_norm = L.take<float>(size_t(nl) * hd);
+    m->tok_q = L.take<int8_t>(V * D);
+    m->tok_s = L.take<float>(V * D / 64);
+    for (auto *v : {&m->wq, &m->wk, &m->wv, &m->wo, &m->w13, &m->w2}) v->assign(nl, nullptr);
+    for (auto *v : {&m->sq, &m->sk, &m->sv, &m->so, &m->s13, &m->s2}) v->assign(nl, nullptr);
+    const size_t A = m->ahd, K = m->kv_dim;
+    for (int l = 0; l < nl; ++l) {
+        m->wq[l] = L.take<int8_t>(A * D);      m->sq[l] = L.take<float>(A * D / 64);
+        m->wk[l] = L.take<int8_t>(K * D);      m->sk[l] = L.take<float>(K * D / 64);
+        m->wv[l] = L.take<int8_t>(K * D);      m->sv[l] = L.take<float>(K * D / 64);
+        m->wo[l] = L.take<int8_t>(D * A);      m->so[l] = L.take<float>(D * A / 64);
+        m->w13[l] = L.take<int8_t>(2 * H * D); m->s13[l] = L.take<float>(2 * H * D / 64);
+        m->w2[l] = L.take<int8_t>(D * H);      m->s2[l] = L.take<float>(D * H / 64);
+    }
+    if (c.shared_classifier) {
+        m->cls_q = m->tok_q;
+        m->cls_s = m->tok_s;
+    } else {
+        m->cls_q = L.take<int8_t>(V * D);
+        m->cls_s = L.take<float>(V * D / 64);
+    }
+    m->kc = L.take<float>(size_t(nl) * S * K);
+    m->vc = L.take<float>(size_t(nl) * S * K);
+    m->x = L.take<float>(D);
+    m->q = L.take<float>(A);
+    m->att = L.take<float>(size_t(c.n_heads) * S);
+    m->xb = L.take<float>(A);
+    m->hb = L.take<float>(2 * H);
+    m->logits = L.take<float>(V);
+    const size_t qmax = D > A ? (D > H ? D : H) : (A > H ? A : H);
+    m->xq = L.take<int8_t>(qmax);
+    m->xs = L.take<float>(qmax / 64);
+}
+
+extern "C" {
+
+q3cu_status q3cu_model_load(q3cu_ctx *ctx, const void *checkpoint, size_t bytes, int ctx_length, q3cu_model **out) {
+    if (!out) return err(Q3CU_ERR_INVALID, "out is NULL");
+    *out = nullptr;
+    if (!q3::ctx_alive(ctx)) return err(Q3CU_ERR_NOT_INIT, "context is NULL or destroyed");
+    if (!checkpoint) return err(Q3CU_ERR_INVALID, "checkpoint is NULL");
+    q3cu_config c;
+    MCHK(q3cu_check_header(checkpoint, bytes, &c));
+    if (bytes < 256) return err(Q3CU_ERR_FORMAT, "image shorter than its 256-byte header");
+    if (ctx_length < 0) return err(Q3CU_ERR_INVALID, "ctx_length %d", ctx_length);
+    if (ctx_length != 0 && ctx_length <= c.seq_len) c.seq_len = ctx_length;     // :240-241
+    if (c.head_dim != 128) return err(Q3CU_ERR_INVALID, "head_dim %d: the kernels take 128", c.head_dim);
+    const int A = c.n_heads * c.head_dim;
+    if (c.dim % 64 || c.hidden_dim % 64 || A % 64)
+        return err(Q3CU_ERR_FORMAT, "dim, hidden_dim and n_heads*head_dim must be multiples of 64");
+
+    q3cu_model *m = new q3cu_model();
+    m->ctx = ctx;
+    m->cfg = c;
+    m->ahd = A;
+    m->kv_dim = c.n_kv_heads * c.head_dim;
+    m->kv_mul = c.n_heads / c.n_kv_heads;
+    m->sms = q3::ctx_sms(ctx);
+    auto fail_free = [&](q3cu_status s) {
+        if (m->arena) cudaFree(m->arena);
+        delete m;
+        return s;
+    };
+    if (q3cu_status s = q3::ctx_use_device(ctx)) return fail_free(s);
+    Layout sizing;
+    place(m, sizing);
+    cudaError_t e = cudaMalloc(&m->arena, sizing.off);
+    if (e != cudaSuccess) return fail_free(cuda_err(e, "cudaMalloc (model)"));
+    Layout L{static_cast<uint8_t *>(m->arena), 0};
+    place(m, L);
+
+    // copy the image in file order
+    const size_t D = c.dim, H = c.hidden_dim, V = c.vocab_size, hd = c.head_dim, K = m->kv_dim;
+    const int nl = c.n_layers;
+    Reader r{static_cast<const uint8_t *>(checkpoint) + 256, static_cast<const uint8_t *>(checkpoint) + bytes};
+    auto up = [&](void *dst, size_t n) -> cudaError_t {
+        const uint8_t *src = r.take(n);
+        if (!src) return cudaSuccess;                       // r.ok reports the short image
+        return cudaMemcpy(dst, src, n, cudaMemcpyHostToDevice);
+    };
+    auto up_q8 = [&](int8_t *q, float *s, size_t n) -> cudaError_t {   // codes then scales
+        cudaError_t e1 = up(q, n);
+        if (e1 != cudaSuccess) return e1;
+        return up(s, n / 64 * 4);
+    };
+    cudaError_t ce = cudaSuccess;
+    auto step = [&](cudaError_t e2) { if (ce == cudaSuccess) ce = e2; };
+    step(up(m->rms_att, size_t(nl) * D * 4));
+    step(up(m->rms_ffn, size_t(nl) * D * 4));
+    step(up(m->rms_final, D * 4));
+    step(up(m->q_norm, size_t(nl) * hd * 4));
+    step(up(m->k_norm, size_t(nl) * hd * 4));
+    step(up_q8(m->tok_q, m->tok_s, V * D));
+    for (int l = 0; l < nl; ++l) step(up_q8(m->wq[l], m->sq[l], size_t(A) * D));
+    for (int l = 0; l < nl; ++l) step(up_q8(m->wk[l], m->sk[l], K * D));
+    for (int l = 0; l < nl; ++l) step(up_q8(m->wv[l], m->sv[l], K * D));
+    for (int l = 0; l < nl; ++l) step(up_q8(m->wo[l], m->so[l], D * size_t(A)));
+    for (int l = 0; l < nl; ++l) step(up_q8(m->w13[l], m->s13[l], H * D));                       // w1: rows 0..H-1
+    for (int l = 0; l < nl; ++l) step(up_q8(m->w2[l], m->s2[l], D * H));
+    for (int l = 0; l < nl; ++l) step(up_q8(m->w13[l] + H * D, m->s13[l] + H * D / 64, H * D));  // w3: rows H..2H-1
+    if (!c.shared_classifier) step(up_q8(m->cls_q, m->cls_s, V * D));
+    if (ce != cudaSuccess) return fail_free(cuda_err(ce, "cudaMemcpy (weights)"));
+    if (!r.ok) return fail_free(err(Q3CU_ERR_FORMAT, "image of %zu bytes is shorter than its header's tensors", bytes));
+    // the KV cache starts at zero, as the reference's calloc'd RunState (:113-114)
+    e = cudaMemset(m->kc, 0, size_t(nl) * c.seq_len * K * 4);
+    if (e == cudaSuccess) e = cudaMemset(m->vc, 0, size_t(nl) * c.seq_len * K * 4);
+    if (e != cudaSuccess) return fail_free(cuda_err(e, "cudaMemset (KV cache)"));
+    *out = m;
+    return Q3CU_OK;
+}
+
+q3cu_status q3cu_model_config(const q3cu_model *m, q3cu_config *out) {
+    if (!m || !out) return err(Q3CU_ERR_INVALID, "NULL argument");
+    *out = m->cfg;
+    return Q3CU_OK;
+}
+
+const float *q3cu_model_logits(const q3cu_model *m) { return m ? m->logits : nullptr; }
+
+q3cu_status q3cu_model_forward(q3cu_model *m, int token, int pos, float *logits_host, q3cu_stream stream) {
+    if (!m) return err(Q3CU_ERR_INVALID, "model is NULL");
+    q3cu_ctx *ctx = m->ctx;
+    if (!q3::ctx_alive(ctx)) return err(Q3CU_ERR_NOT_INIT, "the model's context is destroyed");
+    const q3cu_config &c = m->cfg;
+    if (token < 0 || token >= c.vocab_size) return err(Q3CU_ERR_INDEX, "token %d outside [0, %d)", token, c.vocab_size);
+    if (pos < 0 || pos >= c.seq_len) return err(Q3CU_ERR_INDEX, "pos %d outside [0, %d)", pos, c.seq_len);
+    MCHK(q3::ctx_use_device(ctx));
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const int D = c.dim, H = c.hidden_dim, A = m->ahd, K = m->kv_dim, hd = c.head_dim, S = c.seq_len;
+    const float eps = 1e-6f;                                   // rmsnorm's constant (:283)
+    // RoPE's cos/sin for this position with the C library's calls, as the
+    // reference makes them (:367-368): freq = powf(1e6, -(float)j / (hd/2)),
+    // cosf / sinf of the binary32 product pos * freq.
+    q3::RopeTab tab;
+    for (int j = 0; j < hd / 2; ++j) {
+        const float freq = powf(1e6f, -float(j) / float(hd / 2));
+        const float ang = float(pos) * freq;
+        tab.c[j] = cosf(ang);
+        tab.s[j] = sinf(ang);
+    }
+    // token embedding (:342): the row of the dequantized table
+    MCHK(q3cu_dequantize_q8(ctx, m->tok_q + int64_t(token) * D, m->tok_s + int64_t(token) * (D / 64), D, m->x,
+                            stream));
+    for (int l = 0; l < c.n_layers; ++l) {
+        const int64_t loff = int64_t(l) * S * K;
+        float *kr = m->kc + loff + int64_t(pos) * K, *vr = m->vc + loff + int64_t(pos) * K;
+        // attention rmsnorm + quantize, QKV (:353-359)
+        MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_att + int64_t(l) * D, 1, D, eps, m->xq, m->xs, stream));
+        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->wq[l], m->sq[l], D, A, m->q, s, m->sms), "wq");
+        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->wk[l], m->sk[l], D, K, kr, s, m->sms), "wk");
+        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->wv[l], m->sv[l], D, K, vr, s, m->sms), "wv");
+        // Q/K RMSNorm + RoPE, the key in its cache row (:361-393)
+        MTRY(q3::launch_qk_norm_rope_tab(m->q, kr, c.n_heads, c.n_kv_heads, m->q_norm + int64_t(l) * hd,
+                                         m->k_norm + int64_t(l) * hd, tab, eps, s),
+             "qk_norm_rope");
+        // attention (:395-428)
+        MTRY(q3::launch_attn_decode(m->q, m->kc + loff, m->vc + loff, m->att, m->xb, pos, c.n_heads, K, m->kv_mul, S,
+                                    s),
+             "attention");
+        // output projection + residual (:431-435)
+        MCHK(q3cu_quantize_q8(ctx, m->xb, Q3CU_F32, 1, A, m->xq, m->xs, stream));
+        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->wo[l], m->so[l], A, D, m->x, s, m->sms, m->x), "wo");
+        // FFN (:438-458)
+        MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_ffn + int64_t(l) * D, 1, D, eps, m->xq, m->xs, stream));
+        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->w13[l], m->s13[l], D, 2 * H, m->hb, s, m->sms), "w1|w3");
+        MCHK(q3cu_swiglu_q8(ctx, m->hb, m->hb + H, Q3CU_F32, 1, H, m->xq, m->xs, stream));
+        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->w2[l], m->s2[l], H, D, m->x, s, m->sms, m->x), "w2");
+    }
+    // final rmsnorm + classifier (:462-466)
+    MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_final, 1, D, eps, m->xq, m->xs, stream));
+    MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->cls_q, m->cls_s, D, c.vocab_size, m->logits, s, m->sms),
+         "classifier");
+    if (logits_host) {
+        MTRY(cudaMemcpyAsync(logits_host, m->logits, size_t(c.vocab_size) * 4, cudaMemcpyDeviceToHost, s), "logits D2H");
+        MTRY(cudaStreamSynchronize(s), "cudaStreamSynchronize");
+        MCHK(q3cu_device_status(ctx, stream, nullptr));
+    }
+    return Q3CU_OK;
+}
+
+q3cu_status q3cu_model_destroy(q3cu_model *m) {
+    if (!m) return Q3CU_OK;
+    if (q3::ctx_alive(m->ctx)) q3::ctx_use_device(m->ctx);
+    cudaError_t e = m->arena ? cudaFree(m->arena) : cudaSuccess;
+    delete m;
+    return e == cudaSuccess ? Q3CU_OK : cuda_err(e, "cudaFree (model)");
+}
+
+}  // extern "C"

@@ -66,6 +66,11 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
                 "q3cu_embed_gather": (st, [vp, vp, vp, i32, i32, vp, i64, vp, vp, vp, vp]),
                 "q3cu_matmul_q8": (st, [vp, vp, vp, i32, vp, vp, i32, i32, vp, vp]),
                 "q3cu_execute_quantized_matmul": (st, [vp, vp, vp, vp, vp, vp, i32, i32, i32]),
+                "q3cu_model_load": (st, [vp, vp, C.c_size_t, i32, C.POINTER(vp)]),
+                "q3cu_model_config": (st, [vp, vp]),
+                "q3cu_model_forward": (st, [vp, i32, i32, vp, vp]),
+                "q3cu_model_logits": (vp, [vp]),
+                "q3cu_model_destroy": (st, [vp]),
                 "q3cu_execute_rmsnorm": (st, [vp, vp, vp, vp, i32]),
                 "q3cu_execute_softmax": (st, [vp, vp, i32]),
                 "q3cu_execute_swiglu": (st, [vp, vp, vp, i32]),
@@ -247,3 +252,46 @@ class Q3CU:
     def execute_embedding(self, out, tq, ts, token, dim):
         self._check(self.lib.q3cu_execute_embedding(self.ctx, _ptr(out), _ptr(tq), _ptr(ts), token, dim),
                     "executeEmbedding")
+
+
+class Q3Model:
+    """A checkpoint image (numpy uint8 array or bytes: the reference's file
+    format) resident on the device of `q3` (a Q3CU context), with its KV cache;
+    forward(token, pos) returns the logits as a numpy array."""
+
+    def __init__(self, q3, image, ctx_length=0):
+        import numpy as np
+        self.q3, self.lib = q3, q3.lib
+        self._img = np.ascontiguousarray(np.frombuffer(image, np.uint8) if isinstance(image, (bytes, bytearray))
+                                         else image, np.uint8)
+        self.m = C.c_void_p()
+        q3._check(self.lib.q3cu_model_load(q3.ctx, self._img.ctypes.data, self._img.nbytes, ctx_length,
+                                           C.byref(self.m)), "q3cu_model_load")
+        cfg = (C.c_int32 * 12)()
+        q3._check(self.lib.q3cu_model_config(self.m, cfg), "q3cu_model_config")
+        keys = ("magic", "version", "dim", "hidden_dim", "n_layers", "n_heads", "n_kv_heads", "vocab_size",
+                "seq_len", "head_dim", "shared_classifier", "group_size")
+        self.config = dict(zip(keys, list(cfg)))
+        self._img = None                      # the weights live on the device now
+
+    def forward(self, token, pos, stream=None, to_host=True):
+        import numpy as np
+        out = np.empty(self.config["vocab_size"], np.float32) if to_host else None
+        self.q3._check(self.lib.q3cu_model_forward(self.m, int(token), int(pos),
+                                                   out.ctypes.data if to_host else None, self.q3._stream(stream)),
+                       "q3cu_model_forward")
+        return out
+
+    def logits_ptr(self):
+        return self.lib.q3cu_model_logits(self.m)
+
+    def close(self):
+        if self.m:
+            self.lib.q3cu_model_destroy(self.m)
+            self.m = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

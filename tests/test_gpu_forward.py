@@ -1,0 +1,111 @@
+"""The whole decode step on the device (q3cu_model_load / q3cu_model_forward)
+against the reference CPU engine itself (src/cpu/qwen3_original.c compiled
+unmodified: qwen3_transformer_create + qwen3_forward on the same checkpoint
+file): logits bit-identical at every position, the KV cache carried across
+calls.  Checkpoints are seeded synthetic ones in the reference's export format
+(oracle/checkpoint.py); where the compiled reference is absent the oracle's
+restatement (pinned to it in test_oracle_pin.py) gives the expected logits.
+"""
+import os
+import tempfile
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+
+def same_bits(a, b):
+    a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)
+    na, nb = np.isnan(a), np.isnan(b)
+    return a.shape == b.shape and np.array_equal(na, nb) and \
+        np.array_equal(a[~na].view(np.uint32), b[~nb].view(np.uint32))
+
+
+def expected_logits(path, img, shape, steps, ctx_length=0):
+    """Logits of the reference (or, without it, the oracle) for each (token, pos)."""
+    from oracle.oracle import Reference, build_reference, reference_path
+    if not os.path.exists(reference_path()):
+        build_reference()
+    out = []
+    if os.path.exists(reference_path()):
+        ref = Reference()
+        t = ref.create(path, ctx_length)
+        try:
+            for tok, pos in steps:
+                out.append(ref.forward(t, tok, pos).copy())
+        finally:
+            ref.free(t)
+        return out
+    from oracle.oracle import OracleModel
+    om = OracleModel(img, ctx_length=ctx_length)
+    try:
+        for tok, pos in steps:
+            out.append(om.forward(tok, pos).copy())
+    finally:
+        om.close()
+    return out
+
+
+SHAPES = {
+    "small": dict(dim=256, hidden=768, n_layers=3, n_heads=4, n_kv=2, vocab=300, seq_len=16, head_dim=128),
+    # Qwen3-0.6B's layer shape and vocabulary, 2 layers
+    "qwen3_06b_2l": dict(dim=1024, hidden=3072, n_layers=2, n_heads=16, n_kv=8, vocab=151936, seq_len=48,
+                         head_dim=128),
+}
+
+
+@pytest.mark.parametrize("name", sorted(SHAPES))
+def test_forward_logits_bit_exact(q3, name):
+    from metalqwen3_b200.q3cu import Q3Model
+    from oracle.checkpoint import write_checkpoint
+    shape = SHAPES[name]
+    rng = np.random.default_rng(len(name))
+    npos = 12 if name == "small" else 40
+    steps = [(int(t), p) for p, t in enumerate(rng.integers(0, shape["vocab"], npos))]
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "m.bin")
+        write_checkpoint(path, seed=5, **shape)
+        img = np.fromfile(path, np.uint8)
+        want = expected_logits(path, img, shape, steps)
+    model = Q3Model(q3, img)
+    try:
+        for (tok, pos), w in zip(steps, want):
+            got = model.forward(tok, pos)
+            assert same_bits(got, w), f"{name}: logits differ at pos {pos} (max |diff| {np.nanmax(np.abs(got - w))})"
+    finally:
+        model.close()
+
+
+def test_forward_ctx_length_and_errors(q3):
+    from metalqwen3_b200.q3cu import Q3Error, Q3Model
+    from oracle.checkpoint import checkpoint_image, write_checkpoint
+    shape = SHAPES["small"]
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "m.bin")
+        write_checkpoint(path, seed=9, **shape)
+        img = np.fromfile(path, np.uint8)
+        steps = [(7, 0), (299, 1), (0, 2), (150, 3), (42, 4), (1, 5)]
+        want = expected_logits(path, img, shape, steps, ctx_length=6)        # seq_len capped to 6
+    m = Q3Model(q3, img, ctx_length=6)
+    try:
+        assert m.config["seq_len"] == 6
+        for (tok, pos), w in zip(steps, want):
+            assert same_bits(m.forward(tok, pos), w)
+        with pytest.raises(Q3Error) as e:
+            m.forward(1, 6)                                   # pos beyond the capped context
+        assert e.value.status == 5                            # ERR_INDEX
+        with pytest.raises(Q3Error) as e:
+            m.forward(shape["vocab"], 0)                      # token beyond the vocabulary
+        assert e.value.status == 5
+    finally:
+        m.close()
+    bad = img.copy()
+    bad[0] ^= 0xFF                                            # magic
+    with pytest.raises(Q3Error) as e:
+        Q3Model(q3, bad)
+    assert e.value.status == 10                               # ERR_FORMAT
+    with pytest.raises(Q3Error) as e:
+        Q3Model(q3, img[: img.size - 1000])                   # truncated tensors
+    assert e.value.status == 10
+    assert np.array_equal(checkpoint_image(seed=9, **shape), img)
