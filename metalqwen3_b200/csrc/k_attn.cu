@@ -15,68 +15,115 @@
 // probabilities live in the caller's att buffer ([n_heads][seq_len], like the
 // reference's RunState att), so any position up to seq_len is supported.
 //
-// One CTA per query head, 128 threads (one per element of the head).  Decode
-// is latency-bound (a few microseconds per layer at short contexts); the
-// position-order sum is the serial part and grows with pos.
+// One CTA per query head, 128 threads (one per element of the head).  K and V
+// reach shared memory in chunks of 128 positions by cp.async, double-buffered
+// (64 KB per chunk in flight, the next chunk loading while this one is used);
+// K rows are padded to 528 B so a thread per position reads its row without
+// bank conflicts.  The position-order probability sum is the serial part.
 #include "q3cu_internal.h"
 
 namespace q3 {
 
 constexpr int AT_HD = 128;
+constexpr int AT_CH = 128;                                  // positions per staged chunk
+constexpr int AT_KROW = AT_HD * 4 + 16;                     // padded K row: 33 x 16 B, conflict-free float4 reads
+constexpr size_t AT_BUF = size_t(AT_CH) * AT_KROW;          // 67,584 B per chunk buffer
+constexpr size_t AT_SMEM = 2 * AT_BUF;                      // double-buffered
 
-__global__ void __launch_bounds__(AT_HD) attn_decode_kernel(const float *__restrict__ q, const float *kc,
-                                                            const float *vc, float *att, float *xb, int pos,
-                                                            int kv_dim, int kv_mul, int seq_len) {
+// Copies rows c0 .. c0+n-1 of a cache (this kv head's 128 floats of each) into
+// buf with 16-byte cp.async pieces, `rowb` bytes apart; one commit group.
+__device__ __forceinline__ void attn_stage(uint8_t *buf, const float *cache, int c0, int n, int kv_dim, int kvh,
+                                           int rowb, int tid) {
+    for (int f = tid; f < n * 32; f += AT_HD) {
+        const int r = f >> 5, pc = f & 31;
+        cp_async16(buf + r * rowb + pc * 16, cache + int64_t(c0 + r) * kv_dim + kvh * AT_HD + pc * 4);
+    }
+    cp_async_commit();
+}
+
+__global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__restrict__ q, const float *kc,
+                                                               const float *vc, float *att, float *xb, int pos,
+                                                               int kv_dim, int kv_mul, int seq_len) {
+    extern __shared__ __align__(16) uint8_t tiles[];        // [2][AT_BUF]
     __shared__ __align__(16) float qs[AT_HD];
     __shared__ ExpTab tab;
     __shared__ float red[AT_HD / 32];
     __shared__ float sum_sh;
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kvh = h / kv_mul;
+    const int npos = pos + 1, nch = (npos + AT_CH - 1) / AT_CH;
     qs[tid] = q[int64_t(h) * AT_HD + tid];
     load_exp_table(tab);
-    __syncthreads();
     float *a = att + int64_t(h) * seq_len;
     const float scale = __fsqrt_rn(float(AT_HD));            // sqrtf((float) head_dim)
 
-    // scores: one thread per position, the dot product in index order
+    // scores, chunk by chunk (the next chunk's K rows in flight): thread t
+    // runs position c0 + t's dot product in index order from shared memory
     float m = 0.0f;                                         // softmax's max starts at 0
-    for (int t = tid; t <= pos; t += AT_HD) {
-        const float *k = kc + int64_t(t) * kv_dim + kvh * AT_HD;
-        float s = 0.0f;
-#pragma unroll 8
-        for (int i = 0; i < AT_HD; i += 4) {
-            const float4 kv = *reinterpret_cast<const float4 *>(k + i);
-            s = __fadd_rn(s, __fmul_rn(qs[i], kv.x));
-            s = __fadd_rn(s, __fmul_rn(qs[i + 1], kv.y));
-            s = __fadd_rn(s, __fmul_rn(qs[i + 2], kv.z));
-            s = __fadd_rn(s, __fmul_rn(qs[i + 3], kv.w));
+    attn_stage(tiles, kc, 0, npos < AT_CH ? npos : AT_CH, kv_dim, kvh, AT_KROW, tid);
+    for (int c = 0; c < nch; ++c) {
+        const int c0 = c * AT_CH, n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
+        if (c + 1 < nch) {
+            const int n1 = npos - c0 - AT_CH < AT_CH ? npos - c0 - AT_CH : AT_CH;
+            attn_stage(tiles + ((c + 1) & 1) * AT_BUF, kc, c0 + AT_CH, n1, kv_dim, kvh, AT_KROW, tid);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
         }
-        const float sc = __fdiv_rn(s, scale);
-        a[t] = sc;
-        m = fmaxf(m, sc);                                   // a NaN never replaces the max
+        __syncthreads();                                     // chunk c landed (every thread's pieces)
+        if (tid < n) {
+            const float4 *kr = reinterpret_cast<const float4 *>(tiles + (c & 1) * AT_BUF + tid * AT_KROW);
+            float s = 0.0f;
+#pragma unroll 8
+            for (int i4 = 0; i4 < AT_HD / 4; ++i4) {
+                const float4 kv = kr[i4];
+                s = __fadd_rn(s, __fmul_rn(qs[4 * i4], kv.x));
+                s = __fadd_rn(s, __fmul_rn(qs[4 * i4 + 1], kv.y));
+                s = __fadd_rn(s, __fmul_rn(qs[4 * i4 + 2], kv.z));
+                s = __fadd_rn(s, __fmul_rn(qs[4 * i4 + 3], kv.w));
+            }
+            const float sc = __fdiv_rn(s, scale);
+            a[c0 + tid] = sc;
+            m = fmaxf(m, sc);                                // a NaN never replaces the max
+        }
+        __syncthreads();                                     // before the buffer is refilled
     }
+    // the first V chunk streams in while the softmax runs
+    attn_stage(tiles, vc, 0, npos < AT_CH ? npos : AT_CH, kv_dim, kvh, AT_HD * 4, tid);
     m = warp_max(m);
     if (lane == 0) red[warp] = m;
     __syncthreads();
     m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
     // exp (the host libm's bits), then the sum in position order
-    for (int t = tid; t <= pos; t += AT_HD) a[t] = expf_host(__fsub_rn(a[t], m), tab);
+    for (int t = tid; t < npos; t += AT_HD) a[t] = expf_host(__fsub_rn(a[t], m), tab);
     __syncthreads();
     if (tid == 0) {
         float sum = 0.0f;
-        for (int t = 0; t <= pos; ++t) sum = __fadd_rn(sum, a[t]);
+        for (int t = 0; t < npos; ++t) sum = __fadd_rn(sum, a[t]);
         sum_sh = sum;
     }
     __syncthreads();
     const float sum = sum_sh;
-    for (int t = tid; t <= pos; t += AT_HD) a[t] = __fdiv_rn(a[t], sum);
+    for (int t = tid; t < npos; t += AT_HD) a[t] = __fdiv_rn(a[t], sum);
     __syncthreads();
-    // weighted values: one thread per element, positions in order
-    const float *v = vc + kvh * AT_HD + tid;
+    // weighted values: thread i runs element i's chain over the positions in order
     float acc = 0.0f;
-#pragma unroll 4
-    for (int t = 0; t <= pos; ++t) acc = __fadd_rn(acc, __fmul_rn(a[t], v[int64_t(t) * kv_dim]));
+    for (int c = 0; c < nch; ++c) {
+        const int c0 = c * AT_CH, n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
+        if (c + 1 < nch) {
+            const int n1 = npos - c0 - AT_CH < AT_CH ? npos - c0 - AT_CH : AT_CH;
+            attn_stage(tiles + ((c + 1) & 1) * AT_BUF, vc, c0 + AT_CH, n1, kv_dim, kvh, AT_HD * 4, tid);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();
+        const float *vt = reinterpret_cast<const float *>(tiles + (c & 1) * AT_BUF) + tid;
+        const float *at = a + c0;
+#pragma unroll 8
+        for (int t = 0; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(at[t], vt[t * AT_HD]));
+        __syncthreads();
+    }
     xb[int64_t(h) * AT_HD + tid] = acc;
 }
 
@@ -122,7 +169,9 @@ cudaError_t launch_qk_norm_rope_tab(float *q, float *k, int n_heads, int n_kv, c
 
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, float *xb, int pos,
                                int n_heads, int kv_dim, int kv_mul, int seq_len, cudaStream_t stream) {
-    attn_decode_kernel<<<n_heads, AT_HD, 0, stream>>>(q, kc, vc, att, xb, pos, kv_dim, kv_mul, seq_len);
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_decode_kernel), AT_SMEM, 24);
+    if (e != cudaSuccess) return e;
+    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(q, kc, vc, att, xb, pos, kv_dim, kv_mul, seq_len);
     return cudaGetLastError();
 }
 
