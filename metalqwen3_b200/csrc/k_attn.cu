@@ -6,6 +6,7 @@
 //     att[t] = score / sqrtf(head_dim)
 //     softmax(att, pos + 1)                                   (:291-308)
 //     xb = 0;   for t <= pos: for i: xb[i] += att[t] * v_t[i]   (position order)
+//     quantize(xq, xb, n_heads * head_dim)                    (:431, fused here)
 // and softmax: max starts at 0 (NaN never wins), x = expf(x - max) summed in
 // index order, then x /= sum.  Without FMA contraction every product and sum
 // above is one rounding, so this kernel keeps each chain's order: a thread per
@@ -42,13 +43,14 @@ __device__ __forceinline__ void attn_stage(uint8_t *buf, const float *cache, int
 }
 
 __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__restrict__ q, const float *kc,
-                                                               const float *vc, float *att, float *xb, int pos,
-                                                               int kv_dim, int kv_mul, int seq_len) {
+                                                               const float *vc, float *att, int8_t *xq, float *xs,
+                                                               int pos, int kv_dim, int kv_mul, int seq_len) {
     extern __shared__ __align__(16) uint8_t tiles[];        // [2][AT_BUF]
     __shared__ __align__(16) float qs[AT_HD];
     __shared__ ExpTab tab;
     __shared__ float red[AT_HD / 32];
     __shared__ float sum_sh;
+    __shared__ float gmax[2];
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kvh = h / kv_mul;
     const int npos = pos + 1, nch = (npos + AT_CH - 1) / AT_CH;
@@ -124,7 +126,17 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__re
         for (int t = 0; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(at[t], vt[t * AT_HD]));
         __syncthreads();
     }
-    xb[int64_t(h) * AT_HD + tid] = acc;
+    // the quantize that follows (:431): the head's 128 outputs are Q8_0 groups
+    // 2h and 2h+1 -- group absmax (strict >, from 0), scale = wmax / 127,
+    // code = (int8) round(x / scale), the reference's operations exactly
+    float gm = warp_max(fmaxf(0.0f, fabsf(acc)));           // from 0; a NaN never wins
+    if (lane == 0) red[warp] = gm;
+    __syncthreads();
+    if (tid < 2) gmax[tid] = fmaxf(red[2 * tid], red[2 * tid + 1]);
+    __syncthreads();
+    const float qscale = q8_scale(gmax[tid >> 6]);
+    xq[int64_t(h) * AT_HD + tid] = int8_t(q8_code(acc, qscale));
+    if ((tid & 63) == 0) xs[int64_t(h) * 2 + (tid >> 6)] = qscale;
 }
 
 // Q/K RMSNorm + RoPE of one token (qwen3_original.c:361-393) with the
@@ -167,11 +179,11 @@ cudaError_t launch_qk_norm_rope_tab(float *q, float *k, int n_heads, int n_kv, c
     return cudaGetLastError();
 }
 
-cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, float *xb, int pos,
-                               int n_heads, int kv_dim, int kv_mul, int seq_len, cudaStream_t stream) {
+cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, int8_t *xq, float *xs,
+                               int pos, int n_heads, int kv_dim, int kv_mul, int seq_len, cudaStream_t stream) {
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_decode_kernel), AT_SMEM, 24);
     if (e != cudaSuccess) return e;
-    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(q, kc, vc, att, xb, pos, kv_dim, kv_mul, seq_len);
+    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(q, kc, vc, att, xq, xs, pos, kv_dim, kv_mul, seq_len);
     return cudaGetLastError();
 }
 

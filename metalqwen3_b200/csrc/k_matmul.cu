@@ -53,7 +53,7 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
                                                                const float *__restrict__ xs, int B,
                                                                const int8_t *__restrict__ wq,
                                                                const float *__restrict__ ws, int n, int d, int RB,
-                                                               const float *add, float *out) {
+                                                               const float *add, MmOut out) {
     __shared__ float terms[MM_WARPS][32][33];      // [slot = row * TB + token][group of the pass], padded
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int G = n / GS;                           // groups per row
@@ -133,8 +133,17 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
         if (lane < slots) {
             const int i = i0 + lane / TB, t = t0 + lane % TB;
             if (i < d && t < B) {
-                const int64_t o = int64_t(t) * d + i;
-                out[o] = add ? __fadd_rn(add[o], val) : val;      // residual: x[i] += xb[i] (:434, :457)
+                // output rows [0, e0) -> p0, [e0, e1) -> p1, [e1, d) -> p2, each segment [B][len]
+                float *p;
+                int64_t o;
+                if (i < out.e0) {
+                    p = out.p0; o = int64_t(t) * out.e0 + i;
+                } else if (i < out.e1) {
+                    p = out.p1; o = int64_t(t) * (out.e1 - out.e0) + (i - out.e0);
+                } else {
+                    p = out.p2; o = int64_t(t) * (d - out.e1) + (i - out.e1);
+                }
+                p[o] = add ? __fadd_rn(add[o], val) : val;        // residual: x[i] += xb[i] (:434, :457)
             }
         }
     }
@@ -142,7 +151,7 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
 
 template <int TB>
 static cudaError_t launch_mm_t(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
-                               int d, const float *add, float *out, cudaStream_t stream, int sms) {
+                               int d, const float *add, const MmOut &out, cudaStream_t stream, int sms) {
     const int ntb = (B + TB - 1) / TB;
     // Rows per tile: enough jobs for ~16 warps per SM, at most 32 / TB (one lane per (row, token)).
     const int64_t want = int64_t(sms) * 16;
@@ -160,6 +169,11 @@ static cudaError_t launch_mm_t(const int8_t *xq, const float *xs, int B, const i
 
 cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
                              int d, float *out, cudaStream_t stream, int sms, const float *add) {
+    return launch_matmul_q8_seg(xq, xs, B, wq, ws, n, d, MmOut{out, out, out, d, d}, stream, sms, add);
+}
+
+cudaError_t launch_matmul_q8_seg(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
+                                 int d, const MmOut &out, cudaStream_t stream, int sms, const float *add) {
     if (B == 0 || d == 0) return cudaSuccess;
     if (B == 1) return launch_mm_t<1>(xq, xs, B, wq, ws, n, d, add, out, stream, sms);
     if (B == 2) return launch_mm_t<2>(xq, xs, B, wq, ws, n, d, add, out, stream, sms);

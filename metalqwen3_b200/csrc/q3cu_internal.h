@@ -40,15 +40,23 @@ cudaError_t launch_qk_norm_rope(void *q, void *k, q3cu_dtype dt, const int32_t *
                                 int n_kv, const float *q_norm, const float *k_norm, const InvFreq &inv_freq,
                                 float eps, uint32_t *status, cudaStream_t stream, int sms);
 
+// Where the output rows of a matmul go: rows [0, e0) to p0, [e0, e1) to p1,
+// [e1, d) to p2, each as [B][segment length] (one segment: p0, e0 = e1 = d).
+struct MmOut {
+    float *p0, *p1, *p2;
+    int e0, e1;
+};
+cudaError_t launch_matmul_q8_seg(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
+                                 int d, const MmOut &out, cudaStream_t stream, int sms, const float *add = nullptr);
 // out = W @ x for each token row; with `add`, out = add + W @ x (one rounding).
 cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
                              int d, float *out, cudaStream_t stream, int sms, const float *add = nullptr);
 
 // Decode attention of one token at `pos` (head_dim 128): q [n_heads][128],
-// kc / vc the layer's caches [seq_len][kv_dim], att [n_heads][seq_len] scratch,
-// xb [n_heads][128] out.
-cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, float *xb, int pos,
-                               int n_heads, int kv_dim, int kv_mul, int seq_len, cudaStream_t stream);
+// kc / vc the layer's caches [seq_len][kv_dim], att [n_heads][seq_len] scratch;
+// the output [n_heads][128] as Q8_0 codes xq and scales xs [n_heads * 2].
+cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, int8_t *xq, float *xs,
+                               int pos, int n_heads, int kv_dim, int kv_mul, int seq_len, cudaStream_t stream);
 // Q/K RMSNorm + RoPE of one token, head_dim 128, in place; tab holds
 // cos/sin(pos * freq_j) for j < 64, computed by the caller.
 struct RopeTab {

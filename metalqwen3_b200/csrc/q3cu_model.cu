@@ -17,8 +17,10 @@
 // computes them) instead of the device's sincosf; the
 // matmuls keep the group order (k_matmul.cu) and fuse the residual add
 // (x += W x, one rounding as in :434/:457); attention keeps its three orders
-// (k_attn.cu).  W1 and W3 share their input and are stored as one [2H][dim]
-// matrix, so one launch produces hb and hb2.  Weights, KV cache and run state
+// and quantizes its own output (k_attn.cu).  Weights that share an input are
+// stored as one matrix -- Q|K|V as [A+2K][dim], its output rows going to q and
+// to this position's K and V cache rows; W1|W3 as [2H][dim] -- so a layer is
+// 9 launches.  Weights, KV cache and run state
 // live in one device allocation made at load; forward allocates nothing.
 #include <cmath>
 #include <cstdarg>
@@ -36,9 +38,9 @@ struct q3cu_model {
     float *rms_att = nullptr, *rms_ffn = nullptr, *rms_final = nullptr, *q_norm = nullptr, *k_norm = nullptr;
     int8_t *tok_q = nullptr, *cls_q = nullptr;
     float *tok_s = nullptr, *cls_s = nullptr;
-    std::vector<int8_t *> wq, wk, wv, wo, w13, w2;
-    std::vector<float *> sq, sk, sv, so, s13, s2;
-    float *kc = nullptr, *vc = nullptr, *x = nullptr, *q = nullptr, *att = nullptr, *xb = nullptr, *hb = nullptr,
+    std::vector<int8_t *> wqkv, wo, w13, w2;
+    std::vector<float *> sqkv, so, s13, s2;
+    float *kc = nullptr, *vc = nullptr, *x = nullptr, *q = nullptr, *att = nullptr, *hb = nullptr,
           *logits = nullptr, *xs = nullptr;
     int8_t *xq = nullptr;
 };
@@ -110,13 +112,11 @@ static void place(q3cu_model *m, Layout &L) {
     m->k_norm = L.take<float>(size_t(nl) * hd);
     m->tok_q = L.take<int8_t>(V * D);
     m->tok_s = L.take<float>(V * D / 64);
-    for (auto *v : {&m->wq, &m->wk, &m->wv, &m->wo, &m->w13, &m->w2}) v->assign(nl, nullptr);
-    for (auto *v : {&m->sq, &m->sk, &m->sv, &m->so, &m->s13, &m->s2}) v->assign(nl, nullptr);
+    for (auto *v : {&m->wqkv, &m->wo, &m->w13, &m->w2}) v->assign(nl, nullptr);
+    for (auto *v : {&m->sqkv, &m->so, &m->s13, &m->s2}) v->assign(nl, nullptr);
     const size_t A = m->ahd, K = m->kv_dim;
     for (int l = 0; l < nl; ++l) {
-        m->wq[l] = L.take<int8_t>(A * D);      m->sq[l] = L.take<float>(A * D / 64);
-        m->wk[l] = L.take<int8_t>(K * D);      m->sk[l] = L.take<float>(K * D / 64);
-        m->wv[l] = L.take<int8_t>(K * D);      m->sv[l] = L.take<float>(K * D / 64);
+        m->wqkv[l] = L.take<int8_t>((A + 2 * K) * D); m->sqkv[l] = L.take<float>((A + 2 * K) * D / 64);
         m->wo[l] = L.take<int8_t>(D * A);      m->so[l] = L.take<float>(D * A / 64);
         m->w13[l] = L.take<int8_t>(2 * H * D); m->s13[l] = L.take<float>(2 * H * D / 64);
         m->w2[l] = L.take<int8_t>(D * H);      m->s2[l] = L.take<float>(D * H / 64);
@@ -133,7 +133,6 @@ static void place(q3cu_model *m, Layout &L) {
     m->x = L.take<float>(D);
     m->q = L.take<float>(A);
     m->att = L.take<float>(size_t(c.n_heads) * S);
-    m->xb = L.take<float>(A);
     m->hb = L.take<float>(2 * H);
     m->logits = L.take<float>(V);
     const size_t qmax = D > A ? (D > H ? D : H) : (A > H ? A : H);
@@ -200,9 +199,11 @@ q3cu_status q3cu_model_load(q3cu_ctx *ctx, const void *checkpoint, size_t bytes,
     step(up(m->q_norm, size_t(nl) * hd * 4));
     step(up(m->k_norm, size_t(nl) * hd * 4));
     step(up_q8(m->tok_q, m->tok_s, V * D));
-    for (int l = 0; l < nl; ++l) step(up_q8(m->wq[l], m->sq[l], size_t(A) * D));
-    for (int l = 0; l < nl; ++l) step(up_q8(m->wk[l], m->sk[l], K * D));
-    for (int l = 0; l < nl; ++l) step(up_q8(m->wv[l], m->sv[l], K * D));
+    for (int l = 0; l < nl; ++l) step(up_q8(m->wqkv[l], m->sqkv[l], size_t(A) * D));                 // wq: rows 0..A-1
+    for (int l = 0; l < nl; ++l)                                                                        // wk: A..A+K-1
+        step(up_q8(m->wqkv[l] + size_t(A) * D, m->sqkv[l] + size_t(A) * D / 64, K * D));
+    for (int l = 0; l < nl; ++l)                                                                        // wv: A+K..
+        step(up_q8(m->wqkv[l] + (size_t(A) + K) * D, m->sqkv[l] + (size_t(A) + K) * D / 64, K * D));
     for (int l = 0; l < nl; ++l) step(up_q8(m->wo[l], m->so[l], D * size_t(A)));
     for (int l = 0; l < nl; ++l) step(up_q8(m->w13[l], m->s13[l], H * D));                       // w1: rows 0..H-1
     for (int l = 0; l < nl; ++l) step(up_q8(m->w2[l], m->s2[l], D * H));
@@ -255,19 +256,19 @@ q3cu_status q3cu_model_forward(q3cu_model *m, int token, int pos, float *logits_
         float *kr = m->kc + loff + int64_t(pos) * K, *vr = m->vc + loff + int64_t(pos) * K;
         // attention rmsnorm + quantize, QKV (:353-359)
         MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_att + int64_t(l) * D, 1, D, eps, m->xq, m->xs, stream));
-        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->wq[l], m->sq[l], D, A, m->q, s, m->sms), "wq");
-        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->wk[l], m->sk[l], D, K, kr, s, m->sms), "wk");
-        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->wv[l], m->sv[l], D, K, vr, s, m->sms), "wv");
+        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->wqkv[l], m->sqkv[l], D, A + 2 * K,
+                                      q3::MmOut{m->q, kr, vr, A, A + K}, s, m->sms),
+             "wq|wk|wv");
         // Q/K RMSNorm + RoPE, the key in its cache row (:361-393)
         MTRY(q3::launch_qk_norm_rope_tab(m->q, kr, c.n_heads, c.n_kv_heads, m->q_norm + int64_t(l) * hd,
                                          m->k_norm + int64_t(l) * hd, tab, eps, s),
              "qk_norm_rope");
         // attention (:395-428)
-        MTRY(q3::launch_attn_decode(m->q, m->kc + loff, m->vc + loff, m->att, m->xb, pos, c.n_heads, K, m->kv_mul, S,
-                                    s),
+        // attention + the quantize of its output (:395-428, :431)
+        MTRY(q3::launch_attn_decode(m->q, m->kc + loff, m->vc + loff, m->att, m->xq, m->xs, pos, c.n_heads, K,
+                                    m->kv_mul, S, s),
              "attention");
-        // output projection + residual (:431-435)
-        MCHK(q3cu_quantize_q8(ctx, m->xb, Q3CU_F32, 1, A, m->xq, m->xs, stream));
+        // output projection + residual (:432-435)
         MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->wo[l], m->so[l], A, D, m->x, s, m->sms, m->x), "wo");
         // FFN (:438-458)
         MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_ffn + int64_t(l) * D, 1, D, eps, m->xq, m->xs, stream));
