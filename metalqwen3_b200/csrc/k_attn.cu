@@ -54,6 +54,7 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__re
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kvh = h / kv_mul;
     const int npos = pos + 1, nch = (npos + AT_CH - 1) / AT_CH;
+    griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
     qs[tid] = q[int64_t(h) * AT_HD + tid];
     load_exp_table(tab);
     float *a = att + int64_t(h) * seq_len;

@@ -25,6 +25,10 @@
 // rounded up to a power of two), 32 / GL rows side by side, and U rows' loads
 // are in flight per lane.
 //
+// With `pdl`, the launch may overlap its predecessor (programmatic dependent
+// launch): every warp requests its first rows of W, then waits for the
+// predecessor (griddep_wait) before it reads x or add or writes anything.
+//
 // With `add` set, out = RN(add + val): the residual update that follows the
 // wo and w2 matmuls in the forward pass (x[i] += xb[i], :434 and :457), one
 // rounding as there; out may equal add.
@@ -67,6 +71,7 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
     const int64_t jobs = int64_t(tiles) * ntb;
     const int slots = RB * TB;                      // (row, token) pairs of a tile, <= 32
     float(*tw)[33] = terms[warp];
+    bool waited = false;                            // griddep_wait done (before the first read of x / add)
 
     for (int64_t job = int64_t(blockIdx.x) * MM_WARPS + warp; job < jobs; job += int64_t(gridDim.x) * MM_WARPS) {
         const int tile = int(job % tiles), tb = int(job / tiles);
@@ -76,6 +81,29 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
         for (int g0 = 0; g0 < G; g0 += GL) {
             const int g = g0 + gi;
             const bool gl = g < G;
+            U8 wa[U], wb[U];
+            float wsc[U];
+            bool ok[U];
+            auto load_w = [&](int r) {                  // U rows' codes and scales in flight
+#pragma unroll
+                for (int u = 0; u < U; ++u) {
+                    const int rr = r + u * RP + sub;
+                    ok[u] = gl && rr < rmax;
+                    if (ok[u]) {
+                        const int64_t row = i0 + rr;
+                        wa[u] = ld_nc_v8(wq + row * n + int64_t(g) * GS);
+                        wb[u] = ld_nc_v8(wq + row * n + int64_t(g) * GS + 32);
+                        wsc[u] = ws[row * G + g];
+                    }
+                }
+            };
+            // the first rows' weights are constant data: they are requested before
+            // the wait for the kernel that produced x (programmatic dependent launch)
+            load_w(0);
+            if (!waited) {
+                griddep_wait();
+                waited = true;
+            }
             U8 xa[TB], xb[TB];
             float xsc[TB];
 #pragma unroll
@@ -92,20 +120,7 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
                 }
             }
             for (int r = 0; r < rmax; r += RP * U) {
-                U8 wa[U], wb[U];
-                float wsc[U];
-                bool ok[U];
-#pragma unroll
-                for (int u = 0; u < U; ++u) {        // U rows' loads in flight
-                    const int rr = r + u * RP + sub;
-                    ok[u] = gl && rr < rmax;
-                    if (ok[u]) {
-                        const int64_t row = i0 + rr;
-                        wa[u] = ld_nc_v8(wq + row * n + int64_t(g) * GS);
-                        wb[u] = ld_nc_v8(wq + row * n + int64_t(g) * GS + 32);
-                        wsc[u] = ws[row * G + g];
-                    }
-                }
+                if (r > 0) load_w(r);
 #pragma unroll
                 for (int u = 0; u < U; ++u) {
                     const int rr = r + u * RP + sub;
@@ -151,7 +166,7 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
 
 template <int TB>
 static cudaError_t launch_mm_t(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
-                               int d, const float *add, const MmOut &out, cudaStream_t stream, int sms) {
+                               int d, const float *add, const MmOut &out, cudaStream_t stream, int sms, bool pdl) {
     const int ntb = (B + TB - 1) / TB;
     // Rows per tile: enough jobs for ~16 warps per SM, at most 32 / TB (one lane per (row, token)).
     const int64_t want = int64_t(sms) * 16;
@@ -162,22 +177,34 @@ static cudaError_t launch_mm_t(const int8_t *xq, const float *xs, int B, const i
     const int64_t jobs = int64_t((d + RB - 1) / RB) * ntb;
     int64_t grid = (jobs + MM_WARPS - 1) / MM_WARPS;
     if (grid > int64_t(sms) * 8) grid = int64_t(sms) * 8;
-    matmul_q8_kernel<TB, TB == 1 ? 4 : 2><<<unsigned(grid), MM_THREADS, 0, stream>>>(xq, xs, B, wq, ws, n, d, RB,
-                                                                                    add, out);
-    return cudaGetLastError();
+    if (!pdl) {
+        matmul_q8_kernel<TB, TB == 1 ? 4 : 2><<<unsigned(grid), MM_THREADS, 0, stream>>>(xq, xs, B, wq, ws, n, d, RB,
+                                                                                        add, out);
+        return cudaGetLastError();
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(unsigned(grid));
+    cfg.blockDim = dim3(MM_THREADS);
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, matmul_q8_kernel<TB, TB == 1 ? 4 : 2>, xq, xs, B, wq, ws, n, d, RB, add, out);
 }
 
 cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
                              int d, float *out, cudaStream_t stream, int sms, const float *add) {
-    return launch_matmul_q8_seg(xq, xs, B, wq, ws, n, d, MmOut{out, out, out, d, d}, stream, sms, add);
+    return launch_matmul_q8_seg(xq, xs, B, wq, ws, n, d, MmOut{out, out, out, d, d}, stream, sms, add, false);
 }
 
 cudaError_t launch_matmul_q8_seg(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
-                                 int d, const MmOut &out, cudaStream_t stream, int sms, const float *add) {
+                                 int d, const MmOut &out, cudaStream_t stream, int sms, const float *add, bool pdl) {
     if (B == 0 || d == 0) return cudaSuccess;
-    if (B == 1) return launch_mm_t<1>(xq, xs, B, wq, ws, n, d, add, out, stream, sms);
-    if (B == 2) return launch_mm_t<2>(xq, xs, B, wq, ws, n, d, add, out, stream, sms);
-    return launch_mm_t<4>(xq, xs, B, wq, ws, n, d, add, out, stream, sms);
+    if (B == 1) return launch_mm_t<1>(xq, xs, B, wq, ws, n, d, add, out, stream, sms, pdl);
+    if (B == 2) return launch_mm_t<2>(xq, xs, B, wq, ws, n, d, add, out, stream, sms, pdl);
+    return launch_mm_t<4>(xq, xs, B, wq, ws, n, d, add, out, stream, sms, pdl);
 }
 
 }  // namespace q3

@@ -409,6 +409,7 @@ __global__ void __launch_bounds__(RSM_THREADS) rmsnorm_row_kernel(const T *x, co
     extern __shared__ __align__(128) uint8_t rbuf[];
     __shared__ __align__(8) uint64_t bar[RSM_MAXCH];
     __shared__ float ss_sh;
+    griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
     const int tid = threadIdx.x;
     const int64_t row = blockIdx.x;
     const int row_bytes = dim * ESZ;

@@ -102,6 +102,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 3 : 2) swiglu_v8_kernel(
     constexpr int LPG = GS / N;
     constexpr int STEP = 32 * N;
     __shared__ ExpTab s_tab;
+    griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
     load_exp_table(s_tab);
     __syncthreads();
 

@@ -71,6 +71,15 @@ __device__ __forceinline__ void st_cs_f32(float *p, float v) {
     asm volatile("st.global.cs.f32 [%0], %1;" :: "l"(p), "f"(v) : "memory");
 }
 
+// Programmatic dependent launch (sm_90+).  A kernel launched with the
+// programmatic-serialization attribute may start before its predecessor
+// finishes; griddep_wait() blocks until the predecessor has completed and its
+// writes are visible (it returns at once for an ordinary launch).
+// griddep_launch_dependents() lets such a successor be scheduled now; it
+// changes nothing for ordinary successors.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float4 u4_as_f4(uint4 u) {
     return make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z), __uint_as_float(u.w));
 }

@@ -46,8 +46,11 @@ struct MmOut {
     float *p0, *p1, *p2;
     int e0, e1;
 };
+// pdl: launched with programmatic stream serialization (may overlap the
+// previous kernel in the stream, which must not read what this one writes).
 cudaError_t launch_matmul_q8_seg(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
-                                 int d, const MmOut &out, cudaStream_t stream, int sms, const float *add = nullptr);
+                                 int d, const MmOut &out, cudaStream_t stream, int sms, const float *add = nullptr,
+                                 bool pdl = false);
 // out = W @ x for each token row; with `add`, out = add + W @ x (one rounding).
 cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
                              int d, float *out, cudaStream_t stream, int sms, const float *add = nullptr);

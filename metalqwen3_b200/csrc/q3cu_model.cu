@@ -20,7 +20,9 @@
 // and quantizes its own output (k_attn.cu).  Weights that share an input are
 // stored as one matrix -- Q|K|V as [A+2K][dim], its output rows going to q and
 // to this position's K and V cache rows; W1|W3 as [2H][dim] -- so a layer is
-// 9 launches.  Weights, KV cache and run state
+// 9 launches.  The matmuls are launched as programmatic dependents of the
+// kernel before them (their weight loads start while it finishes; no matmul
+// here writes what its predecessor reads).  Weights, KV cache and run state
 // live in one device allocation made at load; forward allocates nothing.
 #include <cmath>
 #include <cstdarg>
@@ -257,7 +259,7 @@ q3cu_status q3cu_model_forward(q3cu_model *m, int token, int pos, float *logits_
         // attention rmsnorm + quantize, QKV (:353-359)
         MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_att + int64_t(l) * D, 1, D, eps, m->xq, m->xs, stream));
         MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->wqkv[l], m->sqkv[l], D, A + 2 * K,
-                                      q3::MmOut{m->q, kr, vr, A, A + K}, s, m->sms),
+                                      q3::MmOut{m->q, kr, vr, A, A + K}, s, m->sms, nullptr, true),
              "wq|wk|wv");
         // Q/K RMSNorm + RoPE, the key in its cache row (:361-393)
         MTRY(q3::launch_qk_norm_rope_tab(m->q, kr, c.n_heads, c.n_kv_heads, m->q_norm + int64_t(l) * hd,
@@ -269,16 +271,24 @@ q3cu_status q3cu_model_forward(q3cu_model *m, int token, int pos, float *logits_
                                     m->kv_mul, S, s),
              "attention");
         // output projection + residual (:432-435)
-        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->wo[l], m->so[l], A, D, m->x, s, m->sms, m->x), "wo");
+        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->wo[l], m->so[l], A, D, q3::MmOut{m->x, m->x, m->x, D, D}, s,
+                                      m->sms, m->x, true),
+             "wo");
         // FFN (:438-458)
         MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_ffn + int64_t(l) * D, 1, D, eps, m->xq, m->xs, stream));
-        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->w13[l], m->s13[l], D, 2 * H, m->hb, s, m->sms), "w1|w3");
+        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->w13[l], m->s13[l], D, 2 * H,
+                                      q3::MmOut{m->hb, m->hb, m->hb, 2 * H, 2 * H}, s, m->sms, nullptr, true),
+             "w1|w3");
         MCHK(q3cu_swiglu_q8(ctx, m->hb, m->hb + H, Q3CU_F32, 1, H, m->xq, m->xs, stream));
-        MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->w2[l], m->s2[l], H, D, m->x, s, m->sms, m->x), "w2");
+        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->w2[l], m->s2[l], H, D, q3::MmOut{m->x, m->x, m->x, D, D}, s,
+                                      m->sms, m->x, true),
+             "w2");
     }
     // final rmsnorm + classifier (:462-466)
     MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_final, 1, D, eps, m->xq, m->xs, stream));
-    MTRY(q3::launch_matmul_q8(m->xq, m->xs, 1, m->cls_q, m->cls_s, D, c.vocab_size, m->logits, s, m->sms),
+    MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->cls_q, m->cls_s, D, c.vocab_size,
+                                  q3::MmOut{m->logits, m->logits, m->logits, c.vocab_size, c.vocab_size}, s, m->sms,
+                                  nullptr, true),
          "classifier");
     if (logits_host) {
         MTRY(cudaMemcpyAsync(logits_host, m->logits, size_t(c.vocab_size) * 4, cudaMemcpyDeviceToHost, s), "logits D2H");
