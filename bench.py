@@ -779,8 +779,9 @@ class Forward06B(Workload):
 
     h2d_keys = ()
     d2h_keys = ()
-    e2e_note = ("the token id goes in by value and the logits come back to the host inside the call "
-                f"(607,744 bytes); no graph")
+    e2e_note = ("the token id and position go in by value (the library copies them and RoPE's table to the "
+                "device and replays its own graph of the step); the logits come back to the host inside the call "
+                "(607,744 bytes)")
 
     def cpu_step(self, oracle, np, sample, threads, rng):
         """One decode token by the reference's own qwen3_forward on the same checkpoint file."""

@@ -44,7 +44,8 @@ __device__ __forceinline__ void attn_stage(uint8_t *buf, const float *cache, int
 
 __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__restrict__ q, const float *kc,
                                                                const float *vc, float *att, int8_t *xq, float *xs,
-                                                               int pos, int kv_dim, int kv_mul, int seq_len) {
+                                                               const StepParams *__restrict__ sp, int kv_dim,
+                                                               int kv_mul, int seq_len) {
     extern __shared__ __align__(16) uint8_t tiles[];        // [2][AT_BUF]
     __shared__ __align__(16) float qs[AT_HD];
     __shared__ ExpTab tab;
@@ -53,6 +54,7 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__re
     __shared__ float gmax[2];
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kvh = h / kv_mul;
+    const int pos = sp->pos;                                // this step's position (device memory)
     const int npos = pos + 1, nch = (npos + AT_CH - 1) / AT_CH;
     griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
     qs[tid] = q[int64_t(h) * AT_HD + tid];
@@ -142,49 +144,80 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__re
 
 // Q/K RMSNorm + RoPE of one token (qwen3_original.c:361-393) with the
 // rotation's cos/sin given by the host: the reference takes them from the C
-// library (cosf/sinf of pos*freq, :368), so the host computing them with the
-// same calls makes the rotation bit-exact.  One warp per head row (the n_heads
-// query rows, then the n_kv key rows): lane 0 runs the row's sum of squares in
-// index order (rmsnorm, :278-289), then every lane normalises and rotates four
-// elements: x' = w*(ss*x), then (x, y) -> (x c - y s, x s + y c), each product
-// and sum rounded once.
-__global__ void __launch_bounds__(128) qk_norm_rope_tab_kernel(float *q, float *k, int n_heads, int n_kv,
-                                                               const float *__restrict__ qn,
-                                                               const float *__restrict__ kn, RopeTab tab,
-                                                               float eps) {
+// library (cosf/sinf of pos*freq, :367-368), so the host computing them with
+// the same calls makes the rotation bit-exact; they reach the device in the
+// step's parameters, with the position.  The Q|K|V matmul left this token's
+// rows in qkv = [q | k | v]: one warp per head row normalises and rotates the
+// n_heads query rows in place and the n_kv key rows into their cache row at
+// pos (:349-350, keys rotated in the cache as the reference does), and n_kv
+// more warps copy the value rows into theirs.  Lane 0 runs a row's sum of
+// squares in index order (rmsnorm, :278-289); then every lane normalises and
+// rotates four elements: x' = w*(ss*x), (x, y) -> (x c - y s, x s + y c), each
+// product and sum rounded once.
+__global__ void __launch_bounds__(128) qk_norm_rope_step_kernel(float *qkv, float *kc, float *vc, int n_heads, int n_kv,
+                                                                const float *__restrict__ qn,
+                                                                const float *__restrict__ kn,
+                                                                const StepParams *__restrict__ sp, float eps) {
     const int lane = threadIdx.x & 31;
     const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
-    if (row >= n_heads + n_kv) return;                       // whole warps
-    float *v = row < n_heads ? q + int64_t(row) * AT_HD : k + int64_t(row - n_heads) * AT_HD;
-    const float *w = row < n_heads ? qn : kn;
+    if (row >= n_heads + 2 * n_kv) return;                  // whole warps
+    const int kv_dim = n_kv * AT_HD, pos = sp->pos;
+    if (row >= n_heads + n_kv) {                              // value row: copy into the cache
+        const int r = row - n_heads - n_kv;
+        const float *src = qkv + int64_t(n_heads) * AT_HD + kv_dim + r * AT_HD;
+        float *dst = vc + int64_t(pos) * kv_dim + r * AT_HD;
+        reinterpret_cast<float4 *>(dst)[lane] = reinterpret_cast<const float4 *>(src)[lane];
+        return;
+    }
+    const bool isq = row < n_heads;
+    const float *v = isq ? qkv + int64_t(row) * AT_HD : qkv + int64_t(n_heads) * AT_HD + (row - n_heads) * AT_HD;
+    float *o = isq ? qkv + int64_t(row) * AT_HD : kc + int64_t(pos) * kv_dim + (row - n_heads) * AT_HD;
+    const float *w = isq ? qn : kn;
     float ss = 0.0f;
     if (lane == 0) {
         for (int i = 0; i < AT_HD; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
         ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(AT_HD)), eps)));
     }
     ss = __shfl_sync(FULL, ss, 0);
+    float x[2], y[2];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        const int j = lane + 32 * u;                         // pair (j, j + 64)
-        const float x = __fmul_rn(w[j], __fmul_rn(ss, v[j]));
-        const float y = __fmul_rn(w[j + 64], __fmul_rn(ss, v[j + 64]));
-        const float c = tab.c[j], s = tab.s[j];
-        v[j] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s));
-        v[j + 64] = __fadd_rn(__fmul_rn(x, s), __fmul_rn(y, c));
+    for (int u = 0; u < 2; ++u) {                            // read the row before any lane writes it
+        const int j = lane + 32 * u;
+        x[u] = __fmul_rn(w[j], __fmul_rn(ss, v[j]));
+        y[u] = __fmul_rn(w[j + 64], __fmul_rn(ss, v[j + 64]));
+    }
+    __syncwarp();
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {                            // pair (j, j + 64)
+        const int j = lane + 32 * u;
+        const float c = sp->c[j], s = sp->s[j];
+        o[j] = __fsub_rn(__fmul_rn(x[u], c), __fmul_rn(y[u], s));
+        o[j + 64] = __fadd_rn(__fmul_rn(x[u], s), __fmul_rn(y[u], c));
     }
 }
 
-cudaError_t launch_qk_norm_rope_tab(float *q, float *k, int n_heads, int n_kv, const float *qn, const float *kn,
-                                    const RopeTab &tab, float eps, cudaStream_t stream) {
-    qk_norm_rope_tab_kernel<<<(n_heads + n_kv + 3) / 4, 128, 0, stream>>>(q, k, n_heads, n_kv, qn, kn, tab, eps);
+cudaError_t launch_qk_norm_rope_step(float *qkv, float *kc, float *vc, int n_heads, int n_kv, const float *qn,
+                                     const float *kn, const StepParams *sp, float eps, cudaStream_t stream) {
+    qk_norm_rope_step_kernel<<<(n_heads + 2 * n_kv + 3) / 4, 128, 0, stream>>>(qkv, kc, vc, n_heads, n_kv, qn, kn,
+                                                                                 sp, eps);
+    return cudaGetLastError();
+}
+
+__global__ void set_step_kernel(StepParams *sp, StepParams v) {
+    reinterpret_cast<uint32_t *>(sp)[threadIdx.x] = reinterpret_cast<const uint32_t *>(&v)[threadIdx.x];
+}
+
+cudaError_t launch_set_step(StepParams *sp, const StepParams &v, cudaStream_t stream) {
+    set_step_kernel<<<1, sizeof(StepParams) / 4, 0, stream>>>(sp, v);
     return cudaGetLastError();
 }
 
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, int8_t *xq, float *xs,
-                               int pos, int n_heads, int kv_dim, int kv_mul, int seq_len, cudaStream_t stream) {
+                               const StepParams *sp, int n_heads, int kv_dim, int kv_mul, int seq_len,
+                               cudaStream_t stream) {
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_decode_kernel), AT_SMEM, 24);
     if (e != cudaSuccess) return e;
-    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(q, kc, vc, att, xq, xs, pos, kv_dim, kv_mul, seq_len);
+    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(q, kc, vc, att, xq, xs, sp, kv_dim, kv_mul, seq_len);
     return cudaGetLastError();
 }
 

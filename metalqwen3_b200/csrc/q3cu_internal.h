@@ -55,18 +55,24 @@ cudaError_t launch_matmul_q8_seg(const int8_t *xq, const float *xs, int B, const
 cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
                              int d, float *out, cudaStream_t stream, int sms, const float *add = nullptr);
 
-// Decode attention of one token at `pos` (head_dim 128): q [n_heads][128],
+// One decode step's parameters, in device memory: the token, its position and
+// RoPE's cos/sin(pos * freq_j) for j < 64 (head_dim 128), computed on the host.
+struct StepParams {
+    int32_t pos, token, pad0, pad1;
+    float c[64], s[64];
+};
+// Writes v to *sp in stream order (a kernel: usable inside any stream capture).
+cudaError_t launch_set_step(StepParams *sp, const StepParams &v, cudaStream_t stream);
+// Q/K RMSNorm + RoPE of the step's token from qkv = [q | k | v] (head_dim 128):
+// q rotated in place, k rotated into kc's row sp->pos, v copied into vc's.
+cudaError_t launch_qk_norm_rope_step(float *qkv, float *kc, float *vc, int n_heads, int n_kv, const float *qn,
+                                     const float *kn, const StepParams *sp, float eps, cudaStream_t stream);
+// Decode attention of one token at sp->pos (head_dim 128): q [n_heads][128],
 // kc / vc the layer's caches [seq_len][kv_dim], att [n_heads][seq_len] scratch;
 // the output [n_heads][128] as Q8_0 codes xq and scales xs [n_heads * 2].
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, int8_t *xq, float *xs,
-                               int pos, int n_heads, int kv_dim, int kv_mul, int seq_len, cudaStream_t stream);
-// Q/K RMSNorm + RoPE of one token, head_dim 128, in place; tab holds
-// cos/sin(pos * freq_j) for j < 64, computed by the caller.
-struct RopeTab {
-    float c[64], s[64];
-};
-cudaError_t launch_qk_norm_rope_tab(float *q, float *k, int n_heads, int n_kv, const float *qn, const float *kn,
-                                    const RopeTab &tab, float eps, cudaStream_t stream);
+                               const StepParams *sp, int n_heads, int kv_dim, int kv_mul, int seq_len,
+                               cudaStream_t stream);
 
 
 cudaError_t launch_swiglu(const void *hb, const void *hb2, q3cu_dtype dt, int64_t elems, void *out, int8_t *q,

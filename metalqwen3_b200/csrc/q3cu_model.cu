@@ -42,9 +42,13 @@ struct q3cu_model {
     float *tok_s = nullptr, *cls_s = nullptr;
     std::vector<int8_t *> wqkv, wo, w13, w2;
     std::vector<float *> sqkv, so, s13, s2;
-    float *kc = nullptr, *vc = nullptr, *x = nullptr, *q = nullptr, *att = nullptr, *hb = nullptr,
+    float *kc = nullptr, *vc = nullptr, *x = nullptr, *qkv = nullptr, *att = nullptr, *hb = nullptr,
           *logits = nullptr, *xs = nullptr;
     int8_t *xq = nullptr;
+    q3::StepParams *step = nullptr;           // this step's position, token and RoPE table
+    cudaStream_t own = nullptr;               // the model's stream: its graph runs there
+    cudaEvent_t ev_in = nullptr, ev_out = nullptr;
+    cudaGraphExec_t graph = nullptr;          // one decode step, captured at the first call
 };
 
 namespace {
@@ -133,13 +137,14 @@ static void place(q3cu_model *m, Layout &L) {
     m->kc = L.take<float>(size_t(nl) * S * K);
     m->vc = L.take<float>(size_t(nl) * S * K);
     m->x = L.take<float>(D);
-    m->q = L.take<float>(A);
+    m->qkv = L.take<float>(A + 2 * K);
     m->att = L.take<float>(size_t(c.n_heads) * S);
     m->hb = L.take<float>(2 * H);
     m->logits = L.take<float>(V);
     const size_t qmax = D > A ? (D > H ? D : H) : (A > H ? A : H);
     m->xq = L.take<int8_t>(qmax);
     m->xs = L.take<float>(qmax / 64);
+    m->step = L.take<q3::StepParams>(1);
 }
 
 extern "C" {
@@ -217,6 +222,15 @@ q3cu_status q3cu_model_load(q3cu_ctx *ctx, const void *checkpoint, size_t bytes,
     e = cudaMemset(m->kc, 0, size_t(nl) * c.seq_len * K * 4);
     if (e == cudaSuccess) e = cudaMemset(m->vc, 0, size_t(nl) * c.seq_len * K * 4);
     if (e != cudaSuccess) return fail_free(cuda_err(e, "cudaMemset (KV cache)"));
+    e = cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming);
+    if (e != cudaSuccess) {
+        if (m->ev_in) cudaEventDestroy(m->ev_in);
+        if (m->ev_out) cudaEventDestroy(m->ev_out);
+        if (m->own) cudaStreamDestroy(m->own);
+        return fail_free(cuda_err(e, "stream / events"));
+    }
     *out = m;
     return Q3CU_OK;
 }
@@ -229,6 +243,79 @@ q3cu_status q3cu_model_config(const q3cu_model *m, q3cu_config *out) {
 
 const float *q3cu_model_logits(const q3cu_model *m) { return m ? m->logits : nullptr; }
 
+}  // extern "C"
+
+// Every launch of one decode step, in order, on stream s (the step's position
+// and token are read from m->step on the device).
+static q3cu_status enqueue_step(q3cu_model *m, cudaStream_t s) {
+    q3cu_ctx *ctx = m->ctx;
+    const q3cu_config &c = m->cfg;
+    const int D = c.dim, H = c.hidden_dim, A = m->ahd, K = m->kv_dim, hd = c.head_dim, S = c.seq_len;
+    const float eps = 1e-6f;                                   // rmsnorm's constant (:283)
+    const q3cu_stream st = s;
+    // token embedding (:342): the row of the dequantized table
+    MCHK(q3cu_embed_gather(ctx, m->tok_q, m->tok_s, c.vocab_size, D, &m->step->token, 1, m->x, nullptr, nullptr, st));
+    for (int l = 0; l < c.n_layers; ++l) {
+        const int64_t loff = int64_t(l) * S * K;
+        // attention rmsnorm + quantize, Q|K|V (:353-359)
+        MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_att + int64_t(l) * D, 1, D, eps, m->xq, m->xs, st));
+        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->wqkv[l], m->sqkv[l], D, A + 2 * K,
+                                      q3::MmOut{m->qkv, m->qkv, m->qkv, A + 2 * K, A + 2 * K}, s, m->sms, nullptr,
+                                      true),
+             "wq|wk|wv");
+        // Q/K RMSNorm + RoPE; the key and the value into their cache rows (:349-350, :361-393)
+        MTRY(q3::launch_qk_norm_rope_step(m->qkv, m->kc + loff, m->vc + loff, c.n_heads, c.n_kv_heads,
+                                          m->q_norm + int64_t(l) * hd, m->k_norm + int64_t(l) * hd, m->step, eps, s),
+             "qk_norm_rope");
+        // attention + the quantize of its output (:395-428, :431)
+        MTRY(q3::launch_attn_decode(m->qkv, m->kc + loff, m->vc + loff, m->att, m->xq, m->xs, m->step, c.n_heads, K,
+                                    m->kv_mul, S, s),
+             "attention");
+        // output projection + residual (:432-435)
+        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->wo[l], m->so[l], A, D, q3::MmOut{m->x, m->x, m->x, D, D}, s,
+                                      m->sms, m->x, true),
+             "wo");
+        // FFN (:438-458)
+        MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_ffn + int64_t(l) * D, 1, D, eps, m->xq, m->xs, st));
+        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->w13[l], m->s13[l], D, 2 * H,
+                                      q3::MmOut{m->hb, m->hb, m->hb, 2 * H, 2 * H}, s, m->sms, nullptr, true),
+             "w1|w3");
+        MCHK(q3cu_swiglu_q8(ctx, m->hb, m->hb + H, Q3CU_F32, 1, H, m->xq, m->xs, st));
+        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->w2[l], m->s2[l], H, D, q3::MmOut{m->x, m->x, m->x, D, D}, s,
+                                      m->sms, m->x, true),
+             "w2");
+    }
+    // final rmsnorm + classifier (:462-466)
+    MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_final, 1, D, eps, m->xq, m->xs, st));
+    MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->cls_q, m->cls_s, D, c.vocab_size,
+                                  q3::MmOut{m->logits, m->logits, m->logits, c.vocab_size, c.vocab_size}, s, m->sms,
+                                  nullptr, true),
+         "classifier");
+    return Q3CU_OK;
+}
+
+// The step captured once as a CUDA graph on the model's own stream.
+static q3cu_status capture_step(q3cu_model *m) {
+    MTRY(cudaStreamBeginCapture(m->own, cudaStreamCaptureModeRelaxed), "cudaStreamBeginCapture");
+    const q3cu_status st = enqueue_step(m, m->own);
+    cudaGraph_t g = nullptr;
+    const cudaError_t e = cudaStreamEndCapture(m->own, &g);
+    if (st != Q3CU_OK) {
+        if (g) cudaGraphDestroy(g);
+        return st;
+    }
+    if (e != cudaSuccess) return cuda_err(e, "cudaStreamEndCapture");
+    const cudaError_t e2 = cudaGraphInstantiate(&m->graph, g, 0);
+    cudaGraphDestroy(g);
+    if (e2 != cudaSuccess) {
+        m->graph = nullptr;
+        return cuda_err(e2, "cudaGraphInstantiate");
+    }
+    return Q3CU_OK;
+}
+
+extern "C" {
+
 q3cu_status q3cu_model_forward(q3cu_model *m, int token, int pos, float *logits_host, q3cu_stream stream) {
     if (!m) return err(Q3CU_ERR_INVALID, "model is NULL");
     q3cu_ctx *ctx = m->ctx;
@@ -238,58 +325,35 @@ q3cu_status q3cu_model_forward(q3cu_model *m, int token, int pos, float *logits_
     if (pos < 0 || pos >= c.seq_len) return err(Q3CU_ERR_INDEX, "pos %d outside [0, %d)", pos, c.seq_len);
     MCHK(q3::ctx_use_device(ctx));
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const int D = c.dim, H = c.hidden_dim, A = m->ahd, K = m->kv_dim, hd = c.head_dim, S = c.seq_len;
-    const float eps = 1e-6f;                                   // rmsnorm's constant (:283)
-    // RoPE's cos/sin for this position with the C library's calls, as the
-    // reference makes them (:367-368): freq = powf(1e6, -(float)j / (hd/2)),
-    // cosf / sinf of the binary32 product pos * freq.
-    q3::RopeTab tab;
+    // The step's parameters: RoPE's cos/sin for this position with the C
+    // library's calls, as the reference makes them (:367-368):
+    // freq = powf(1e6, -(float)j / (hd/2)), cosf / sinf of the binary32 product pos * freq.
+    q3::StepParams sp{};
+    sp.pos = pos;
+    sp.token = token;
+    const int hd = c.head_dim;
     for (int j = 0; j < hd / 2; ++j) {
         const float freq = powf(1e6f, -float(j) / float(hd / 2));
         const float ang = float(pos) * freq;
-        tab.c[j] = cosf(ang);
-        tab.s[j] = sinf(ang);
+        sp.c[j] = cosf(ang);
+        sp.s[j] = sinf(ang);
     }
-    // token embedding (:342): the row of the dequantized table
-    MCHK(q3cu_dequantize_q8(ctx, m->tok_q + int64_t(token) * D, m->tok_s + int64_t(token) * (D / 64), D, m->x,
-                            stream));
-    for (int l = 0; l < c.n_layers; ++l) {
-        const int64_t loff = int64_t(l) * S * K;
-        float *kr = m->kc + loff + int64_t(pos) * K, *vr = m->vc + loff + int64_t(pos) * K;
-        // attention rmsnorm + quantize, QKV (:353-359)
-        MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_att + int64_t(l) * D, 1, D, eps, m->xq, m->xs, stream));
-        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->wqkv[l], m->sqkv[l], D, A + 2 * K,
-                                      q3::MmOut{m->q, kr, vr, A, A + K}, s, m->sms, nullptr, true),
-             "wq|wk|wv");
-        // Q/K RMSNorm + RoPE, the key in its cache row (:361-393)
-        MTRY(q3::launch_qk_norm_rope_tab(m->q, kr, c.n_heads, c.n_kv_heads, m->q_norm + int64_t(l) * hd,
-                                         m->k_norm + int64_t(l) * hd, tab, eps, s),
-             "qk_norm_rope");
-        // attention (:395-428)
-        // attention + the quantize of its output (:395-428, :431)
-        MTRY(q3::launch_attn_decode(m->q, m->kc + loff, m->vc + loff, m->att, m->xq, m->xs, pos, c.n_heads, K,
-                                    m->kv_mul, S, s),
-             "attention");
-        // output projection + residual (:432-435)
-        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->wo[l], m->so[l], A, D, q3::MmOut{m->x, m->x, m->x, D, D}, s,
-                                      m->sms, m->x, true),
-             "wo");
-        // FFN (:438-458)
-        MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_ffn + int64_t(l) * D, 1, D, eps, m->xq, m->xs, stream));
-        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->w13[l], m->s13[l], D, 2 * H,
-                                      q3::MmOut{m->hb, m->hb, m->hb, 2 * H, 2 * H}, s, m->sms, nullptr, true),
-             "w1|w3");
-        MCHK(q3cu_swiglu_q8(ctx, m->hb, m->hb + H, Q3CU_F32, 1, H, m->xq, m->xs, stream));
-        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->w2[l], m->s2[l], H, D, q3::MmOut{m->x, m->x, m->x, D, D}, s,
-                                      m->sms, m->x, true),
-             "w2");
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    MTRY(cudaStreamIsCapturing(s, &cap), "cudaStreamIsCapturing");
+    if (cap != cudaStreamCaptureStatusNone) {
+        // inside the caller's capture: the launches join it, the parameters as a kernel
+        MTRY(q3::launch_set_step(m->step, sp, s), "step parameters");
+        MCHK(enqueue_step(m, s));
+    } else {
+        // the model's own graph, replayed on its stream between two events on the caller's
+        MTRY(cudaEventRecord(m->ev_in, s), "cudaEventRecord");
+        MTRY(cudaStreamWaitEvent(m->own, m->ev_in, 0), "cudaStreamWaitEvent");
+        MTRY(cudaMemcpyAsync(m->step, &sp, sizeof(sp), cudaMemcpyHostToDevice, m->own), "step parameters");
+        if (!m->graph) MCHK(capture_step(m));
+        MTRY(cudaGraphLaunch(m->graph, m->own), "cudaGraphLaunch");
+        MTRY(cudaEventRecord(m->ev_out, m->own), "cudaEventRecord");
+        MTRY(cudaStreamWaitEvent(s, m->ev_out, 0), "cudaStreamWaitEvent");
     }
-    // final rmsnorm + classifier (:462-466)
-    MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_final, 1, D, eps, m->xq, m->xs, stream));
-    MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->cls_q, m->cls_s, D, c.vocab_size,
-                                  q3::MmOut{m->logits, m->logits, m->logits, c.vocab_size, c.vocab_size}, s, m->sms,
-                                  nullptr, true),
-         "classifier");
     if (logits_host) {
         MTRY(cudaMemcpyAsync(logits_host, m->logits, size_t(c.vocab_size) * 4, cudaMemcpyDeviceToHost, s), "logits D2H");
         MTRY(cudaStreamSynchronize(s), "cudaStreamSynchronize");
@@ -301,6 +365,11 @@ q3cu_status q3cu_model_forward(q3cu_model *m, int token, int pos, float *logits_
 q3cu_status q3cu_model_destroy(q3cu_model *m) {
     if (!m) return Q3CU_OK;
     if (q3::ctx_alive(m->ctx)) q3::ctx_use_device(m->ctx);
+    if (m->own) cudaStreamSynchronize(m->own);
+    if (m->graph) cudaGraphExecDestroy(m->graph);
+    if (m->ev_in) cudaEventDestroy(m->ev_in);
+    if (m->ev_out) cudaEventDestroy(m->ev_out);
+    if (m->own) cudaStreamDestroy(m->own);
     cudaError_t e = m->arena ? cudaFree(m->arena) : cudaSuccess;
     delete m;
     return e == cudaSuccess ? Q3CU_OK : cuda_err(e, "cudaFree (model)");
