@@ -771,7 +771,7 @@ class Forward06B(Workload):
         gr.replay()
         if events is not None:
             events[0][1].record(stream)
-        return 9 * self.layers + 3
+        return 9 * self.layers + 4                 # + the kernel that stores the step parameters
 
     def launch_e2e(self, q3, d, stream):
         self._model(q3, d).forward(7, self.pos, stream=stream, to_host=True)
