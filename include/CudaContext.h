@@ -18,6 +18,7 @@
 
 #include <cstdint>
 #include <string>
+#include <vector>
 
 #include "q3cu.h"
 
@@ -73,6 +74,29 @@ private:
     int device_;
     q3cu_ctx *ctx_ = nullptr;
     std::string last_error_;
+};
+
+// The reference's Transformer on the device: a checkpoint image loaded once
+// (build_transformer / read_checkpoint, src/cpu/qwen3_original.c:185-258) and
+// its decode step (forward, :333-468), through q3cu_model_*.  forward()
+// returns the logits like the reference's forward does (a buffer the object
+// owns, valid until the next call), with the reference's bits.  Throws
+// std::runtime_error on failure.
+class CudaModel {
+public:
+    CudaModel(CudaContext &ctx, const void *checkpoint, size_t bytes, int ctx_length = 0);
+    ~CudaModel();
+    CudaModel(const CudaModel &) = delete;
+    CudaModel &operator=(const CudaModel &) = delete;
+
+    const q3cu_config &config() const { return cfg_; }
+    const float *forward(int token, int pos);          // host logits [vocab], synchronous
+    const float *deviceLogits() const;                 // the same logits on the device
+
+private:
+    q3cu_model *m_ = nullptr;
+    q3cu_config cfg_{};
+    std::vector<float> logits_;
 };
 
 #endif

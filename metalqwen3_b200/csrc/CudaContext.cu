@@ -90,3 +90,25 @@ void CudaContext::embedGather(const int8_t *tq, const float *ts, int vocab, int 
 void CudaContext::checkDeviceStatus(q3cu_stream stream) {
     check(q3cu_device_status(ctx_, stream, nullptr), "checkDeviceStatus");
 }
+
+static void model_check(q3cu_status s, const char *op) {
+    if (s == Q3CU_OK) return;
+    throw std::runtime_error(std::string(op) + ": " + q3cu_status_string(s) + " (" + q3cu_last_error_string() + ")");
+}
+
+CudaModel::CudaModel(CudaContext &ctx, const void *checkpoint, size_t bytes, int ctx_length) {
+    model_check(q3cu_model_load(ctx.raw(), checkpoint, bytes, ctx_length, &m_), "q3cu_model_load");
+    model_check(q3cu_model_config(m_, &cfg_), "q3cu_model_config");
+    logits_.resize(size_t(cfg_.vocab_size));
+}
+
+CudaModel::~CudaModel() {
+    if (m_) q3cu_model_destroy(m_);
+}
+
+const float *CudaModel::forward(int token, int pos) {
+    model_check(q3cu_model_forward(m_, token, pos, logits_.data(), nullptr), "q3cu_model_forward");
+    return logits_.data();
+}
+
+const float *CudaModel::deviceLogits() const { return q3cu_model_logits(m_); }

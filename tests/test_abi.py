@@ -32,8 +32,47 @@ def test_cudacontext_symbols_exported():
     syms = subprocess.run(["nm", "-D", "-C", library_path()], capture_output=True, text=True).stdout
     for m in ("CudaContext::executeRMSNorm", "CudaContext::executeSoftmax", "CudaContext::executeSwiGLU",
               "CudaContext::executeRoPE", "CudaContext::executeQuantize", "CudaContext::executeEmbedding",
-              "CudaContext::initialize", "CudaContext::cleanup"):
+              "CudaContext::initialize", "CudaContext::cleanup", "CudaContext::executeQuantizedMatMul",
+              "CudaModel::CudaModel", "CudaModel::forward"):
         assert m in syms, m
+
+
+CXX_PROGRAM = r'''
+#include "CudaContext.h"
+#include <cstdio>
+#include <fstream>
+#include <iterator>
+#include <vector>
+// The engine-side use of the C++ boundary: context, MetalContext-style calls, a model and its decode step.
+int main(int argc, char **argv) {
+    CudaContext ctx(0);
+    if (!ctx.initialize()) { std::printf("%s\n", ctx.lastError().c_str()); return 2; }
+    float x[64], w[64], o[64];
+    for (int i = 0; i < 64; ++i) { x[i] = 0.1f * i; w[i] = 1.0f; }
+    ctx.executeRMSNorm(o, x, w, 64);
+    if (argc > 1) {
+        std::ifstream f(argv[1], std::ios::binary);
+        std::vector<char> img((std::istreambuf_iterator<char>(f)), std::istreambuf_iterator<char>());
+        CudaModel m(ctx, img.data(), img.size());
+        const float *logits = m.forward(1, 0);
+        std::printf("%d %a\n", m.config().vocab_size, logits[0]);
+    }
+    return 0;
+}
+'''
+
+
+def test_cpp_boundary_compiles_and_links(tmp_path):
+    """An engine-side C++ program using CudaContext and CudaModel builds against the
+    headers and links against libq3cu.so (running it needs a GPU)."""
+    import subprocess
+    from metalqwen3_b200.build import library_path
+    src = tmp_path / "engine.cpp"
+    src.write_text(CXX_PROGRAM)
+    libdir = os.path.dirname(library_path())
+    subprocess.run(["g++", "-std=c++17", "-O1", "-I", os.path.join(ROOT, "include"), str(src), "-o",
+                    str(tmp_path / "engine"), "-L", libdir, "-lq3cu", f"-Wl,-rpath,{libdir}"], check=True)
+    assert (tmp_path / "engine").exists()
 
 
 def test_status_strings(lib):

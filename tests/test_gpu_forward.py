@@ -109,3 +109,26 @@ def test_forward_ctx_length_and_errors(q3):
         Q3Model(q3, img[: img.size - 1000])                   # truncated tensors
     assert e.value.status == 10
     assert np.array_equal(checkpoint_image(seed=9, **shape), img)
+
+
+def test_cpp_engine_program(q3, tmp_path):
+    """The C++ boundary end to end: CudaContext + CudaModel in a compiled program,
+    run on a checkpoint file; its first logit has the reference's bits."""
+    import subprocess
+    from metalqwen3_b200.build import library_path
+    from oracle.checkpoint import write_checkpoint
+    from test_abi import CXX_PROGRAM, ROOT
+    shape = SHAPES["small"]
+    path = str(tmp_path / "m.bin")
+    write_checkpoint(path, seed=4, **shape)
+    want = expected_logits(path, np.fromfile(path, np.uint8), shape, [(1, 0)])[0]
+    src = tmp_path / "engine.cpp"
+    src.write_text(CXX_PROGRAM)
+    libdir = os.path.dirname(library_path())
+    exe = str(tmp_path / "engine")
+    subprocess.run(["g++", "-std=c++17", "-O1", "-I", os.path.join(ROOT, "include"), str(src), "-o", exe,
+                    "-L", libdir, "-lq3cu", f"-Wl,-rpath,{libdir}"], check=True)
+    out = subprocess.run([exe, path], check=True, capture_output=True, text=True, timeout=120).stdout.split()
+    assert int(out[0]) == shape["vocab"]
+    got = np.float32(float.fromhex(out[1]))
+    assert got.view(np.uint32) == want[0].view(np.uint32)
