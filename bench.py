@@ -689,8 +689,9 @@ class Forward06B(Workload):
     position `pos` (attention over pos + 1 KV rows): the embedding row, 28
     layers of RMSNorm+Q8_0, Q/K/V matmuls, QK-norm+RoPE, attention, quantize,
     wo + residual, RMSNorm+Q8_0, W1|W3, SwiGLU+Q8_0, w2 + residual, then the
-    final RMSNorm+Q8_0 and the classifier -- 255 launches (Q|K|V one matmul,
-    the attention output quantized in the attention kernel), replayed as one
+    final RMSNorm+Q8_0 and the classifier -- 283 launches (Q|K|V one matmul,
+    attention as a scores launch and a softmax/values launch that quantizes its
+    output), every launch after the first a programmatic dependent, replayed as one
     CUDA graph per timed step.  The checkpoint is a seeded synthetic image in the
     reference's file format (codes uniform in [-127, 127], scales
     |N(0, 0.01)|, norm weights 1 + N(0, 0.1)); the reference arm runs its own
@@ -717,7 +718,7 @@ class Forward06B(Workload):
         return {"workload": "Qwen3-0.6B decode token through the whole model on the device (28 layers, classifier)",
                 "tokens_per_gpu": 1, "position": self.pos, "dim": self.dim, "hidden": self.hidden,
                 "layers": self.layers, "n_heads": self.nh, "n_kv_heads": self.nkv, "head_dim": self.hd,
-                "vocab": self.vocab, "launches_per_step": 9 * self.layers + 3,
+                "vocab": self.vocab, "launches_per_step": 10 * self.layers + 3,
                 "weights": "seeded synthetic checkpoint, codes uniform [-127,127], scales |N(0,0.01)|",
                 "launch": "one CUDA graph replay per step; e2e: the q3cu_model_forward call with logits to the host"}
 
@@ -771,14 +772,20 @@ class Forward06B(Workload):
         gr.replay()
         if events is not None:
             events[0][1].record(stream)
-        return 9 * self.layers + 4                 # + the kernel that stores the step parameters
+        return 10 * self.layers + 4                # + the kernel that stores the step parameters
 
     def launch_e2e(self, q3, d, stream):
         self._model(q3, d).forward(7, self.pos, stream=stream, to_host=True)
-        return 9 * self.layers + 3
+        return 10 * self.layers + 3
 
     h2d_keys = ()
     d2h_keys = ()
+    lib_h2d_bytes = 528                     # the step parameters: position, token, 64 cos + 64 sin
+
+    @property
+    def lib_d2h_bytes(self):
+        return 4 * self.vocab                    # the logits
+
     e2e_note = ("the token id and position go in by value (the library copies them and RoPE's table to the "
                 "device and replays its own graph of the step); the logits come back to the host inside the call "
                 "(607,744 bytes)")
@@ -1118,8 +1125,8 @@ def main():
     # ---- end to end: host buffers, copies inside the timed region ----------
     hin = {k: d[k].detach().to("cpu").pin_memory() for k in wl.h2d_keys}
     hout = {k: torch.empty(d[k].shape, dtype=d[k].dtype).pin_memory() for k in wl.d2h_keys}
-    h2d = sum(t.numel() * t.element_size() for t in hin.values())
-    d2h = sum(t.numel() * t.element_size() for t in hout.values())
+    h2d = sum(t.numel() * t.element_size() for t in hin.values()) + getattr(wl, "lib_h2d_bytes", 0)
+    d2h = sum(t.numel() * t.element_size() for t in hout.values()) + getattr(wl, "lib_d2h_bytes", 0)
 
     # Row-sliceable workloads pipeline each step over E2E_CHUNKS token-row chunks:
     # copy-in on two streams (alternate chunks), kernels on another, copy-out on

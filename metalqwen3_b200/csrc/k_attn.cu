@@ -142,6 +142,174 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__re
     if ((tid & 63) == 0) xs[int64_t(h) * 2 + (tid >> 6)] = qscale;
 }
 
+// The same attention in two launches that spread over the GPU (the fused
+// kernel above runs on only n_heads SMs and streams 512 B per cached position
+// through each):
+//   attn_scores_kernel: a CTA per (head, chunk of 128 positions) work item,
+//     grid-stride over the items of this position -- the chunk's K rows staged
+//     by cp.async (padded, as above), a thread per position runs its score
+//     chain and writes att;
+//   attn_values_kernel: a CTA per (head, half-head = 64 elements = one Q8_0
+//     group) -- the row max, the libm-identical exponentials into shared
+//     memory, their sum in position order by one thread, the division, then a
+//     thread per element runs its value chain over the positions (V half-rows
+//     through an AV_NST-deep cp.async ring) and the CTA quantizes its group.
+// Both halves of a head compute the same probabilities (the same operations on
+// the same scores), so every chain keeps the reference's order and bits.  Both
+// kernels read the position from device memory and size their work from it,
+// so a captured graph serves every position.  Each is launched as a
+// programmatic dependent of the kernel before it and waits for it
+// (griddep_wait) before reading anything that kernel or an earlier one wrote.
+constexpr int AV_COLS = 64;                                  // elements per values CTA
+constexpr int AV_ROWB = AV_COLS * 4;                         // staged V half-row
+constexpr size_t AV_BUF = size_t(AT_CH) * AV_ROWB;           // 32 KB per chunk
+constexpr int AV_NST = 4;                                    // ring depth
+constexpr int AV_MAXPOS = 16384;                             // probabilities in shared memory up to here
+constexpr int AS_PER_SM = 3;                                 // resident scores CTAs per SM (67.5 KB each)
+
+__global__ void __launch_bounds__(AT_HD) attn_scores_kernel(const float *__restrict__ q, const float *kc, float *att,
+                                                            const StepParams *__restrict__ sp, int n_heads,
+                                                            int kv_dim, int kv_mul, int seq_len) {
+    extern __shared__ __align__(16) uint8_t tile[];          // [AT_CH][AT_KROW]
+    __shared__ __align__(16) float qs[AT_HD];
+    griddep_launch_dependents();
+    griddep_wait();                                          // q and this position's K row
+    const int tid = threadIdx.x;
+    const int npos = sp->pos + 1, items = (npos + AT_CH - 1) / AT_CH * n_heads;
+    for (int w = blockIdx.x; w < items; w += gridDim.x) {
+        const int h = w % n_heads, c0 = (w / n_heads) * AT_CH;
+        const int n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
+        __syncthreads();                                     // the previous item's reads of tile / qs are done
+        qs[tid] = q[int64_t(h) * AT_HD + tid];
+        attn_stage(tile, kc, c0, n, kv_dim, h / kv_mul, AT_KROW, tid);
+        cp_async_wait<0>();
+        __syncthreads();
+        if (tid < n) {
+            const float4 *kr = reinterpret_cast<const float4 *>(tile + tid * AT_KROW);
+            float s = 0.0f;
+#pragma unroll 8
+            for (int i4 = 0; i4 < AT_HD / 4; ++i4) {
+                const float4 kv = kr[i4];
+                s = __fadd_rn(s, __fmul_rn(qs[4 * i4], kv.x));
+                s = __fadd_rn(s, __fmul_rn(qs[4 * i4 + 1], kv.y));
+                s = __fadd_rn(s, __fmul_rn(qs[4 * i4 + 2], kv.z));
+                s = __fadd_rn(s, __fmul_rn(qs[4 * i4 + 3], kv.w));
+            }
+            att[int64_t(h) * seq_len + c0 + tid] = __fdiv_rn(s, __fsqrt_rn(float(AT_HD)));
+        }
+    }
+}
+
+// acc + p[0] v[0] + p[1] v[AV_COLS] + ... over n positions in order (one
+// rounding per product and per add, as the reference's loop): p 16-byte aligned
+// shared memory (broadcast), v this thread's column of a staged chunk.  The
+// next 8 positions' operands are loaded while the current 8 are added.
+__device__ __forceinline__ float value_chain(float acc, const float *p, const float *v, int n) {
+    const float4 *p4 = reinterpret_cast<const float4 *>(p);
+    const int nb = n >> 3;
+    if (nb > 0) {
+        float4 pa = p4[0], pb = p4[1];
+        float va[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) va[i] = v[i * AV_COLS];
+        for (int b = 0; b < nb; ++b) {
+            const int kn = b + 1 < nb ? b + 1 : b;                 // the last batch reloads itself
+            const float4 qa = p4[2 * kn], qb = p4[2 * kn + 1];
+            float vn[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) vn[i] = v[(kn * 8 + i) * AV_COLS];
+            acc = __fadd_rn(acc, __fmul_rn(pa.x, va[0]));
+            acc = __fadd_rn(acc, __fmul_rn(pa.y, va[1]));
+            acc = __fadd_rn(acc, __fmul_rn(pa.z, va[2]));
+            acc = __fadd_rn(acc, __fmul_rn(pa.w, va[3]));
+            acc = __fadd_rn(acc, __fmul_rn(pb.x, va[4]));
+            acc = __fadd_rn(acc, __fmul_rn(pb.y, va[5]));
+            acc = __fadd_rn(acc, __fmul_rn(pb.z, va[6]));
+            acc = __fadd_rn(acc, __fmul_rn(pb.w, va[7]));
+            pa = qa;
+            pb = qb;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) va[i] = vn[i];
+        }
+    }
+    for (int t = nb << 3; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(p[t], v[t * AV_COLS]));
+    return acc;
+}
+
+// Copies columns [col0, col0 + 64) of V rows c0 .. c0+n-1 of kv head kvh into buf.
+__device__ __forceinline__ void attn_stage_half(uint8_t *buf, const float *vc, int c0, int n, int kv_dim, int kvh,
+                                                int col0, int tid) {
+    for (int f = tid; f < n * (AV_ROWB / 16); f += AT_HD) {
+        const int r = f / (AV_ROWB / 16), pc = f % (AV_ROWB / 16);
+        cp_async16(buf + r * AV_ROWB + pc * 16, vc + int64_t(c0 + r) * kv_dim + kvh * AT_HD + col0 + pc * 4);
+    }
+    cp_async_commit();
+}
+
+__global__ void __launch_bounds__(AT_HD, 1) attn_values_kernel(const float *att, const float *vc, int8_t *xq,
+                                                               float *xs, const StepParams *__restrict__ sp,
+                                                               int kv_dim, int kv_mul, int seq_len) {
+    extern __shared__ __align__(16) uint8_t dyn[];          // [AV_NST][AV_BUF] V ring, then [seq_len] probabilities
+    float *pr = reinterpret_cast<float *>(dyn + AV_NST * AV_BUF);
+    __shared__ ExpTab tab;
+    __shared__ float red[AT_HD / 32];
+    __shared__ float sum_sh;
+    griddep_launch_dependents();
+    const int h = blockIdx.x, part = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int kvh = h / kv_mul, col0 = part * AV_COLS;
+    load_exp_table(tab);
+    griddep_wait();                                          // att (and the caches, written two kernels back)
+    const int npos = sp->pos + 1, nch = (npos + AT_CH - 1) / AT_CH;
+    // the first AV_NST - 1 chunks of V stream in while the softmax runs
+    for (int c = 0; c < AV_NST - 1; ++c) {
+        if (c < nch) {
+            const int c0 = c * AT_CH;
+            attn_stage_half(dyn + c * AV_BUF, vc, c0, npos - c0 < AT_CH ? npos - c0 : AT_CH, kv_dim, kvh, col0, tid);
+        } else {
+            cp_async_commit();                               // an empty group keeps the count uniform
+        }
+    }
+    const float *a = att + int64_t(h) * seq_len;
+    float m = 0.0f;                                           // softmax's max starts at 0
+    for (int t = tid; t < npos; t += AT_HD) m = fmaxf(m, a[t]);   // a NaN never replaces the max
+    m = warp_max(m);
+    if (lane == 0) red[warp] = m;
+    __syncthreads();                                          // (also: the exp table is loaded)
+    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+    for (int t = tid; t < npos; t += AT_HD) pr[t] = expf_host(__fsub_rn(a[t], m), tab);
+    __syncthreads();
+    if (tid == 0) sum_sh = ordered_sum_smem(0.0f, pr, npos);
+    __syncthreads();
+    const float sum = sum_sh;
+    for (int t = tid; t < npos; t += AT_HD) pr[t] = __fdiv_rn(pr[t], sum);
+    // value chains: thread j < 64 runs element col0 + j over the positions in order
+    float acc = 0.0f;
+    for (int c = 0; c < nch; ++c) {
+        const int cn = c + AV_NST - 1;                        // into the slot chunk c - 1 used
+        if (cn < nch) {
+            const int c0 = cn * AT_CH;
+            attn_stage_half(dyn + (cn % AV_NST) * AV_BUF, vc, c0, npos - c0 < AT_CH ? npos - c0 : AT_CH, kv_dim,
+                            kvh, col0, tid);
+        } else {
+            cp_async_commit();
+        }
+        cp_async_wait<AV_NST - 1>();
+        __syncthreads();                                      // chunk c landed; (c == 0) the probabilities are final
+        if (tid < AV_COLS) {
+            const int c0 = c * AT_CH, n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
+            acc = value_chain(acc, pr + c0, reinterpret_cast<const float *>(dyn + (c % AV_NST) * AV_BUF) + tid, n);
+        }
+        __syncthreads();                                      // before the slot is refilled
+    }
+    // the quantize of this group (:431): absmax from 0, scale = wmax / 127, codes
+    const float gm = warp_max(tid < AV_COLS ? fmaxf(0.0f, fabsf(acc)) : 0.0f);
+    if (lane == 0) red[warp] = gm;
+    __syncthreads();
+    const float qscale = q8_scale(fmaxf(red[0], red[1]));
+    if (tid < AV_COLS) xq[int64_t(h) * AT_HD + col0 + tid] = int8_t(q8_code(acc, qscale));
+    if (tid == 0) xs[int64_t(h) * 2 + part] = qscale;
+}
+
 // Q/K RMSNorm + RoPE of one token (qwen3_original.c:361-393) with the
 // rotation's cos/sin given by the host: the reference takes them from the C
 // library (cosf/sinf of pos*freq, :367-368), so the host computing them with
@@ -158,8 +326,11 @@ __global__ void __launch_bounds__(128) qk_norm_rope_step_kernel(float *qkv, floa
                                                                 const float *__restrict__ qn,
                                                                 const float *__restrict__ kn,
                                                                 const StepParams *__restrict__ sp, float eps) {
-    const int lane = threadIdx.x & 31;
-    const int row = blockIdx.x * 4 + (threadIdx.x >> 5);
+    __shared__ __align__(16) float rows[4][AT_HD], sq[4][AT_HD];
+    griddep_launch_dependents();                  // the attention launches wait for this kernel before reading
+    griddep_wait();                               // qkv from the matmul before
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int row = blockIdx.x * 4 + warp;
     if (row >= n_heads + 2 * n_kv) return;                  // whole warps
     const int kv_dim = n_kv * AT_HD, pos = sp->pos;
     if (row >= n_heads + n_kv) {                              // value row: copy into the cache
@@ -173,20 +344,26 @@ __global__ void __launch_bounds__(128) qk_norm_rope_step_kernel(float *qkv, floa
     const float *v = isq ? qkv + int64_t(row) * AT_HD : qkv + int64_t(n_heads) * AT_HD + (row - n_heads) * AT_HD;
     float *o = isq ? qkv + int64_t(row) * AT_HD : kc + int64_t(pos) * kv_dim + (row - n_heads) * AT_HD;
     const float *w = isq ? qn : kn;
+    // the row and its squares into shared memory (one 16-byte load per lane),
+    // then lane 0 runs the sum of squares in index order (:365)
+    const float4 r4 = reinterpret_cast<const float4 *>(v)[lane];
+    reinterpret_cast<float4 *>(rows[warp])[lane] = r4;
+    reinterpret_cast<float4 *>(sq[warp])[lane] =
+        make_float4(__fmul_rn(r4.x, r4.x), __fmul_rn(r4.y, r4.y), __fmul_rn(r4.z, r4.z), __fmul_rn(r4.w, r4.w));
+    __syncwarp();
     float ss = 0.0f;
     if (lane == 0) {
-        for (int i = 0; i < AT_HD; ++i) ss = __fadd_rn(ss, __fmul_rn(v[i], v[i]));
+        ss = ordered_sum_smem(0.0f, sq[warp], AT_HD);
         ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(AT_HD)), eps)));
     }
     ss = __shfl_sync(FULL, ss, 0);
     float x[2], y[2];
 #pragma unroll
-    for (int u = 0; u < 2; ++u) {                            // read the row before any lane writes it
+    for (int u = 0; u < 2; ++u) {
         const int j = lane + 32 * u;
-        x[u] = __fmul_rn(w[j], __fmul_rn(ss, v[j]));
-        y[u] = __fmul_rn(w[j + 64], __fmul_rn(ss, v[j + 64]));
+        x[u] = __fmul_rn(w[j], __fmul_rn(ss, rows[warp][j]));
+        y[u] = __fmul_rn(w[j + 64], __fmul_rn(ss, rows[warp][j + 64]));
     }
-    __syncwarp();
 #pragma unroll
     for (int u = 0; u < 2; ++u) {                            // pair (j, j + 64)
         const int j = lane + 32 * u;
@@ -198,9 +375,8 @@ __global__ void __launch_bounds__(128) qk_norm_rope_step_kernel(float *qkv, floa
 
 cudaError_t launch_qk_norm_rope_step(float *qkv, float *kc, float *vc, int n_heads, int n_kv, const float *qn,
                                      const float *kn, const StepParams *sp, float eps, cudaStream_t stream) {
-    qk_norm_rope_step_kernel<<<(n_heads + 2 * n_kv + 3) / 4, 128, 0, stream>>>(qkv, kc, vc, n_heads, n_kv, qn, kn,
-                                                                                 sp, eps);
-    return cudaGetLastError();
+    return launch_dependent(qk_norm_rope_step_kernel, dim3((n_heads + 2 * n_kv + 3) / 4), dim3(128), 0, stream, qkv,
+                            kc, vc, n_heads, n_kv, qn, kn, sp, eps);
 }
 
 __global__ void set_step_kernel(StepParams *sp, StepParams v) {
@@ -214,7 +390,21 @@ cudaError_t launch_set_step(StepParams *sp, const StepParams &v, cudaStream_t st
 
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, int8_t *xq, float *xs,
                                const StepParams *sp, int n_heads, int kv_dim, int kv_mul, int seq_len,
-                               cudaStream_t stream) {
+                               cudaStream_t stream, int sms) {
+    if (seq_len <= AV_MAXPOS) {                               // two launches, (head, chunk) / (head, half)
+        const size_t vsm = AV_NST * AV_BUF + size_t(seq_len) * 4;
+        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_scores_kernel), AT_BUF, 25);
+        if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void *>(attn_values_kernel),
+                                                   AV_NST * AV_BUF + size_t(AV_MAXPOS) * 4, 26);
+        if (e != cudaSuccess) return e;
+        const int64_t items = int64_t(n_heads) * ((seq_len + AT_CH - 1) / AT_CH);
+        const int grid = int(items < int64_t(AS_PER_SM) * sms ? items : int64_t(AS_PER_SM) * sms);
+        e = launch_dependent(attn_scores_kernel, dim3(grid), dim3(AT_HD), AT_BUF, stream, q, kc, att, sp, n_heads, kv_dim, kv_mul,
+                       seq_len);
+        if (e != cudaSuccess) return e;
+        return launch_dependent(attn_values_kernel, dim3(n_heads, 2), dim3(AT_HD), vsm, stream, att, vc, xq, xs, sp, kv_dim, kv_mul,
+                          seq_len);
+    }
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_decode_kernel), AT_SMEM, 24);
     if (e != cudaSuccess) return e;
     attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(q, kc, vc, att, xq, xs, sp, kv_dim, kv_mul, seq_len);

@@ -59,6 +59,9 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
                                                                const float *__restrict__ ws, int n, int d, int RB,
                                                                const float *add, MmOut out) {
     __shared__ float terms[MM_WARPS][32][33];      // [slot = row * TB + token][group of the pass], padded
+    // No early griddep_launch_dependents(): the successor starts when this grid
+    // completes.  Triggering at the start let the chain of dependent launches
+    // run ahead (each of them triggers early) and cost 0.12 ms per decode token.
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int G = n / GS;                           // groups per row
     // A pass covers GL consecutive groups (G rounded up to a power of two, at
@@ -182,16 +185,8 @@ static cudaError_t launch_mm_t(const int8_t *xq, const float *xs, int B, const i
                                                                                         add, out);
         return cudaGetLastError();
     }
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(unsigned(grid));
-    cfg.blockDim = dim3(MM_THREADS);
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, matmul_q8_kernel<TB, TB == 1 ? 4 : 2>, xq, xs, B, wq, ws, n, d, RB, add, out);
+    return launch_dependent(matmul_q8_kernel<TB, TB == 1 ? 4 : 2>, dim3(unsigned(grid)), dim3(MM_THREADS), 0, stream,
+                            xq, xs, B, wq, ws, n, d, RB, add, out);
 }
 
 cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,

@@ -419,6 +419,7 @@ __global__ void __launch_bounds__(RSM_THREADS) rmsnorm_row_kernel(const T *x, co
         for (int c = 0; c < nch; ++c) mbar_init(&bar[c], 1);
         mbar_init_fence();
     }
+    griddep_wait();                               // x from the kernel before (a dependent launch)
     __syncthreads();
     for (int f = tid; f < row_bytes / 16; f += RSM_THREADS) {
         cp_async16(rbuf + f * 16, src + f * 16);
@@ -489,9 +490,8 @@ static cudaError_t launch_rms_t(const T *x, const float *w, int64_t rows, int di
         cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(rmsnorm_row_kernel<T, Q8>),
                                          size_t(RSM_CB) * RSM_MAXCH, rslot);
         if (e != cudaSuccess) return e;
-        rmsnorm_row_kernel<T, Q8><<<unsigned(rows), RSM_THREADS, size_t(row_bytes), stream>>>(x, w, dim, n_div, eps,
-                                                                                          out, q, s, status);
-        return cudaGetLastError();
+        return launch_dependent(rmsnorm_row_kernel<T, Q8>, dim3(unsigned(rows)), dim3(RSM_THREADS), size_t(row_bytes),
+                                stream, x, w, dim, n_div, eps, out, q, s, status);
     }
     const int slot = 2 + (sizeof(T) == 4 ? 0 : 2) + (Q8 ? 1 : 0);
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(rmsnorm_kernel<T, Q8>), RMS_SMEM, slot);

@@ -104,6 +104,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 3 : 2) swiglu_v8_kernel(
     __shared__ ExpTab s_tab;
     griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
     load_exp_table(s_tab);
+    griddep_wait();                               // hb / hb2 from the kernel before (a dependent launch)
     __syncthreads();
 
     const int lane = threadIdx.x & 31;
@@ -185,9 +186,9 @@ static cudaError_t launch_swiglu_t(const T *hb, const T *hb2, int64_t elems, T *
     const int per_sm = v8 ? (sizeof(T) == 4 ? 3 : 2) : 8;    // v8: one resident wave (its launch bounds)
     if (blocks > int64_t(sms) * per_sm) blocks = int64_t(sms) * per_sm;
     if (v8)
-        swiglu_v8_kernel<T, U, Q8><<<unsigned(blocks), 256, 0, stream>>>(hb, hb2, elems, out, q, s);
-    else
-        swiglu_kernel<T, U, Q8><<<unsigned(blocks), 256, 0, stream>>>(hb, hb2, elems, out, q, s);
+        return launch_dependent(swiglu_v8_kernel<T, U, Q8>, dim3(unsigned(blocks)), dim3(256), 0, stream, hb, hb2,
+                                elems, out, q, s);
+    swiglu_kernel<T, U, Q8><<<unsigned(blocks), 256, 0, stream>>>(hb, hb2, elems, out, q, s);
     return cudaGetLastError();
 }
 

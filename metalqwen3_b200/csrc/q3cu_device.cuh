@@ -508,6 +508,37 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
 // ---------------------------------------------------------------------------
 // reductions
 // ---------------------------------------------------------------------------
+// acc + p[0] + p[1] + ... + p[n-1] by one thread, in index order with one
+// binary32 rounding per add (the reference's serial loops).  p is 16-byte
+// aligned shared memory; 16 values are loaded while the previous 16 are added,
+// so the chain runs at the add latency, not the load latency.
+__device__ __forceinline__ float ordered_sum_smem(float acc, const float *p, int n) {
+    const float4 *p4 = reinterpret_cast<const float4 *>(p);
+    const int nb = n >> 4;
+    if (nb > 0) {
+        float4 cur[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) cur[j] = p4[j];
+        for (int b = 0; b < nb; ++b) {
+            float4 nxt[4];
+            const int kn = (b + 1 < nb ? b + 1 : b) * 4;               // the last batch reloads itself
+#pragma unroll
+            for (int j = 0; j < 4; ++j) nxt[j] = p4[kn + j];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                acc = __fadd_rn(acc, cur[j].x);
+                acc = __fadd_rn(acc, cur[j].y);
+                acc = __fadd_rn(acc, cur[j].z);
+                acc = __fadd_rn(acc, cur[j].w);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) cur[j] = nxt[j];
+        }
+    }
+    for (int t = nb << 4; t < n; ++t) acc = __fadd_rn(acc, p[t]);
+    return acc;
+}
+
 __device__ __forceinline__ float warp_max(float v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));

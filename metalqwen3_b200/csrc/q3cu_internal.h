@@ -19,6 +19,28 @@ int ctx_sms(const q3cu_ctx *ctx);
 // `slot` (< 32) names the kernel instantiation.
 cudaError_t ensure_smem_attr(const void *kernel, size_t bytes, int slot);
 
+// Launches `kernel` as a programmatic dependent of the stream's previous
+// kernel: its CTAs may start before that kernel has completed, so the kernel
+// calls griddep_wait() before it reads or writes any global memory that an
+// earlier launch writes or reads (every thread that does, on every path), and
+// griddep_launch_dependents() where its own successor may start.  When the
+// previous work is not a kernel the launch behaves as an ordinary one.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                             Args... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
+}
+
 // Every launcher enqueues on `stream`, allocates nothing and returns the
 // launch error.  `sms` is the device's multiprocessor count (grid sizing).
 cudaError_t launch_quantize_q8(const void *x, q3cu_dtype dt, int64_t elems, int8_t *q, float *s,
@@ -72,7 +94,7 @@ cudaError_t launch_qk_norm_rope_step(float *qkv, float *kc, float *vc, int n_hea
 // the output [n_heads][128] as Q8_0 codes xq and scales xs [n_heads * 2].
 cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, int8_t *xq, float *xs,
                                const StepParams *sp, int n_heads, int kv_dim, int kv_mul, int seq_len,
-                               cudaStream_t stream);
+                               cudaStream_t stream, int sms);
 
 
 cudaError_t launch_swiglu(const void *hb, const void *hb2, q3cu_dtype dt, int64_t elems, void *out, int8_t *q,

@@ -269,7 +269,7 @@ static q3cu_status enqueue_step(q3cu_model *m, cudaStream_t s) {
              "qk_norm_rope");
         // attention + the quantize of its output (:395-428, :431)
         MTRY(q3::launch_attn_decode(m->qkv, m->kc + loff, m->vc + loff, m->att, m->xq, m->xs, m->step, c.n_heads, K,
-                                    m->kv_mul, S, s),
+                                    m->kv_mul, S, s, m->sms),
              "attention");
         // output projection + residual (:432-435)
         MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->wo[l], m->so[l], A, D, q3::MmOut{m->x, m->x, m->x, D, D}, s,

@@ -77,6 +77,41 @@ def test_forward_logits_bit_exact(q3, name):
         model.close()
 
 
+LONG = {
+    # 32 query heads over 8 kv heads, every position of a 1800-position context:
+    # the attention's score work items (32 heads x 15 chunks of 128 positions)
+    # outnumber its grid of 3 CTAs per SM near the end, and the V ring of 4
+    # chunks wraps several times
+    "split_1800": (dict(dim=128, hidden=384, n_layers=2, n_heads=32, n_kv=8, vocab=200, seq_len=1800,
+                        head_dim=128), range(1800)),
+    # seq_len above the two-launch limit of 16384 positions: the single fused
+    # attention kernel, over its first 300 positions (3 chunks)
+    "fused_16400": (dict(dim=256, hidden=768, n_layers=2, n_heads=4, n_kv=2, vocab=300, seq_len=16400,
+                         head_dim=128), range(300)),
+}
+
+
+@pytest.mark.parametrize("name", sorted(LONG))
+def test_forward_long_context_bit_exact(q3, name):
+    from metalqwen3_b200.q3cu import Q3Model
+    from oracle.checkpoint import write_checkpoint
+    shape, positions = LONG[name]
+    rng = np.random.default_rng(11)
+    steps = [(int(rng.integers(0, shape["vocab"])), p) for p in positions]
+    with tempfile.TemporaryDirectory() as d:
+        path = os.path.join(d, "m.bin")
+        write_checkpoint(path, seed=3, **shape)
+        img = np.fromfile(path, np.uint8)
+        want = expected_logits(path, img, shape, steps)
+    model = Q3Model(q3, img)
+    try:
+        for (tok, pos), w in zip(steps, want):
+            got = model.forward(tok, pos)
+            assert same_bits(got, w), f"{name}: logits differ at pos {pos} (max |diff| {np.nanmax(np.abs(got - w))})"
+    finally:
+        model.close()
+
+
 def test_forward_ctx_length_and_errors(q3):
     from metalqwen3_b200.q3cu import Q3Error, Q3Model
     from oracle.checkpoint import checkpoint_image, write_checkpoint
