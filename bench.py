@@ -689,9 +689,11 @@ class Forward06B(Workload):
     position `pos` (attention over pos + 1 KV rows): the embedding row, 28
     layers of RMSNorm+Q8_0, Q/K/V matmuls, QK-norm+RoPE, attention, quantize,
     wo + residual, RMSNorm+Q8_0, W1|W3, SwiGLU+Q8_0, w2 + residual, then the
-    final RMSNorm+Q8_0 and the classifier -- 283 launches (Q|K|V one matmul,
-    attention as a scores launch and a softmax/values launch that quantizes its
-    output), every launch after the first a programmatic dependent, replayed as one
+    final RMSNorm+Q8_0 and the classifier -- 171 launches (Q|K|V one matmul;
+    the layer's two RMSNorm+Q8_0 and its SwiGLU+Q8_0 computed by the matmuls
+    that consume them; attention as a scores launch that also does QK-norm+RoPE
+    and a softmax/values launch that quantizes its output), every launch after
+    the first a programmatic dependent, replayed as one
     CUDA graph per timed step.  The checkpoint is a seeded synthetic image in the
     reference's file format (codes uniform in [-127, 127], scales
     |N(0, 0.01)|, norm weights 1 + N(0, 0.1)); the reference arm runs its own
@@ -718,7 +720,7 @@ class Forward06B(Workload):
         return {"workload": "Qwen3-0.6B decode token through the whole model on the device (28 layers, classifier)",
                 "tokens_per_gpu": 1, "position": self.pos, "dim": self.dim, "hidden": self.hidden,
                 "layers": self.layers, "n_heads": self.nh, "n_kv_heads": self.nkv, "head_dim": self.hd,
-                "vocab": self.vocab, "launches_per_step": 10 * self.layers + 3,
+                "vocab": self.vocab, "launches_per_step": 6 * self.layers + 3,
                 "weights": "seeded synthetic checkpoint, codes uniform [-127,127], scales |N(0,0.01)|",
                 "launch": "one CUDA graph replay per step; e2e: the q3cu_model_forward call with logits to the host"}
 
@@ -772,11 +774,11 @@ class Forward06B(Workload):
         gr.replay()
         if events is not None:
             events[0][1].record(stream)
-        return 10 * self.layers + 4                # + the kernel that stores the step parameters
+        return 6 * self.layers + 4                 # + the kernel that stores the step parameters
 
     def launch_e2e(self, q3, d, stream):
         self._model(q3, d).forward(7, self.pos, stream=stream, to_host=True)
-        return 10 * self.layers + 3
+        return 6 * self.layers + 3
 
     h2d_keys = ()
     d2h_keys = ()

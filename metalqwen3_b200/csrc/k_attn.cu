@@ -167,21 +167,74 @@ constexpr int AV_NST = 4;                                    // ring depth
 constexpr int AV_MAXPOS = 16384;                             // probabilities in shared memory up to here
 constexpr int AS_PER_SM = 3;                                 // resident scores CTAs per SM (67.5 KB each)
 
-__global__ void __launch_bounds__(AT_HD) attn_scores_kernel(const float *__restrict__ q, const float *kc, float *att,
-                                                            const StepParams *__restrict__ sp, int n_heads,
-                                                            int kv_dim, int kv_mul, int seq_len) {
+// QK-RMSNorm + RoPE of one head row (:361-393) by one warp: v the row in
+// global memory, w its norm weight; the rotated row to out (shared or global
+// memory; out may be v, which is read whole before any lane writes).  Lane 0
+// runs the sum of squares in index order from shared memory; rows / sq are
+// this warp's 128-float scratch.
+__device__ __forceinline__ void norm_rope_row(const float *v, const float *__restrict__ w,
+                                              const StepParams *__restrict__ sp, float eps, float *rows, float *sq,
+                                              float *out, int lane) {
+    const float4 r4 = reinterpret_cast<const float4 *>(v)[lane];
+    reinterpret_cast<float4 *>(rows)[lane] = r4;
+    reinterpret_cast<float4 *>(sq)[lane] =
+        make_float4(__fmul_rn(r4.x, r4.x), __fmul_rn(r4.y, r4.y), __fmul_rn(r4.z, r4.z), __fmul_rn(r4.w, r4.w));
+    __syncwarp();
+    float ss = 0.0f;
+    if (lane == 0) {
+        ss = ordered_sum_smem(0.0f, sq, AT_HD);
+        ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(AT_HD)), eps)));
+    }
+    ss = __shfl_sync(FULL, ss, 0);
+#pragma unroll
+    for (int u = 0; u < 2; ++u) {                            // pair (j, j + 64)
+        const int j = lane + 32 * u;
+        const float x = __fmul_rn(w[j], __fmul_rn(ss, rows[j]));
+        const float y = __fmul_rn(w[j + 64], __fmul_rn(ss, rows[j + 64]));
+        const float c = sp->c[j], s = sp->s[j];
+        out[j] = __fsub_rn(__fmul_rn(x, c), __fmul_rn(y, s));
+        out[j + 64] = __fadd_rn(__fmul_rn(x, s), __fmul_rn(y, c));
+    }
+    __syncwarp();                                            // out written, scratch free
+}
+
+// Scores with the step's QK-norm + RoPE folded in: qkv holds this token's raw
+// [q | k | v] rows.  Each work item normalizes and rotates its head's q into
+// shared memory (warp 0).  The item holding position pos also rotates the kv
+// head's k straight into its tile row (warp 1) and, once per kv head (the
+// first of its query heads), writes that k row and the v row into the caches
+// for the values kernel and later steps (warps 1 and 2).
+__global__ void __launch_bounds__(AT_HD) attn_scores_kernel(const float *qkv, float *kc, float *vc, float *att,
+                                                            const float *__restrict__ qn,
+                                                            const float *__restrict__ kn,
+                                                            const StepParams *__restrict__ sp, float eps,
+                                                            int n_heads, int kv_dim, int kv_mul, int seq_len) {
     extern __shared__ __align__(16) uint8_t tile[];          // [AT_CH][AT_KROW]
     __shared__ __align__(16) float qs[AT_HD];
+    __shared__ __align__(16) float scr[2][2][AT_HD];
     griddep_launch_dependents();
-    griddep_wait();                                          // q and this position's K row
-    const int tid = threadIdx.x;
-    const int npos = sp->pos + 1, items = (npos + AT_CH - 1) / AT_CH * n_heads;
+    griddep_wait();                                          // qkv from the matmul before
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int pos = sp->pos, npos = pos + 1, items = (npos + AT_CH - 1) / AT_CH * n_heads;
+    const int qdim = n_heads * AT_HD;
     for (int w = blockIdx.x; w < items; w += gridDim.x) {
-        const int h = w % n_heads, c0 = (w / n_heads) * AT_CH;
+        const int h = w % n_heads, c0 = (w / n_heads) * AT_CH, kvh = h / kv_mul;
         const int n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
+        const bool last = c0 + n == npos;                    // this chunk holds position pos
         __syncthreads();                                     // the previous item's reads of tile / qs are done
-        qs[tid] = q[int64_t(h) * AT_HD + tid];
-        attn_stage(tile, kc, c0, n, kv_dim, h / kv_mul, AT_KROW, tid);
+        attn_stage(tile, kc, c0, last ? n - 1 : n, kv_dim, kvh, AT_KROW, tid);   // cached rows below pos
+        if (warp == 0) {
+            norm_rope_row(qkv + int64_t(h) * AT_HD, qn, sp, eps, scr[0][0], scr[0][1], qs, lane);
+        } else if (warp == 1 && last) {
+            float *kr = reinterpret_cast<float *>(tile + (n - 1) * AT_KROW);
+            norm_rope_row(qkv + qdim + kvh * AT_HD, kn, sp, eps, scr[1][0], scr[1][1], kr, lane);
+            if (h % kv_mul == 0)
+                reinterpret_cast<float4 *>(kc + int64_t(pos) * kv_dim + kvh * AT_HD)[lane] =
+                    reinterpret_cast<const float4 *>(kr)[lane];
+        } else if (warp == 2 && last && h % kv_mul == 0) {
+            reinterpret_cast<float4 *>(vc + int64_t(pos) * kv_dim + kvh * AT_HD)[lane] =
+                reinterpret_cast<const float4 *>(qkv + qdim + kv_dim + kvh * AT_HD)[lane];
+        }
         cp_async_wait<0>();
         __syncthreads();
         if (tid < n) {
@@ -343,40 +396,39 @@ __global__ void __launch_bounds__(128) qk_norm_rope_step_kernel(float *qkv, floa
     const bool isq = row < n_heads;
     const float *v = isq ? qkv + int64_t(row) * AT_HD : qkv + int64_t(n_heads) * AT_HD + (row - n_heads) * AT_HD;
     float *o = isq ? qkv + int64_t(row) * AT_HD : kc + int64_t(pos) * kv_dim + (row - n_heads) * AT_HD;
-    const float *w = isq ? qn : kn;
-    // the row and its squares into shared memory (one 16-byte load per lane),
-    // then lane 0 runs the sum of squares in index order (:365)
-    const float4 r4 = reinterpret_cast<const float4 *>(v)[lane];
-    reinterpret_cast<float4 *>(rows[warp])[lane] = r4;
-    reinterpret_cast<float4 *>(sq[warp])[lane] =
-        make_float4(__fmul_rn(r4.x, r4.x), __fmul_rn(r4.y, r4.y), __fmul_rn(r4.z, r4.z), __fmul_rn(r4.w, r4.w));
-    __syncwarp();
-    float ss = 0.0f;
-    if (lane == 0) {
-        ss = ordered_sum_smem(0.0f, sq[warp], AT_HD);
-        ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ss, float(AT_HD)), eps)));
-    }
-    ss = __shfl_sync(FULL, ss, 0);
-    float x[2], y[2];
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {
-        const int j = lane + 32 * u;
-        x[u] = __fmul_rn(w[j], __fmul_rn(ss, rows[warp][j]));
-        y[u] = __fmul_rn(w[j + 64], __fmul_rn(ss, rows[warp][j + 64]));
-    }
-#pragma unroll
-    for (int u = 0; u < 2; ++u) {                            // pair (j, j + 64)
-        const int j = lane + 32 * u;
-        const float c = sp->c[j], s = sp->s[j];
-        o[j] = __fsub_rn(__fmul_rn(x[u], c), __fmul_rn(y[u], s));
-        o[j + 64] = __fadd_rn(__fmul_rn(x[u], s), __fmul_rn(y[u], c));
-    }
+    norm_rope_row(v, isq ? qn : kn, sp, eps, rows[warp], sq[warp], o, lane);
 }
 
-cudaError_t launch_qk_norm_rope_step(float *qkv, float *kc, float *vc, int n_heads, int n_kv, const float *qn,
+static cudaError_t launch_qk_norm_rope_step(float *qkv, float *kc, float *vc, int n_heads, int n_kv, const float *qn,
                                      const float *kn, const StepParams *sp, float eps, cudaStream_t stream) {
     return launch_dependent(qk_norm_rope_step_kernel, dim3((n_heads + 2 * n_kv + 3) / 4), dim3(128), 0, stream, qkv,
                             kc, vc, n_heads, n_kv, qn, kn, sp, eps);
+}
+
+cudaError_t launch_attention_step(float *qkv, float *kc, float *vc, float *att, int8_t *xq, float *xs,
+                                  const StepParams *sp, int n_heads, int n_kv, const float *qn, const float *kn,
+                                  float eps, int seq_len, cudaStream_t stream, int sms) {
+    const int kv_dim = n_kv * AT_HD, kv_mul = n_heads / n_kv;
+    if (seq_len <= AV_MAXPOS) {                               // two launches, (head, chunk) / (head, half)
+        const size_t vsm = AV_NST * AV_BUF + size_t(seq_len) * 4;
+        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_scores_kernel), AT_BUF, 25);
+        if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void *>(attn_values_kernel),
+                                                   AV_NST * AV_BUF + size_t(AV_MAXPOS) * 4, 26);
+        if (e != cudaSuccess) return e;
+        const int64_t items = int64_t(n_heads) * ((seq_len + AT_CH - 1) / AT_CH);
+        const int grid = int(items < int64_t(AS_PER_SM) * sms ? items : int64_t(AS_PER_SM) * sms);
+        e = launch_dependent(attn_scores_kernel, dim3(grid), dim3(AT_HD), AT_BUF, stream, qkv, kc, vc, att, qn, kn, sp,
+                             eps, n_heads, kv_dim, kv_mul, seq_len);
+        if (e != cudaSuccess) return e;
+        return launch_dependent(attn_values_kernel, dim3(n_heads, 2), dim3(AT_HD), vsm, stream, att, vc, xq, xs, sp,
+                                kv_dim, kv_mul, seq_len);
+    }
+    // long contexts: the rotations into q and the caches first, then one kernel
+    cudaError_t e = launch_qk_norm_rope_step(qkv, kc, vc, n_heads, n_kv, qn, kn, sp, eps, stream);
+    if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void *>(attn_decode_kernel), AT_SMEM, 24);
+    if (e != cudaSuccess) return e;
+    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(qkv, kc, vc, att, xq, xs, sp, kv_dim, kv_mul, seq_len);
+    return cudaGetLastError();
 }
 
 __global__ void set_step_kernel(StepParams *sp, StepParams v) {
@@ -388,27 +440,5 @@ cudaError_t launch_set_step(StepParams *sp, const StepParams &v, cudaStream_t st
     return cudaGetLastError();
 }
 
-cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, int8_t *xq, float *xs,
-                               const StepParams *sp, int n_heads, int kv_dim, int kv_mul, int seq_len,
-                               cudaStream_t stream, int sms) {
-    if (seq_len <= AV_MAXPOS) {                               // two launches, (head, chunk) / (head, half)
-        const size_t vsm = AV_NST * AV_BUF + size_t(seq_len) * 4;
-        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_scores_kernel), AT_BUF, 25);
-        if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void *>(attn_values_kernel),
-                                                   AV_NST * AV_BUF + size_t(AV_MAXPOS) * 4, 26);
-        if (e != cudaSuccess) return e;
-        const int64_t items = int64_t(n_heads) * ((seq_len + AT_CH - 1) / AT_CH);
-        const int grid = int(items < int64_t(AS_PER_SM) * sms ? items : int64_t(AS_PER_SM) * sms);
-        e = launch_dependent(attn_scores_kernel, dim3(grid), dim3(AT_HD), AT_BUF, stream, q, kc, att, sp, n_heads, kv_dim, kv_mul,
-                       seq_len);
-        if (e != cudaSuccess) return e;
-        return launch_dependent(attn_values_kernel, dim3(n_heads, 2), dim3(AT_HD), vsm, stream, att, vc, xq, xs, sp, kv_dim, kv_mul,
-                          seq_len);
-    }
-    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_decode_kernel), AT_SMEM, 24);
-    if (e != cudaSuccess) return e;
-    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(q, kc, vc, att, xq, xs, sp, kv_dim, kv_mul, seq_len);
-    return cudaGetLastError();
-}
 
 }  // namespace q3

@@ -52,13 +52,106 @@ __device__ __forceinline__ int dot64(const U8 &a0, const U8 &a1, const U8 &b0, c
     return acc;
 }
 
-template <int TB, int U>
+// Shared-memory layout of a fused input: codes [n], scales [n / 64] (padded to
+// 16 bytes), then for PRO_RMS the row and its squares [n] each.
+__host__ __device__ constexpr int pro_scales_bytes(int n) { return ((n / GS) * 4 + 15) & ~15; }
+__host__ __device__ constexpr int pro_smem_bytes(int pro, int n) {
+    return n + pro_scales_bytes(n) + (pro == PRO_RMS ? 8 * n : 0);
+}
+constexpr int PRO_RMS_MAXN = 16384, PRO_SWIGLU_MAXN = 32768;
+
+// The fused input (B = 1) by every thread of the CTA; ends with a barrier.
+template <int PRO>
+__device__ __forceinline__ void mm_prologue(const MmPro &pro, int n, uint8_t *psm) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int8_t *xq_s = reinterpret_cast<int8_t *>(psm);
+    float *xs_s = reinterpret_cast<float *>(psm + n);
+    const int units = n / 8;                        // 8 values per lane; a group is 8 lanes (n % 64 == 0)
+    if constexpr (PRO == PRO_RMS) {
+        __shared__ float ss_sh;
+        float *row = reinterpret_cast<float *>(psm + n + pro_scales_bytes(n));
+        float *sq = row + n;
+        for (int i = tid; i < n / 4; i += MM_THREADS) {
+            const float4 v = u4_as_f4(ld_v4(pro.a + 4 * i));
+            reinterpret_cast<float4 *>(row)[i] = v;
+            reinterpret_cast<float4 *>(sq)[i] =
+                make_float4(__fmul_rn(v.x, v.x), __fmul_rn(v.y, v.y), __fmul_rn(v.z, v.z), __fmul_rn(v.w, v.w));
+        }
+        __syncthreads();
+        if (tid == 0)                                 // ss = 1 / sqrt(sum / n + eps), the sum in index order
+            ss_sh = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(ordered_sum_smem(0.0f, sq, n), float(n)), pro.eps)));
+        __syncthreads();
+        const f2 ss2 = pk2(ss_sh, ss_sh);
+        for (int u0 = warp * 32; u0 < units; u0 += MM_THREADS) {
+            const int u = u0 + lane;
+            const bool act = u < units;                 // whole groups of 8 lanes
+            float o[8];
+            if (act) {
+                float xv[8], wv[8];
+                Vec<float>::widen(*reinterpret_cast<const uint4 *>(row + 8 * u), xv);
+                Vec<float>::widen(*reinterpret_cast<const uint4 *>(row + 8 * u + 4), xv + 4);
+                Vec<float>::widen(ld_l1_v4(pro.w + 8 * u), wv);
+                Vec<float>::widen(ld_l1_v4(pro.w + 8 * u + 4), wv + 4);
+#pragma unroll
+                for (int i = 0; i < 8; i += 2)            // w * (ss * x)
+                    up2(mul2(pk2(wv[i], wv[i + 1]), mul2(ss2, pk2(xv[i], xv[i + 1]))), o[i], o[i + 1]);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+            }
+            uint32_t codes[2];
+            const float scale = q8_encode_lane<8, 8>(o, codes);
+            if (act) {
+                *reinterpret_cast<uint2 *>(xq_s + 8 * u) = make_uint2(codes[0], codes[1]);
+                if ((lane & 7) == 0) xs_s[u >> 3] = scale;
+            }
+        }
+    } else {
+        __shared__ ExpTab tab;
+        load_exp_table(tab);
+        __syncthreads();
+        for (int u0 = warp * 32; u0 < units; u0 += MM_THREADS) {
+            const int u = u0 + lane;
+            const bool act = u < units;
+            float o[8];
+            if (act) {
+                const U8 ra = ld_v8(pro.a + 8 * u), rb = ld_v8(pro.b + 8 * u);
+                float a[8], b[8];
+                Wide<float>::widen(ra, a);
+                Wide<float>::widen(rb, b);
+                swiglu_lane<8>(a, b, o, tab);
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) o[i] = 0.0f;
+            }
+            uint32_t codes[2];
+            const float scale = q8_encode_lane<8, 8>(o, codes);
+            if (act) {
+                *reinterpret_cast<uint2 *>(xq_s + 8 * u) = make_uint2(codes[0], codes[1]);
+                if ((lane & 7) == 0) xs_s[u >> 3] = scale;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ U8 ld_shared_v8(const int8_t *p) {
+    const uint4 lo = *reinterpret_cast<const uint4 *>(p), hi = *reinterpret_cast<const uint4 *>(p + 16);
+    return U8{{lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w}};
+}
+
+// PRO = 0: x codes / scales from global memory.  PRO_RMS / PRO_SWIGLU (TB = 1):
+// every CTA computes x into shared memory first (mm_prologue), after asking L2
+// for its warps' first rows of W and waiting for the kernel that wrote pro.a.
+template <int TB, int U, int PRO>
 __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__restrict__ xq,
                                                                const float *__restrict__ xs, int B,
                                                                const int8_t *__restrict__ wq,
                                                                const float *__restrict__ ws, int n, int d, int RB,
-                                                               const float *add, MmOut out) {
+                                                               const float *add, MmOut out, MmPro pro) {
+    static_assert(PRO == 0 || TB == 1, "a fused input is one token");
     __shared__ float terms[MM_WARPS][32][33];      // [slot = row * TB + token][group of the pass], padded
+    extern __shared__ __align__(16) uint8_t psm[]; // the fused input (PRO != 0)
     // No early griddep_launch_dependents(): the successor starts when this grid
     // completes.  Triggering at the start let the chain of dependent launches
     // run ahead (each of them triggers early) and cost 0.12 ms per decode token.
@@ -75,6 +168,20 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
     const int slots = RB * TB;                      // (row, token) pairs of a tile, <= 32
     float(*tw)[33] = terms[warp];
     bool waited = false;                            // griddep_wait done (before the first read of x / add)
+    if constexpr (PRO != 0) {
+        const int64_t j0 = int64_t(blockIdx.x) * MM_WARPS + warp;
+        if (lane == 0 && j0 < jobs) {               // this warp's first tile of W, into L2
+            const int i0 = int(j0 % tiles) * RB, rm = d - i0 < RB ? d - i0 : RB;
+            const int8_t *pw = wq + int64_t(i0) * n;
+            const float *ps = ws + int64_t(i0) * G;
+            if ((reinterpret_cast<uintptr_t>(pw) & 15) == 0) prefetch_l2_bulk(pw, uint32_t(rm) * uint32_t(n));
+            if ((reinterpret_cast<uintptr_t>(ps) & 15) == 0 && (rm * G) % 4 == 0)
+                prefetch_l2_bulk(ps, uint32_t(rm * G) * 4u);
+        }
+        griddep_wait();                             // pro.a / pro.b / add from the kernel before
+        waited = true;
+        mm_prologue<PRO>(pro, n, psm);
+    }
 
     for (int64_t job = int64_t(blockIdx.x) * MM_WARPS + warp; job < jobs; job += int64_t(gridDim.x) * MM_WARPS) {
         const int tile = int(job % tiles), tb = int(job / tiles);
@@ -111,8 +218,13 @@ __global__ void __launch_bounds__(MM_THREADS) matmul_q8_kernel(const int8_t *__r
             float xsc[TB];
 #pragma unroll
             for (int t = 0; t < TB; ++t) {
-                const int8_t *xp = xq + int64_t(t0 + t) * n + int64_t(g) * GS;
-                if (gl && t0 + t < B) {
+                if (PRO != 0 && gl) {
+                    const int8_t *sp = reinterpret_cast<const int8_t *>(psm) + int64_t(g) * GS;
+                    xa[t] = ld_shared_v8(sp);
+                    xb[t] = ld_shared_v8(sp + 32);
+                    xsc[t] = reinterpret_cast<const float *>(psm + n)[g];
+                } else if (gl && t0 + t < B) {
+                    const int8_t *xp = xq + int64_t(t0 + t) * n + int64_t(g) * GS;
                     xa[t] = ld_nc_v8(xp);
                     xb[t] = ld_nc_v8(xp + 32);
                     xsc[t] = xs[int64_t(t0 + t) * G + g];
@@ -181,12 +293,41 @@ static cudaError_t launch_mm_t(const int8_t *xq, const float *xs, int B, const i
     int64_t grid = (jobs + MM_WARPS - 1) / MM_WARPS;
     if (grid > int64_t(sms) * 8) grid = int64_t(sms) * 8;
     if (!pdl) {
-        matmul_q8_kernel<TB, TB == 1 ? 4 : 2><<<unsigned(grid), MM_THREADS, 0, stream>>>(xq, xs, B, wq, ws, n, d, RB,
-                                                                                        add, out);
+        matmul_q8_kernel<TB, TB == 1 ? 4 : 2, 0><<<unsigned(grid), MM_THREADS, 0, stream>>>(xq, xs, B, wq, ws, n, d,
+                                                                                           RB, add, out, MmPro{});
         return cudaGetLastError();
     }
-    return launch_dependent(matmul_q8_kernel<TB, TB == 1 ? 4 : 2>, dim3(unsigned(grid)), dim3(MM_THREADS), 0, stream,
-                            xq, xs, B, wq, ws, n, d, RB, add, out);
+    return launch_dependent(matmul_q8_kernel<TB, TB == 1 ? 4 : 2, 0>, dim3(unsigned(grid)), dim3(MM_THREADS), 0,
+                            stream, xq, xs, B, wq, ws, n, d, RB, add, out, MmPro{});
+}
+
+// Tiles as launch_mm_t<1> sizes them; always a dependent launch.
+template <int PRO>
+static cudaError_t launch_mm_pro(const MmPro &pro, int n, const int8_t *wq, const float *ws, int d, const float *add,
+                                 const MmOut &out, cudaStream_t stream, int sms) {
+    const int64_t want = int64_t(sms) * 16;
+    int64_t rb = (int64_t(d) + want - 1) / want;
+    if (rb < 1) rb = 1;
+    if (rb > 32) rb = 32;
+    const int RB = int(rb);
+    const int64_t jobs = (d + RB - 1) / RB;
+    int64_t grid = (jobs + MM_WARPS - 1) / MM_WARPS;
+    if (grid > int64_t(sms) * 8) grid = int64_t(sms) * 8;
+    const int cap = pro_smem_bytes(PRO, PRO == PRO_RMS ? PRO_RMS_MAXN : PRO_SWIGLU_MAXN);
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(matmul_q8_kernel<1, 4, PRO>), size_t(cap),
+                                     PRO == PRO_RMS ? 27 : 28);
+    if (e != cudaSuccess) return e;
+    return launch_dependent(matmul_q8_kernel<1, 4, PRO>, dim3(unsigned(grid)), dim3(MM_THREADS),
+                            size_t(pro_smem_bytes(PRO, n)), stream, static_cast<const int8_t *>(nullptr),
+                            static_cast<const float *>(nullptr), 1, wq, ws, n, d, RB, add, out, pro);
+}
+
+cudaError_t launch_matmul_q8_pro(MmProKind kind, const MmPro &pro, int n, const int8_t *wq, const float *ws, int d,
+                                 const MmOut &out, cudaStream_t stream, int sms, const float *add) {
+    if (d == 0) return cudaSuccess;
+    if (n <= 0 || n % GS != 0 || (kind == PRO_RMS ? n > PRO_RMS_MAXN : n > PRO_SWIGLU_MAXN)) return cudaErrorInvalidValue;
+    return kind == PRO_RMS ? launch_mm_pro<PRO_RMS>(pro, n, wq, ws, d, add, out, stream, sms)
+                           : launch_mm_pro<PRO_SWIGLU>(pro, n, wq, ws, d, add, out, stream, sms);
 }
 
 cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,

@@ -82,19 +82,9 @@ __global__ void __launch_bounds__(256) swiglu_kernel(const T *hb, const T *__res
     }
 }
 
-// The exact scalar chain for one element (the rare lanes the fast path flags).
-__device__ __forceinline__ float swiglu_exact(float a, float b, const ExpTab &tab) {
-    const float ex = expf_host(-a, tab);
-    return __fmul_rn(a, __fmul_rn(b, __frcp_rn(__fadd_rn(1.0f, ex))));
-}
-
 // Main kernel: 32 bytes of hb and hb2 per lane per step (8 f32 / 16 bf16), so a
-// 64-group spans 8 / 4 lanes.  Per element: the expf core (binary64, branch
-// free), then 1/(1+e) by a rcp.approx seed and one Markstein correction step
-// (rcp_rn_1to2p120: correctly rounded for 1 <= d < 2^120, checked against
-// __frcp_rn on every such d), and the two products, element pairs in packed
-// f32x2 arithmetic.  Lanes holding an |a| >= 83 (or NaN) recompute their values
-// with swiglu_exact before the group reduction; codes come from q8_encode_lane.
+// 64-group spans 8 / 4 lanes; the values by swiglu_lane (q3cu_device.cuh),
+// codes from q8_encode_lane.
 template <typename T, int U, bool Q8>
 __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 3 : 2) swiglu_v8_kernel(const T *hb, const T *__restrict__ hb2, int64_t elems,
                                                         T *out, int8_t *__restrict__ q, float *__restrict__ s) {
@@ -133,26 +123,7 @@ __global__ void __launch_bounds__(256, sizeof(T) == 4 ? 3 : 2) swiglu_v8_kernel(
                 float a[N], b[N];
                 Wide<T>::widen(ra[u], a);
                 Wide<T>::widen(rb[u], b);
-                // |a| < 83 keeps -a off expf's special inputs (|x| >= 88, NaN, inf) and
-                // d = 1 + e^-a inside [1, 2^120), where rcp_rn_1to2p120's one correction
-                // step is exact.  Pairs use packed f32x2 arithmetic; nd = -1 - e is -d
-                // exactly (round-to-nearest is symmetric), so d's negation costs nothing.
-                bool slow = false;
-                const f2 NEG1 = pk2(-1.0f, -1.0f), ONE = pk2(1.0f, 1.0f);
-#pragma unroll
-                for (int i = 0; i < N; i += 2) {
-                    slow |= !(fabsf(a[i]) < 83.0f) | !(fabsf(a[i + 1]) < 83.0f);
-                    const f2 nd = sub2(NEG1, pk2(expf_core(-a[i], s_tab), expf_core(-a[i + 1], s_tab)));
-                    float nd0, nd1;
-                    up2(nd, nd0, nd1);
-                    const f2 y0 = pk2(rcp_approx(-nd0), rcp_approx(-nd1));
-                    const f2 y = fma2(y0, fma2(nd, y0, ONE), y0);      // y0 + y0*(1 - d*y0)
-                    up2(mul2(pk2(a[i], a[i + 1]), mul2(pk2(b[i], b[i + 1]), y)), o[i], o[i + 1]);
-                }
-                if (__builtin_expect(slow, 0)) {
-#pragma unroll
-                    for (int i = 0; i < N; ++i) o[i] = swiglu_exact(a[i], b[i], s_tab);
-                }
+                swiglu_lane<N>(a, b, o, s_tab);
             } else {
 #pragma unroll
                 for (int i = 0; i < N; ++i) o[i] = 0.0f;

@@ -49,6 +49,11 @@ __device__ __forceinline__ uint4 ld_l1_v4(const void *p) {
                  : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
     return v;
 }
+// Asks L2 to fetch [p, p + bytes) (p 16-byte aligned, bytes a multiple of 16);
+// nothing waits for it.
+__device__ __forceinline__ void prefetch_l2_bulk(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
+}
 // Coherent load (data the same kernel may have written).
 __device__ __forceinline__ uint4 ld_v4(const void *p) {
     uint4 v;
@@ -373,6 +378,42 @@ __device__ __forceinline__ void load_exp_table(ExpTab &t) {
 }
 __device__ __forceinline__ float expf_host(float x, const ExpTab &t) { return q3_expf_fast(x, t.hi, t.lo); }
 __device__ __forceinline__ float expf_core(float x, const ExpTab &t) { return q3_expf_core(x, t.hi, t.lo); }
+
+// SwiGLU of one element by the reference's chain (:449-450), exactly:
+// a * (b * (1 / (1 + expf(-a)))), expf with the host libm's bits.
+__device__ __forceinline__ float swiglu_exact(float a, float b, const ExpTab &tab) {
+    const float ex = expf_host(-a, tab);
+    return __fmul_rn(a, __fmul_rn(b, __frcp_rn(__fadd_rn(1.0f, ex))));
+}
+
+// SwiGLU of the N (even) values a lane holds, bit-identical to swiglu_exact.
+// Per element: the expf core (binary64, branch free), then 1/(1+e) by a
+// rcp.approx seed and one Markstein correction step (correctly rounded for
+// 1 <= d < 2^120, checked against __frcp_rn on every such d), and the two
+// products, element pairs in packed f32x2 arithmetic.  |a| < 83 keeps -a off
+// expf's special inputs (|x| >= 88, NaN, inf) and d = 1 + e^-a inside
+// [1, 2^120); nd = -1 - e is -d exactly (round-to-nearest is symmetric), so
+// d's negation costs nothing.  A lane holding an |a| >= 83 (or NaN) recomputes
+// its values with swiglu_exact.
+template <int N>
+__device__ __forceinline__ void swiglu_lane(const float *a, const float *b, float *o, const ExpTab &tab) {
+    bool slow = false;
+    const f2 NEG1 = pk2(-1.0f, -1.0f), ONE = pk2(1.0f, 1.0f);
+#pragma unroll
+    for (int i = 0; i < N; i += 2) {
+        slow |= !(fabsf(a[i]) < 83.0f) | !(fabsf(a[i + 1]) < 83.0f);
+        const f2 nd = sub2(NEG1, pk2(expf_core(-a[i], tab), expf_core(-a[i + 1], tab)));
+        float nd0, nd1;
+        up2(nd, nd0, nd1);
+        const f2 y0 = pk2(rcp_approx(-nd0), rcp_approx(-nd1));
+        const f2 y = fma2(y0, fma2(nd, y0, ONE), y0);      // y0 + y0*(1 - d*y0)
+        up2(mul2(pk2(a[i], a[i + 1]), mul2(pk2(b[i], b[i + 1]), y)), o[i], o[i + 1]);
+    }
+    if (__builtin_expect(slow, 0)) {
+#pragma unroll
+        for (int i = 0; i < N; ++i) o[i] = swiglu_exact(a[i], b[i], tab);
+    }
+}
 
 // exp(d) for -80 <= d <= 0, where only accuracy is required (softmax: 1e-5
 // relative), in binary32 without the binary64 core: exp(d) = 2^t, t = d*log2(e).

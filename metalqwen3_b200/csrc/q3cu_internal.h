@@ -68,6 +68,19 @@ struct MmOut {
     float *p0, *p1, *p2;
     int e0, e1;
 };
+// The input of a fused one-token matmul, computed by every CTA into shared
+// memory before its dot products:
+//   PRO_RMS:    x = Q8_0(RMSNorm(a; weight w, eps))  (:281-291, then quantize)
+//   PRO_SWIGLU: x = Q8_0(SwiGLU(a, b))               (:449-450, then :453)
+// with the operations of rmsnorm_row_kernel and swiglu_v8_kernel, so the codes
+// and scales are the ones those kernels store.
+enum MmProKind { PRO_RMS = 1, PRO_SWIGLU = 2 };
+struct MmPro {
+    const float *a, *b, *w;
+    float eps;
+};
+cudaError_t launch_matmul_q8_pro(MmProKind kind, const MmPro &pro, int n, const int8_t *wq, const float *ws, int d,
+                                 const MmOut &out, cudaStream_t stream, int sms, const float *add);
 // pdl: launched with programmatic stream serialization (may overlap the
 // previous kernel in the stream, which must not read what this one writes).
 cudaError_t launch_matmul_q8_seg(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
@@ -85,16 +98,17 @@ struct StepParams {
 };
 // Writes v to *sp in stream order (a kernel: usable inside any stream capture).
 cudaError_t launch_set_step(StepParams *sp, const StepParams &v, cudaStream_t stream);
-// Q/K RMSNorm + RoPE of the step's token from qkv = [q | k | v] (head_dim 128):
-// q rotated in place, k rotated into kc's row sp->pos, v copied into vc's.
-cudaError_t launch_qk_norm_rope_step(float *qkv, float *kc, float *vc, int n_heads, int n_kv, const float *qn,
-                                     const float *kn, const StepParams *sp, float eps, cudaStream_t stream);
-// Decode attention of one token at sp->pos (head_dim 128): q [n_heads][128],
-// kc / vc the layer's caches [seq_len][kv_dim], att [n_heads][seq_len] scratch;
-// the output [n_heads][128] as Q8_0 codes xq and scales xs [n_heads * 2].
-cudaError_t launch_attn_decode(const float *q, const float *kc, const float *vc, float *att, int8_t *xq, float *xs,
-                               const StepParams *sp, int n_heads, int kv_dim, int kv_mul, int seq_len,
-                               cudaStream_t stream, int sms);
+// Attention of the step's token at sp->pos (head_dim 128), from the raw
+// qkv = [q | k | v] rows of the Q|K|V matmul: QK-RMSNorm + RoPE of q and k
+// (:361-393), k and v into the layer's cache rows at pos (kc / vc
+// [seq_len][n_kv * 128]), scores, softmax and weighted values (:395-428;
+// att [n_heads][seq_len] scratch), the output [n_heads][128] as Q8_0 codes xq
+// and scales xs [n_heads * 2] (:431).  Up to 16,384 positions: two launches
+// with the rotations inside the first; beyond: a rotation launch, then one
+// fused attention kernel.
+cudaError_t launch_attention_step(float *qkv, float *kc, float *vc, float *att, int8_t *xq, float *xs,
+                                  const StepParams *sp, int n_heads, int n_kv, const float *qn, const float *kn,
+                                  float eps, int seq_len, cudaStream_t stream, int sms);
 
 
 cudaError_t launch_swiglu(const void *hb, const void *hb2, q3cu_dtype dt, int64_t elems, void *out, int8_t *q,

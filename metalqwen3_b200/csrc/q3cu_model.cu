@@ -11,18 +11,23 @@
 //
 // Every step keeps the reference's roundings, so the logits are its bits:
 // the embedding row is dequantized on lookup (the reference dequantizes the
-// whole table at load, :203-205; same product per element); RMSNorm+Q8_0,
-// quantize, SwiGLU+Q8_0 are the library's bit-exact kernels; QK-norm+RoPE takes
+// whole table at load, :203-205; same product per element); the layer's
+// RMSNorm+Q8_0 and SwiGLU+Q8_0 are computed, with the operations of the
+// library's bit-exact kernels, by every CTA of the matmul that consumes them
+// (launch_matmul_q8_pro); the final RMSNorm+Q8_0 is its own kernel, because
+// the classifier's grid is more than one wave; QK-norm+RoPE takes
 // its cos/sin from the host's libm for the step's position (as the reference
 // computes them) instead of the device's sincosf; the
 // matmuls keep the group order (k_matmul.cu) and fuse the residual add
 // (x += W x, one rounding as in :434/:457); attention keeps its three orders
 // and quantizes its own output (k_attn.cu).  Weights that share an input are
-// stored as one matrix -- Q|K|V as [A+2K][dim], its output rows going to q and
-// to this position's K and V cache rows; W1|W3 as [2H][dim] -- so a layer is
-// 9 launches.  The matmuls are launched as programmatic dependents of the
-// kernel before them (their weight loads start while it finishes; no matmul
-// here writes what its predecessor reads).  Weights, KV cache and run state
+// stored as one matrix -- Q|K|V as [A+2K][dim] into one [q | k | v] buffer,
+// W1|W3 as [2H][dim] -- so a layer is 6 launches (QK-norm+RoPE and the
+// cache-row writes inside the attention's first launch).  Every launch after
+// the embedding row is a programmatic dependent of the kernel before it (its
+// weight loads or its prologue start while that kernel finishes; each waits
+// for it before touching what it wrote, and no kernel here writes what its
+// predecessor reads).  Weights, KV cache and run state
 // live in one device allocation made at load; forward allocates nothing.
 #include <cmath>
 #include <cstdarg>
@@ -257,33 +262,30 @@ static q3cu_status enqueue_step(q3cu_model *m, cudaStream_t s) {
     MCHK(q3cu_embed_gather(ctx, m->tok_q, m->tok_s, c.vocab_size, D, &m->step->token, 1, m->x, nullptr, nullptr, st));
     for (int l = 0; l < c.n_layers; ++l) {
         const int64_t loff = int64_t(l) * S * K;
-        // attention rmsnorm + quantize, Q|K|V (:353-359)
-        MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_att + int64_t(l) * D, 1, D, eps, m->xq, m->xs, st));
-        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->wqkv[l], m->sqkv[l], D, A + 2 * K,
-                                      q3::MmOut{m->qkv, m->qkv, m->qkv, A + 2 * K, A + 2 * K}, s, m->sms, nullptr,
-                                      true),
-             "wq|wk|wv");
-        // Q/K RMSNorm + RoPE; the key and the value into their cache rows (:349-350, :361-393)
-        MTRY(q3::launch_qk_norm_rope_step(m->qkv, m->kc + loff, m->vc + loff, c.n_heads, c.n_kv_heads,
-                                          m->q_norm + int64_t(l) * hd, m->k_norm + int64_t(l) * hd, m->step, eps, s),
-             "qk_norm_rope");
-        // attention + the quantize of its output (:395-428, :431)
-        MTRY(q3::launch_attn_decode(m->qkv, m->kc + loff, m->vc + loff, m->att, m->xq, m->xs, m->step, c.n_heads, K,
-                                    m->kv_mul, S, s, m->sms),
+        // attention rmsnorm + quantize, Q|K|V (:353-359): one launch, every CTA
+        // normalizes and quantizes x into its shared memory
+        MTRY(q3::launch_matmul_q8_pro(q3::PRO_RMS, q3::MmPro{m->x, nullptr, m->rms_att + int64_t(l) * D, eps}, D,
+                                      m->wqkv[l], m->sqkv[l], A + 2 * K,
+                                      q3::MmOut{m->qkv, m->qkv, m->qkv, A + 2 * K, A + 2 * K}, s, m->sms, nullptr),
+             "rmsnorm + wq|wk|wv");
+        // Q/K RMSNorm + RoPE, the key and the value into their cache rows,
+        // attention and the quantize of its output (:349-350, :361-428, :431)
+        MTRY(q3::launch_attention_step(m->qkv, m->kc + loff, m->vc + loff, m->att, m->xq, m->xs, m->step, c.n_heads,
+                                       c.n_kv_heads, m->q_norm + int64_t(l) * hd, m->k_norm + int64_t(l) * hd, eps,
+                                       S, s, m->sms),
              "attention");
         // output projection + residual (:432-435)
         MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->wo[l], m->so[l], A, D, q3::MmOut{m->x, m->x, m->x, D, D}, s,
                                       m->sms, m->x, true),
              "wo");
         // FFN (:438-458)
-        MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_ffn + int64_t(l) * D, 1, D, eps, m->xq, m->xs, st));
-        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->w13[l], m->s13[l], D, 2 * H,
-                                      q3::MmOut{m->hb, m->hb, m->hb, 2 * H, 2 * H}, s, m->sms, nullptr, true),
-             "w1|w3");
-        MCHK(q3cu_swiglu_q8(ctx, m->hb, m->hb + H, Q3CU_F32, 1, H, m->xq, m->xs, st));
-        MTRY(q3::launch_matmul_q8_seg(m->xq, m->xs, 1, m->w2[l], m->s2[l], H, D, q3::MmOut{m->x, m->x, m->x, D, D}, s,
-                                      m->sms, m->x, true),
-             "w2");
+        MTRY(q3::launch_matmul_q8_pro(q3::PRO_RMS, q3::MmPro{m->x, nullptr, m->rms_ffn + int64_t(l) * D, eps}, D,
+                                      m->w13[l], m->s13[l], 2 * H, q3::MmOut{m->hb, m->hb, m->hb, 2 * H, 2 * H}, s,
+                                      m->sms, nullptr),
+             "rmsnorm + w1|w3");
+        MTRY(q3::launch_matmul_q8_pro(q3::PRO_SWIGLU, q3::MmPro{m->hb, m->hb + H, nullptr, 0.0f}, H, m->w2[l],
+                                      m->s2[l], D, q3::MmOut{m->x, m->x, m->x, D, D}, s, m->sms, m->x),
+             "swiglu + w2");
     }
     // final rmsnorm + classifier (:462-466)
     MCHK(q3cu_rmsnorm_q8(ctx, m->x, Q3CU_F32, m->rms_final, 1, D, eps, m->xq, m->xs, st));
