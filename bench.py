@@ -777,7 +777,10 @@ class Forward06B(Workload):
         return 6 * self.layers + 4                 # + the kernel that stores the step parameters
 
     def launch_e2e(self, q3, d, stream):
-        self._model(q3, d).forward(7, self.pos, stream=stream, to_host=True)
+        if "logits_host" not in d:                 # the caller's pinned logits buffer, reused every step
+            import torch
+            d["logits_host"] = torch.empty(self.vocab, dtype=torch.float32, pin_memory=True).numpy()
+        self._model(q3, d).forward(7, self.pos, stream=stream, out=d["logits_host"])
         return 6 * self.layers + 3
 
     h2d_keys = ()
@@ -790,7 +793,7 @@ class Forward06B(Workload):
 
     e2e_note = ("the token id and position go in by value (the library copies them and RoPE's table to the "
                 "device and replays its own graph of the step); the logits come back to the host inside the call "
-                "(607,744 bytes)")
+                "(607,744 bytes, into the caller's pinned buffer)")
 
     def cpu_step(self, oracle, np, sample, threads, rng):
         """One decode token by the reference's own qwen3_forward on the same checkpoint file."""

@@ -274,13 +274,20 @@ class Q3Model:
         self.config = dict(zip(keys, list(cfg)))
         self._img = None                      # the weights live on the device now
 
-    def forward(self, token, pos, stream=None, to_host=True):
+    def forward(self, token, pos, stream=None, to_host=True, out=None):
+        """Logits of `token` at `pos` as a new float32 array, or into `out` (a
+        C-contiguous float32 array of vocab_size, e.g. over pinned memory), or
+        left on the device (to_host=False; see logits_ptr)."""
         import numpy as np
-        out = np.empty(self.config["vocab_size"], np.float32) if to_host else None
+        if to_host and out is None:
+            out = np.empty(self.config["vocab_size"], np.float32)
+        if to_host and (out.dtype != np.float32 or out.size != self.config["vocab_size"]
+                        or not out.flags["C_CONTIGUOUS"]):
+            raise ValueError("out must be a C-contiguous float32 array of vocab_size elements")
         self.q3._check(self.lib.q3cu_model_forward(self.m, int(token), int(pos),
                                                    out.ctypes.data if to_host else None, self.q3._stream(stream)),
                        "q3cu_model_forward")
-        return out
+        return out if to_host else None
 
     def logits_ptr(self):
         return self.lib.q3cu_model_logits(self.m)

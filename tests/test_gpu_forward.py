@@ -73,6 +73,11 @@ def test_forward_logits_bit_exact(q3, name):
         for (tok, pos), w in zip(steps, want):
             got = model.forward(tok, pos)
             assert same_bits(got, w), f"{name}: logits differ at pos {pos} (max |diff| {np.nanmax(np.abs(got - w))})"
+        # the same step again into a caller's buffer (the cache row at pos is rewritten with the same values)
+        buf = np.full(shape["vocab"], np.nan, np.float32)
+        assert model.forward(tok, pos, out=buf) is buf and same_bits(buf, want[-1])
+        with pytest.raises(ValueError):
+            model.forward(tok, pos, out=np.empty(shape["vocab"], np.float64))
     finally:
         model.close()
 
