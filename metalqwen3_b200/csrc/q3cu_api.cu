@@ -156,6 +156,7 @@ q3cu_status set_error(q3cu_status s, const char *msg) { return fail(s, "%s", msg
 bool ctx_alive(const q3cu_ctx *ctx) { return ctx && ctx->alive; }
 q3cu_status ctx_use_device(q3cu_ctx *ctx) { return use_device(ctx); }
 int ctx_sms(const q3cu_ctx *ctx) { return ctx->sms; }
+uint32_t *ctx_status_word(const q3cu_ctx *ctx) { return ctx->d_status; }
 }  // namespace q3
 
 extern "C" {

@@ -14,6 +14,7 @@ q3cu_status set_error(q3cu_status s, const char *msg);   // records msg for q3cu
 bool ctx_alive(const q3cu_ctx *ctx);
 q3cu_status ctx_use_device(q3cu_ctx *ctx);                // makes the context's device current
 int ctx_sms(const q3cu_ctx *ctx);
+uint32_t *ctx_status_word(const q3cu_ctx *ctx);               // the device status word (Q3CU_DEV_* bits)
 
 // Raises a kernel's dynamic shared-memory limit once per (device, slot):
 // `slot` (< 32) names the kernel instantiation.

@@ -54,6 +54,10 @@ struct q3cu_model {
     cudaStream_t own = nullptr;               // the model's stream: its graph runs there
     cudaEvent_t ev_in = nullptr, ev_out = nullptr;
     cudaGraphExec_t graph = nullptr;          // one decode step, captured at the first call
+    // pinned host staging: the step parameters copied in, the status word read back
+    q3::StepParams *h_step = nullptr;
+    uint32_t *h_status = nullptr;
+    cudaEvent_t ev_step = nullptr;            // the copy of h_step has been made
 };
 
 namespace {
@@ -230,12 +234,18 @@ q3cu_status q3cu_model_load(q3cu_ctx *ctx, const void *checkpoint, size_t bytes,
     e = cudaStreamCreateWithFlags(&m->own, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_in, cudaEventDisableTiming);
     if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_out, cudaEventDisableTiming);
+    if (e == cudaSuccess) e = cudaEventCreateWithFlags(&m->ev_step, cudaEventDisableTiming);
+    void *hb = nullptr;
+    if (e == cudaSuccess) e = cudaHostAlloc(&hb, sizeof(q3::StepParams) + 16, cudaHostAllocDefault);
     if (e != cudaSuccess) {
         if (m->ev_in) cudaEventDestroy(m->ev_in);
         if (m->ev_out) cudaEventDestroy(m->ev_out);
+        if (m->ev_step) cudaEventDestroy(m->ev_step);
         if (m->own) cudaStreamDestroy(m->own);
-        return fail_free(cuda_err(e, "stream / events"));
+        return fail_free(cuda_err(e, "stream / events / pinned staging"));
     }
+    m->h_step = static_cast<q3::StepParams *>(hb);
+    m->h_status = reinterpret_cast<uint32_t *>(static_cast<uint8_t *>(hb) + sizeof(q3::StepParams));
     *out = m;
     return Q3CU_OK;
 }
@@ -348,18 +358,25 @@ q3cu_status q3cu_model_forward(q3cu_model *m, int token, int pos, float *logits_
         MCHK(enqueue_step(m, s));
     } else {
         // the model's own graph, replayed on its stream between two events on the caller's
+        MTRY(cudaEventSynchronize(m->ev_step), "cudaEventSynchronize");   // the last step's copy has read h_step
+        *m->h_step = sp;
         MTRY(cudaEventRecord(m->ev_in, s), "cudaEventRecord");
         MTRY(cudaStreamWaitEvent(m->own, m->ev_in, 0), "cudaStreamWaitEvent");
-        MTRY(cudaMemcpyAsync(m->step, &sp, sizeof(sp), cudaMemcpyHostToDevice, m->own), "step parameters");
+        MTRY(cudaMemcpyAsync(m->step, m->h_step, sizeof(sp), cudaMemcpyHostToDevice, m->own), "step parameters");
+        MTRY(cudaEventRecord(m->ev_step, m->own), "cudaEventRecord");
         if (!m->graph) MCHK(capture_step(m));
         MTRY(cudaGraphLaunch(m->graph, m->own), "cudaGraphLaunch");
         MTRY(cudaEventRecord(m->ev_out, m->own), "cudaEventRecord");
         MTRY(cudaStreamWaitEvent(s, m->ev_out, 0), "cudaStreamWaitEvent");
     }
     if (logits_host) {
+        // the logits and the status word back in one round trip; a set word is
+        // reported (and cleared) by q3cu_device_status
         MTRY(cudaMemcpyAsync(logits_host, m->logits, size_t(c.vocab_size) * 4, cudaMemcpyDeviceToHost, s), "logits D2H");
+        MTRY(cudaMemcpyAsync(m->h_status, q3::ctx_status_word(ctx), sizeof(uint32_t), cudaMemcpyDeviceToHost, s),
+             "status D2H");
         MTRY(cudaStreamSynchronize(s), "cudaStreamSynchronize");
-        MCHK(q3cu_device_status(ctx, stream, nullptr));
+        if (*m->h_status) MCHK(q3cu_device_status(ctx, stream, nullptr));
     }
     return Q3CU_OK;
 }
@@ -371,7 +388,9 @@ q3cu_status q3cu_model_destroy(q3cu_model *m) {
     if (m->graph) cudaGraphExecDestroy(m->graph);
     if (m->ev_in) cudaEventDestroy(m->ev_in);
     if (m->ev_out) cudaEventDestroy(m->ev_out);
+    if (m->ev_step) cudaEventDestroy(m->ev_step);
     if (m->own) cudaStreamDestroy(m->own);
+    if (m->h_step) cudaFreeHost(m->h_step);
     cudaError_t e = m->arena ? cudaFree(m->arena) : cudaSuccess;
     delete m;
     return e == cudaSuccess ? Q3CU_OK : cuda_err(e, "cudaFree (model)");
