@@ -150,10 +150,11 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__re
 //     by cp.async (padded, as above), a thread per position runs its score
 //     chain and writes att;
 //   attn_values_kernel: a CTA per (head, half-head = 64 elements = one Q8_0
-//     group) -- the row max, the libm-identical exponentials into shared
-//     memory, their sum in position order by one thread, the division, then a
-//     thread per element runs its value chain over the positions (V half-rows
-//     through an AV_NST-deep cp.async ring) and the CTA quantizes its group.
+//     group) -- two warps take the row max, the libm-identical exponentials
+//     into shared memory, their sum in position order by one thread, the
+//     division, then a thread per element runs its value chain over the
+//     positions, while the other two warps stream V half-rows through an
+//     AV_NST-deep cp.async ring; the CTA quantizes its group.
 // Both halves of a head compute the same probabilities (the same operations on
 // the same scores), so every chain keeps the reference's order and bits.  Both
 // kernels read the position from device memory and size their work from it,
@@ -163,7 +164,7 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__re
 constexpr int AV_COLS = 64;                                  // elements per values CTA
 constexpr int AV_ROWB = AV_COLS * 4;                         // staged V half-row
 constexpr size_t AV_BUF = size_t(AT_CH) * AV_ROWB;           // 32 KB per chunk
-constexpr int AV_NST = 4;                                    // ring depth
+constexpr int AV_NST = 4;                                    // ring depth (three chunks in flight)
 constexpr int AV_MAXPOS = 16384;                             // probabilities in shared memory up to here
 constexpr int AS_PER_SM = 3;                                 // resident scores CTAs per SM (67.5 KB each)
 
@@ -289,10 +290,11 @@ __device__ __forceinline__ float value_chain(float acc, const float *p, const fl
     return acc;
 }
 
-// Copies columns [col0, col0 + 64) of V rows c0 .. c0+n-1 of kv head kvh into buf.
+// Copies columns [col0, col0 + 64) of V rows c0 .. c0+n-1 of kv head kvh into
+// buf, by threads t = 0 .. nthr-1 of the copying warps.
 __device__ __forceinline__ void attn_stage_half(uint8_t *buf, const float *vc, int c0, int n, int kv_dim, int kvh,
-                                                int col0, int tid) {
-    for (int f = tid; f < n * (AV_ROWB / 16); f += AT_HD) {
+                                                int col0, int t, int nthr) {
+    for (int f = t; f < n * (AV_ROWB / 16); f += nthr) {
         const int r = f / (AV_ROWB / 16), pc = f % (AV_ROWB / 16);
         cp_async16(buf + r * AV_ROWB + pc * 16, vc + int64_t(c0 + r) * kv_dim + kvh * AT_HD + col0 + pc * 4);
     }
@@ -310,50 +312,57 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_values_kernel(const float *att,
     griddep_launch_dependents();
     const int h = blockIdx.x, part = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kvh = h / kv_mul, col0 = part * AV_COLS;
+    // Warps 0-1 run the value chains (thread = element); warps 2-3 copy V.  An
+    // SM holds only ~50 KB of cp.async in flight, so issuing a chunk can stall
+    // its issuer: only the copying warps issue, while the chains run.
+    const bool producer = tid >= AV_COLS;
+    const int pt = tid - AV_COLS;
     load_exp_table(tab);
     griddep_wait();                                          // att (and the caches, written two kernels back)
     const int npos = sp->pos + 1, nch = (npos + AT_CH - 1) / AT_CH;
-    // the first AV_NST - 1 chunks of V stream in while the softmax runs
-    for (int c = 0; c < AV_NST - 1; ++c) {
+    auto stage = [&](int c) {                                // chunk c into slot c % AV_NST, or an empty group
         if (c < nch) {
             const int c0 = c * AT_CH;
-            attn_stage_half(dyn + c * AV_BUF, vc, c0, npos - c0 < AT_CH ? npos - c0 : AT_CH, kv_dim, kvh, col0, tid);
-        } else {
-            cp_async_commit();                               // an empty group keeps the count uniform
-        }
-    }
-    const float *a = att + int64_t(h) * seq_len;
-    float m = 0.0f;                                           // softmax's max starts at 0
-    for (int t = tid; t < npos; t += AT_HD) m = fmaxf(m, a[t]);   // a NaN never replaces the max
-    m = warp_max(m);
-    if (lane == 0) red[warp] = m;
-    __syncthreads();                                          // (also: the exp table is loaded)
-    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    for (int t = tid; t < npos; t += AT_HD) pr[t] = expf_host(__fsub_rn(a[t], m), tab);
-    __syncthreads();
-    if (tid == 0) sum_sh = ordered_sum_smem(0.0f, pr, npos);
-    __syncthreads();
-    const float sum = sum_sh;
-    for (int t = tid; t < npos; t += AT_HD) pr[t] = __fdiv_rn(pr[t], sum);
-    // value chains: thread j < 64 runs element col0 + j over the positions in order
-    float acc = 0.0f;
-    for (int c = 0; c < nch; ++c) {
-        const int cn = c + AV_NST - 1;                        // into the slot chunk c - 1 used
-        if (cn < nch) {
-            const int c0 = cn * AT_CH;
-            attn_stage_half(dyn + (cn % AV_NST) * AV_BUF, vc, c0, npos - c0 < AT_CH ? npos - c0 : AT_CH, kv_dim,
-                            kvh, col0, tid);
+            attn_stage_half(dyn + (c % AV_NST) * AV_BUF, vc, c0, npos - c0 < AT_CH ? npos - c0 : AT_CH, kv_dim, kvh,
+                            col0, pt, AT_HD - AV_COLS);
         } else {
             cp_async_commit();
         }
-        cp_async_wait<AV_NST - 1>();
-        __syncthreads();                                      // chunk c landed; (c == 0) the probabilities are final
-        if (tid < AV_COLS) {
+    };
+    if (producer) {                                          // the first chunks stream in during the softmax
+        for (int c = 0; c < AV_NST - 1; ++c) stage(c);
+    } else {                                                 // the softmax by the chain warps (named barrier 1)
+        const float *a = att + int64_t(h) * seq_len;
+        float m = 0.0f;                                       // softmax's max starts at 0
+        for (int t = tid; t < npos; t += AV_COLS) m = fmaxf(m, a[t]);   // a NaN never replaces the max
+        m = warp_max(m);
+        if (lane == 0) red[warp] = m;
+        named_sync(1, AV_COLS);                               // (also: the exp table is loaded)
+        m = fmaxf(red[0], red[1]);
+        for (int t = tid; t < npos; t += AV_COLS) pr[t] = expf_host(__fsub_rn(a[t], m), tab);
+        named_sync(1, AV_COLS);
+        if (tid == 0) sum_sh = ordered_sum_smem(0.0f, pr, npos);
+        named_sync(1, AV_COLS);
+        const float sum = sum_sh;
+        for (int t = tid; t < npos; t += AV_COLS) pr[t] = __fdiv_rn(pr[t], sum);
+    }
+    // value chains: thread j < 64 runs element col0 + j over the positions in
+    // order.  Iteration c: chunk c has landed (the copiers' wait, then the
+    // barrier), the copiers refill slot (c + AV_NST - 1) % AV_NST -- chunk
+    // c - 1's, which every chain finished before this barrier -- while the
+    // chains run c.
+    float acc = 0.0f;
+    for (int c = 0; c < nch; ++c) {
+        if (producer) cp_async_wait<AV_NST - 2>();            // chunks c .. c + AV_NST - 2 were pending
+        __syncthreads();                                      // chunk c visible; (c == 0) the probabilities are final
+        if (producer) {
+            stage(c + AV_NST - 1);
+        } else {
             const int c0 = c * AT_CH, n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
             acc = value_chain(acc, pr + c0, reinterpret_cast<const float *>(dyn + (c % AV_NST) * AV_BUF) + tid, n);
         }
-        __syncthreads();                                      // before the slot is refilled
     }
+    if (producer) cp_async_wait<0>();                         // nothing in flight at exit
     // the quantize of this group (:431): absmax from 0, scale = wmax / 127, codes
     const float gm = warp_max(tid < AV_COLS ? fmaxf(0.0f, fabsf(acc)) : 0.0f);
     if (lane == 0) red[warp] = gm;
