@@ -261,30 +261,39 @@ __global__ void __launch_bounds__(AT_HD) attn_scores_kernel(const float *qkv, fl
 __device__ __forceinline__ float value_chain(float acc, const float *p, const float *v, int n) {
     const float4 *p4 = reinterpret_cast<const float4 *>(p);
     const int nb = n >> 3;
+    // two register sets, A and B, alternate: one batch is loaded while the
+    // other is added, with no copies between them
+    auto add8 = [&](const float4 &pa, const float4 &pb, const float *x) {
+        acc = __fadd_rn(acc, __fmul_rn(pa.x, x[0]));
+        acc = __fadd_rn(acc, __fmul_rn(pa.y, x[1]));
+        acc = __fadd_rn(acc, __fmul_rn(pa.z, x[2]));
+        acc = __fadd_rn(acc, __fmul_rn(pa.w, x[3]));
+        acc = __fadd_rn(acc, __fmul_rn(pb.x, x[4]));
+        acc = __fadd_rn(acc, __fmul_rn(pb.y, x[5]));
+        acc = __fadd_rn(acc, __fmul_rn(pb.z, x[6]));
+        acc = __fadd_rn(acc, __fmul_rn(pb.w, x[7]));
+    };
     if (nb > 0) {
-        float4 pa = p4[0], pb = p4[1];
-        float va[8];
+        float4 a0 = p4[0], b0 = p4[1];
+        float x0[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) va[i] = v[i * AV_COLS];
-        for (int b = 0; b < nb; ++b) {
-            const int kn = b + 1 < nb ? b + 1 : b;                 // the last batch reloads itself
-            const float4 qa = p4[2 * kn], qb = p4[2 * kn + 1];
-            float vn[8];
+        for (int i = 0; i < 8; ++i) x0[i] = v[i * AV_COLS];
+        int b = 0;
+        for (; b + 2 <= nb; b += 2) {
+            const int k1 = b + 1;                                  // < nb
+            const float4 a1 = p4[2 * k1], b1 = p4[2 * k1 + 1];
+            float x1[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) vn[i] = v[(kn * 8 + i) * AV_COLS];
-            acc = __fadd_rn(acc, __fmul_rn(pa.x, va[0]));
-            acc = __fadd_rn(acc, __fmul_rn(pa.y, va[1]));
-            acc = __fadd_rn(acc, __fmul_rn(pa.z, va[2]));
-            acc = __fadd_rn(acc, __fmul_rn(pa.w, va[3]));
-            acc = __fadd_rn(acc, __fmul_rn(pb.x, va[4]));
-            acc = __fadd_rn(acc, __fmul_rn(pb.y, va[5]));
-            acc = __fadd_rn(acc, __fmul_rn(pb.z, va[6]));
-            acc = __fadd_rn(acc, __fmul_rn(pb.w, va[7]));
-            pa = qa;
-            pb = qb;
+            for (int i = 0; i < 8; ++i) x1[i] = v[(k1 * 8 + i) * AV_COLS];
+            add8(a0, b0, x0);                                      // batch b
+            const int k2 = b + 2 < nb ? b + 2 : k1;                // past the end: reload (unused)
+            a0 = p4[2 * k2];
+            b0 = p4[2 * k2 + 1];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) va[i] = vn[i];
+            for (int i = 0; i < 8; ++i) x0[i] = v[(k2 * 8 + i) * AV_COLS];
+            add8(a1, b1, x1);                                      // batch b + 1
         }
+        if (b < nb) add8(a0, b0, x0);                              // odd count: the last batch
     }
     for (int t = nb << 3; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(p[t], v[t * AV_COLS]));
     return acc;
