@@ -43,12 +43,68 @@ GS = 64
 E2E_CHUNKS = 8          # token-row chunks of the pipelined end-to-end step
 
 
+# ---------------------------------------------------------------------------- parity helpers
+# After timing, the checker leg compares a sample of the last timed step's
+# outputs with the oracle (oracle/, the CPU restatement of the reference pinned
+# to it by the tests) applied to that step's inputs: mismatch counts go on the
+# JSON line.  Inputs that the step updates in place are snapshotted (a few rows)
+# between the last two timed steps, outside the timed events.
+RTOL, ATOL, BF16_RTOL = 1e-5, 1e-6, 1e-2
+
+
+def _host(t):
+    import numpy as np
+    import torch
+    if t.dtype == torch.bfloat16:
+        return t.view(torch.int16).cpu().numpy().view(np.uint16)
+    return t.detach().cpu().numpy()
+
+
+def _sample_rows(n, k=16):
+    import numpy as np
+    return np.unique(np.linspace(0, max(n - 1, 0), min(n, k)).round().astype(np.int64)) if n else np.zeros(0, np.int64)
+
+
+def _q8_mismatch(qg, sg, qo, so):
+    import numpy as np
+    return int((qg != qo).sum()) + int((np.ascontiguousarray(sg).view(np.uint32) !=
+                                        np.ascontiguousarray(so).view(np.uint32)).sum())
+
+
+def _f32(a):
+    import numpy as np
+    return (a.astype(np.uint32) << 16).view(np.float32) if a.dtype == np.uint16 else np.asarray(a, np.float32)
+
+
+def _tol_mismatch(g, o, rtol, atol):
+    """Elements of g outside atol + rtol*|o| of o (NaN must match NaN)."""
+    import numpy as np
+    g, o = _f32(g).ravel(), _f32(o).ravel()
+    nan = np.isnan(o)
+    bad = int((np.isnan(g) != nan).sum())
+    return bad + int((np.abs(g[~nan] - o[~nan]) > atol + rtol * np.abs(o[~nan])).sum())
+
+
+def _softmax_mismatch(g, x, lens):
+    """Scores of the rows of g outside 1e-5 rel / 1e-6 abs of a binary64 softmax
+    of the inputs x (the max starting at 0, as the reference's)."""
+    import numpy as np
+    bad, o = 0, 0
+    for n in lens:
+        r = x[o:o + n].astype(np.float64)
+        e = np.exp(r - max(0.0, float(r.max())))
+        bad += _tol_mismatch(g[o:o + n], (e / e.sum()).astype(np.float64), RTOL, ATOL)
+        o += n
+    return bad
+
+
 # ---------------------------------------------------------------------------- workloads
 class Workload:
     name = ""
     tokens = 0
     dtype = "f32"
     e2e_note = ""
+    scaling = "weak"
 
     def kernels(self):              # [(name, algorithmic bytes per launch)]
         raise NotImplementedError
@@ -152,6 +208,22 @@ class Prefill4B(Workload):
     def bytes_for_tokens(self, n):
         return self.total_bytes() * n / self.tokens
 
+    def parity_snapshot(self, d):
+        S = _sample_rows(self.tokens)
+        return {"rows": S, "q": _host(d["q"][S]), "k": _host(d["k"][S])}
+
+    def parity(self, oracle, snap, d):
+        S = snap["rows"]
+        qn, kn, w = _host(d["qn"]), _host(d["kn"]), _host(d["w"])
+        qo, so = oracle.rows_rmsnorm_q8(_host(d["x"][S]), w)
+        qr, kr = oracle.rows_qk_norm_rope(snap["q"], snap["k"], _host(d["pos"][S]), qn, kn)
+        ho, hs = oracle.rows_swiglu_q8(_host(d["hb"][S]), _host(d["hb2"][S]))
+        rt, at = (BF16_RTOL, ATOL) if snap["q"].dtype.kind == "u" else (RTOL, ATOL)
+        return {"token_rows": int(S.size),
+                "rmsnorm_q8": _q8_mismatch(_host(d["xq"][S]), _host(d["xs"][S]), qo, so),
+                "qk_norm_rope": _tol_mismatch(_host(d["q"][S]), qr, rt, at) + _tol_mismatch(_host(d["k"][S]), kr, rt, at),
+                "swiglu_q8": _q8_mismatch(_host(d["hq"][S]), _host(d["hs"][S]), ho, hs)}
+
 
 def _ragged(np, pos, nh):
     """Offsets and lengths of the attention score rows of tokens at `pos`:
@@ -199,7 +271,7 @@ class _BF16Layer(Workload):
             "q": torch.randn(T, self.nh, self.hd, device=dev, generator=g).to(torch.bfloat16),
             "k": torch.randn(T, self.nkv, self.hd, device=dev, generator=g).to(torch.bfloat16),
             "pos": torch.from_numpy(pos).to(dev),
-            "att": 2.0 * torch.randn(int(lens.sum()), device=dev, generator=g),
+            "att": torch.randn(int(lens.sum()), device=dev, generator=g).mul_(2.0),
             "off": torch.from_numpy(off).to(dev), "len": torch.from_numpy(lens).to(dev),
             "xq": torch.empty(T, D, dtype=torch.int8, device=dev),
             "xs": torch.empty(T, D // GS, dtype=torch.float32, device=dev),
@@ -272,17 +344,49 @@ class _BF16Layer(Workload):
     def bytes_for_tokens(self, n):
         return sum(b for _, b in self.kernel_bytes(self.sample_pos(n)))
 
+    def parity_snapshot(self, d):
+        import numpy as np
+        snap = Prefill4B.parity_snapshot(self, d)
+        off, lens = _ragged(np, self.pos, self.nh)
+        R = _sample_rows(lens.size)
+        R = np.unique(np.concatenate([R, [int(np.argmax(lens))]])) if lens.size else R
+        att = d["att"]
+        snap["sm_rows"], snap["sm_in"] = R, [_host(att[int(off[r]):int(off[r]) + int(lens[r])]) for r in R]
+        return snap
+
+    def parity(self, oracle, snap, d):
+        import numpy as np
+        out = Prefill4B.parity(self, oracle, snap, d)
+        off, lens = _ragged(np, self.pos, self.nh)
+        R, att = snap["sm_rows"], d["att"]
+        g = np.concatenate([_host(att[int(off[r]):int(off[r]) + int(lens[r])]) for r in R]) if R.size else \
+            np.zeros(0, np.float32)
+        x = np.concatenate(snap["sm_in"]) if R.size else g
+        out["softmax_rows"] = _softmax_mismatch(g, x, [int(lens[r]) for r in R])
+        out["softmax_row_count"] = int(R.size)
+        return out
+
 
 class Decode8B(_BF16Layer):
     """Qwen3-8B-shaped batched decode: T bf16 tokens at positions uniform in
-    0..32767 (seed 0)."""
+    0..32767 (seed 0).  Under torchrun the tokens are split over the ranks in
+    contiguous runs of near-equal softmax work (sum of pos + 1; strong
+    scaling)."""
     name = "decode8b"
 
-    def __init__(self, tokens=256, dim=4096, nh=32, nkv=8, hd=128, hidden=12288, maxpos=32767, seed=0):
+    scaling = "strong"
+
+    def __init__(self, tokens=256, dim=4096, nh=32, nkv=8, hd=128, hidden=12288, maxpos=32767, seed=0, shard=None):
         import numpy as np
-        self.tokens, self.dim, self.nh, self.nkv, self.hd, self.hidden = tokens, dim, nh, nkv, hd, hidden
-        self.pos = np.random.default_rng(seed).integers(0, maxpos + 1, size=tokens).astype(np.int32)
-        self.e2e_tokens = tokens
+        from metalqwen3_b200.shard import split_by_work
+        self.dim, self.nh, self.nkv, self.hd, self.hidden = dim, nh, nkv, hd, hidden
+        pos = np.random.default_rng(seed).integers(0, maxpos + 1, size=tokens).astype(np.int32)
+        self.total_tokens = tokens
+        if shard is not None:          # this rank's tokens: contiguous, cut at equal softmax work (sum of pos + 1)
+            a, b = split_by_work(pos.astype(np.int64) + 1, shard[1])[shard[0]]
+            pos = pos[a:b]
+        self.pos, self.tokens = pos, int(pos.size)
+        self.e2e_tokens = self.tokens
 
     def sample_pos(self, n):
         return self.pos[:n]
@@ -297,16 +401,26 @@ class Decode8B(_BF16Layer):
 
 
 class Prefill14B(_BF16Layer):
-    """Qwen3-14B-shaped long-context prefill, one layer: per GPU T bf16 tokens
-    in sequences of 4096 (positions 0..4095 each), 1% outlier channels x20,
-    causal softmax of every head's row."""
+    """Qwen3-14B-shaped long-context prefill, one layer: T bf16 tokens in all
+    (131,072 = 32 sequences of 4096, positions 0..4095 each), 1% outlier
+    channels x20, causal softmax of every head's row.  Under torchrun the
+    sequences are split over the ranks (strong scaling); --weak runs T on every
+    GPU."""
     name = "prefill14b"
     outliers = True
 
-    def __init__(self, tokens=16384, dim=5120, nh=40, nkv=8, hd=128, hidden=17408, seqlen=4096, e2e_tokens=512):
+    scaling = "strong"
+
+    def __init__(self, tokens=131072, dim=5120, nh=40, nkv=8, hd=128, hidden=17408, seqlen=4096, e2e_tokens=512,
+                 shard=None):
         import numpy as np
-        self.tokens, self.dim, self.nh, self.nkv, self.hd, self.hidden, self.seqlen = \
-            tokens, dim, nh, nkv, hd, hidden, seqlen
+        from metalqwen3_b200.shard import split_even
+        self.dim, self.nh, self.nkv, self.hd, self.hidden, self.seqlen = dim, nh, nkv, hd, hidden, seqlen
+        self.total_tokens = tokens
+        if shard is not None:          # this rank's whole sequences (token rows are independent)
+            a, b = split_even((tokens + seqlen - 1) // seqlen, shard[1])[shard[0]]
+            tokens = max(0, min(tokens, b * seqlen) - a * seqlen)
+        self.tokens = tokens
         self.pos = (np.arange(tokens) % seqlen).astype(np.int32)
         self.e2e_tokens = min(e2e_tokens, tokens)
         self.e2e_note = (f"end to end on the first {self.e2e_tokens} tokens of a sequence per step (a full step "
@@ -329,20 +443,31 @@ class Prefill14B(_BF16Layer):
 class Embed(Workload):
     """Q8_0 embedding dequant/gather: a vocab x dim Q8_0 table on the device, N
     Zipf(1.1)-distributed token ids; each lookup writes the f32 row and its
-    re-quantized Q8_0 codes + scales."""
+    re-quantized Q8_0 codes + scales.  Under torchrun the table is replicated on
+    every GPU (made outside the timed region) and the ids are split over the
+    ranks (strong scaling)."""
     name = "embed"
     dtype = "int8 codes + f32 scales -> f32 rows + Q8_0"
 
-    def __init__(self, tokens=1048576, vocab=151936, dim=4096, seed=0, e2e_lookups=65536):
+    scaling = "strong"
+
+    def __init__(self, tokens=1048576, vocab=151936, dim=4096, seed=0, e2e_lookups=65536, shard=None):
         import numpy as np
-        self.tokens, self.vocab, self.dim = tokens, vocab, dim
+        from metalqwen3_b200.shard import split_even
+        self.vocab, self.dim = vocab, dim
         rng = np.random.default_rng(seed)
         ranks = np.empty(0, np.int64)
         while ranks.size < tokens:                     # Zipf(1.1), truncated to the vocab by rejection
             r = rng.zipf(1.1, size=tokens)
             ranks = np.concatenate([ranks, r[r <= vocab]])
         perm = rng.permutation(vocab)                  # rank -> token id: a seeded permutation
-        self.ids = perm[ranks[:tokens] - 1].astype(np.int32)
+        ids = perm[ranks[:tokens] - 1].astype(np.int32)
+        self.total_tokens = tokens
+        if shard is not None:                          # this rank's lookups (the table is replicated)
+            a, b = split_even(tokens, shard[1])[shard[0]]
+            ids = ids[a:b]
+        self.ids, self.tokens = ids, int(ids.size)
+        tokens = self.tokens
         self.e2e_lookups = min(e2e_lookups, tokens)
         self.e2e_note = (f"end to end on a sub-batch of {self.e2e_lookups} lookups per step (one full step "
                          f"moves {tokens * dim * 5 / 1e9:.1f} GB of rows to the host)")
@@ -404,6 +529,19 @@ class Embed(Workload):
 
     def bytes_for_tokens(self, n):
         return self.total_bytes() * n / self.tokens
+
+    def parity_snapshot(self, d):
+        return {"rows": _sample_rows(self.tokens, 64)}
+
+    def parity(self, oracle, snap, d):
+        import numpy as np
+        import torch
+        S = snap["rows"]
+        ids = torch.from_numpy(self.ids[S].astype(np.int64)).to(d["tq"].device)
+        ro, rq, rs, bad = oracle.rows_embed(_host(d["tq"][ids]), _host(d["ts"][ids]), np.arange(S.size, dtype=np.int32))
+        return {"lookups": int(S.size), "bad_ids": int(bad),
+                "f32_rows": int((_host(d["out"][S]).view(np.uint32) != ro.view(np.uint32)).sum()),
+                "q8_rows": _q8_mismatch(_host(d["oq"][S]), _host(d["os"][S]), rq, rs)}
 
 
 class Decode06B(Workload):
@@ -575,6 +713,26 @@ class Decode06B(Workload):
     def bytes_for_tokens(self, n):
         return self.total_bytes()
 
+    def parity_snapshot(self, d):
+        return {}
+
+    def parity(self, oracle, snap, d):
+        """The outputs the step leaves behind: the embedding row, the final
+        RMSNorm+Q8_0 and the last layer's quantize and SwiGLU+Q8_0."""
+        import numpy as np
+        import torch
+        L = self.layers
+        ids = d["ids"].to(torch.int64)
+        ro, _, _, _ = oracle.rows_embed(_host(d["tq"][ids]), _host(d["ts"][ids]),
+                                        np.arange(self.tokens, dtype=np.int32), want_q8=False)
+        xq, xs = oracle.rows_rmsnorm_q8(_host(d["xfin"]), _host(d["wfin"]))
+        aq, as_ = oracle.rows_quantize(_host(d["ao"][L - 1]))
+        hq, hs = oracle.rows_swiglu_q8(_host(d["hb"][L - 1]), _host(d["hb2"][L - 1]))
+        return {"embed_gather": int((_host(d["emb"]).view(np.uint32) != ro.view(np.uint32)).sum()),
+                "rmsnorm_q8": _q8_mismatch(_host(d["xq"]), _host(d["xs"]), xq, xs),
+                "quantize_q8": _q8_mismatch(_host(d["aq"]), _host(d["as"]), aq, as_),
+                "swiglu_q8": _q8_mismatch(_host(d["hq"]), _host(d["hs"]), hq, hs)}
+
 
 class Matmul06B(Workload):
     """Qwen3-0.6B decode-token Q8_0 matmuls (qwen3_original.c:357-359, :432,
@@ -681,6 +839,23 @@ class Matmul06B(Workload):
 
     def bytes_for_tokens(self, n):
         return self.total_bytes() / self.tokens
+
+    def parity_snapshot(self, d):
+        return {}
+
+    def parity(self, oracle, snap, d):
+        """256 classifier rows and the whole last-layer w2 product, bit for bit."""
+        import numpy as np
+        out = {}
+        for nm, rows in (("cls", _sample_rows(self.vocab, 256)), (f"w2{self.layers - 1}", None)):
+            wq, ws = d["wq_" + nm], d["ws_" + nm]
+            if rows is not None:
+                wq, ws = wq[rows], ws[rows]
+            o = oracle.matmul(_host(d["xq_" + nm]), _host(d["xs_" + nm]), _host(wq), _host(ws))
+            g = _host(d["o_" + nm])
+            g = g[:, rows] if rows is not None else g
+            out[nm] = int((np.ascontiguousarray(g).view(np.uint32) != o.view(np.uint32)).sum())
+        return out
 
 
 class Forward06B(Workload):
@@ -813,6 +988,29 @@ class Forward06B(Workload):
 
     def bytes_for_tokens(self, n):
         return self.total_bytes()
+
+    def parity_snapshot(self, d):
+        return {}
+
+    def parity(self, oracle, snap, d):
+        """The logits of the last end-to-end step against the reference's own
+        qwen3_forward (the oracle's restatement where it is not built) on the
+        same checkpoint, token and position, with the same zero KV cache below
+        pos: every one of the vocab logits bit for bit."""
+        import numpy as np
+        g = np.asarray(d["logits_host"], np.float32)
+        try:
+            self.cpu_step(None, np, 1, 1, None)          # builds the reference model on the same image
+            want = self._ref.forward(self._t, 7, self.pos)
+        except (FileNotFoundError, OSError):
+            from oracle.oracle import OracleModel
+            om = OracleModel(self.image(1234), ctx_length=self.pos + 1, oracle=oracle)
+            want = om.forward(7, self.pos)
+            om.close()
+        nan = np.isnan(want)
+        return {"logits": int((np.isnan(g) != nan).sum() +
+                              (g[~nan].view(np.uint32) != want[~nan].view(np.uint32)).sum()),
+                "vocab": int(want.size)}
 
 
 WORKLOADS = {"prefill4b": Prefill4B, "decode8b": Decode8B, "embed": Embed, "prefill14b": Prefill14B,
@@ -953,7 +1151,8 @@ def run_reference(args, wl):
     line = {
         "impl": "reference", "metric": METRIC, "value": round(val, 4), "unit": "GB/s", "n_gpus": args.gpus,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(el / args.steps * 1e3, 4),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+        "higher_is_better": True, "scaling": wl.scaling if not args.weak else "weak", "vs_baseline": None,
+        "dtype": wl.dtype, "data": "synthetic",
         "config": dict(wl.config(), sample_tokens_per_step=sample),
         "tokens_per_s": round(getattr(wl, "cpu_tokens", sample) * args.steps / el, 2),
         "cpu_baseline": {"value": round(val, 4), "unit": "GB/s", "cores": threads, "kind": kind,
@@ -1037,6 +1236,70 @@ METRIC = "fused layer-kernel HBM GB/s & tokens/s at 1/2/4/8 B200; % of HBM roofl
 
 
 # ---------------------------------------------------------------------------- our arm
+def h2d_probe(args):
+    """Host<->device copy bandwidth of every rank at once (pinned host memory,
+    1 GiB per copy, CUDA events on the copying stream, max over ranks): the
+    ceiling of the end-to-end numbers at N GPUs.  One JSON line."""
+    import torch
+    import torch.distributed as dist
+    world, rank, local, dev = _dist_init(torch, dist)
+    nbytes = 1 << 30
+    h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    g = torch.empty(nbytes, dtype=torch.uint8, device=dev)
+    s = torch.cuda.Stream(device=dev)
+    out = {}
+    for name, (dst, src) in (("h2d", (g, h)), ("d2h", (h, g))):
+        for _ in range(2):
+            with torch.cuda.stream(s):
+                dst.copy_(src, non_blocking=True)
+        s.synchronize()
+        _barrier(dist, world, local)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with torch.cuda.stream(s):
+            e0.record(s)
+            for _ in range(args.steps):
+                dst.copy_(src, non_blocking=True)
+            e1.record(s)
+        s.synchronize()
+        ms = e0.elapsed_time(e1)
+        per = torch.tensor([nbytes * args.steps / (ms / 1e3) / 1e9], device=dev, dtype=torch.float64)
+        mx = torch.tensor([ms], device=dev, dtype=torch.float64)
+        if world > 1:
+            allv = [torch.zeros_like(per) for _ in range(world)]
+            dist.all_gather(allv, per)
+            dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        else:
+            allv = [per]
+        out[name] = {"per_rank_gbs": [round(float(v.item()), 2) for v in allv],
+                     "aggregate_gbs": round(world * nbytes * args.steps / (float(mx.item()) / 1e3) / 1e9, 2)}
+    if rank == 0:
+        aff = sorted(os.sched_getaffinity(0))
+        print(json.dumps({"probe": "pinned host <-> device copies, all ranks at once", "n_gpus": world,
+                          "bytes_per_copy": nbytes, "copies": args.steps, **out,
+                          "rank0_cpu_affinity": f"{aff[0]}-{aff[-1]} ({len(aff)} cpus)" if aff else None}),
+              flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+    return 0
+
+
+def _dist_init(torch, dist):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    return world, rank, local, dev
+
+
+def _barrier(dist, world, local):
+    if world > 1:
+        dist.barrier(device_ids=[local])
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -1044,15 +1307,29 @@ def main():
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="prefill4b")
-    ap.add_argument("--tokens", type=int, default=0, help="token rows per GPU (default: the workload's)")
+    ap.add_argument("--tokens", type=int, default=0,
+                    help="token rows (lookups): per GPU for weak workloads, the total for strong ones")
+    ap.add_argument("--weak", action="store_true",
+                    help="run a strong-scaling workload with its whole size on every GPU (replicas)")
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-kernels", action="store_true",
                     help="time each kernel of the workload on the reference's CPU code (1 core and all cores) and exit")
+    ap.add_argument("--h2d-probe", action="store_true",
+                    help="measure pinned host<->device copy bandwidth on every rank at once and exit")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    wl = WORKLOADS[args.workload](tokens=args.tokens) if args.tokens else WORKLOADS[args.workload]()
+    if args.h2d_probe:
+        return h2d_probe(args)
+    cls = WORKLOADS[args.workload]
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    rank_env = int(os.environ.get("RANK", "0"))
+    strong = cls.scaling == "strong" and not args.weak
+    kw = {"tokens": args.tokens} if args.tokens else {}
+    if strong:
+        kw["shard"] = (rank_env, world_env)
+    wl = cls(**kw)
 
     if args.impl == "reference":
         return run_reference(args, wl)
@@ -1062,14 +1339,7 @@ def main():
     import torch
     import torch.distributed as dist
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
-    if world > 1:
-        import datetime
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
+    world, rank, local, dev = _dist_init(torch, dist)
 
     from metalqwen3_b200.q3cu import Q3CU
     q3 = Q3CU(local)
@@ -1087,27 +1357,47 @@ def main():
         flush_r.amax()
 
     def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local])
+        _barrier(dist, world, local)
 
-    # warm-up
+    # warm-up; the host time to enqueue one step sizes the start gate below
+    enq = []
     with torch.cuda.stream(stream):
         for _ in range(args.warmup):
+            t0 = time.perf_counter()
             wl.launch(q3, d, stream)
+            enq.append(time.perf_counter() - t0)
             cold_l2()
     stream.synchronize()
     if q3.device_status(stream) != 0:
         raise RuntimeError("device status set during warm-up")
+    # Every timed step starts from a common point on all ranks: a host barrier,
+    # then a fixed-length device sleep (torch's bounded spin kernel) on the
+    # stream while the host enqueues the step behind it.  The step's start event
+    # follows the sleep, so neither the barrier's skew between hosts nor the
+    # host's launch latency falls inside the step; its end event follows the
+    # step's last kernel.  Step time = max over ranks of end - start, per step.
+    gate_s = max(100e-6, 3.0 * statistics.median(enq[1:] or enq))
+    gate_cycles = int(gate_s * 2.0e9)
 
     clocks = ClockSampler(local)
     clocks.start()
     ev = [[[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(nk)] for _ in range(args.steps)]
+    sev = [[torch.cuda.Event(enable_timing=True) for _ in range(2)] for _ in range(args.steps)]
+    snap = None
     barrier()
     torch.cuda.synchronize(dev)
     launches = 0
     with torch.cuda.stream(stream):
         for i in range(args.steps):
+            if i == args.steps - 1 and hasattr(wl, "parity_snapshot"):
+                stream.synchronize()
+                snap = wl.parity_snapshot(d)        # inputs of the last step that it updates in place
+                cold_l2()
+            barrier()
+            torch.cuda._sleep(gate_cycles)
+            sev[i][0].record(stream)
             launches += wl.launch(q3, d, stream, events=ev[i])
+            sev[i][1].record(stream)
             cold_l2()                           # outside the events: L2 cold for the next step
     stream.synchronize()
     torch.cuda.synchronize(dev)
@@ -1115,12 +1405,24 @@ def main():
     clk = clocks.stop()
 
     per_kernel = [[ev[i][k][0].elapsed_time(ev[i][k][1]) for i in range(args.steps)] for k in range(nk)]
-    step_ms = [sum(per_kernel[k][i] for k in range(nk)) for i in range(args.steps)]
-    total_ms = sum(step_ms)
+    step_ms = torch.tensor([sev[i][0].elapsed_time(sev[i][1]) for i in range(args.steps)], dtype=torch.float64,
+                           device=dev)
+    kern_ms = torch.tensor([sum(per_kernel[k][i] for k in range(nk)) for i in range(args.steps)],
+                           dtype=torch.float64, device=dev)
+    step_bytes = torch.tensor([float(wl.total_bytes()), float(wl.tokens)], dtype=torch.float64, device=dev)
+    own_ms = float(step_ms.sum().item())
     if world > 1:
-        t = torch.tensor([total_ms], device=dev, dtype=torch.float64)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        total_ms = float(t.item())
+        dist.all_reduce(step_ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(kern_ms, op=dist.ReduceOp.MAX)
+        dist.all_reduce(step_bytes, op=dist.ReduceOp.SUM)
+        rank_ms = [torch.zeros(1, dtype=torch.float64, device=dev) for _ in range(world)]
+        dist.all_gather(rank_ms, torch.tensor([own_ms], dtype=torch.float64, device=dev))
+        rank_ms = [float(t.item()) / args.steps for t in rank_ms]
+    else:
+        rank_ms = [own_ms / args.steps]
+    total_ms = float(step_ms.sum().item())
+    kernel_ms = float(kern_ms.sum().item())
+    all_bytes, all_tokens = float(step_bytes[0].item()), float(step_bytes[1].item())
     if q3.device_status(stream) != 0:
         raise RuntimeError("device status set during the timed region")
 
@@ -1136,9 +1438,9 @@ def main():
     # Row-sliceable workloads pipeline each step over E2E_CHUNKS token-row chunks:
     # copy-in on two streams (alternate chunks), kernels on another, copy-out on
     # a fourth, so PCIe moves inputs and outputs at the same time (it is full
-    # duplex).  A chunk's
-    # copy-in for the next step waits for its copy-out (q and k are updated in
-    # place).  Other workloads copy in, run and copy out on one stream.
+    # duplex).  A chunk's copy-in for the next step waits for its copy-out (q and
+    # k are updated in place).  Other workloads copy in, run and copy out on one
+    # stream.
     chunks = [(i * wl.tokens // E2E_CHUNKS, (i + 1) * wl.tokens // E2E_CHUNKS)
               for i in range(E2E_CHUNKS)] if hasattr(wl, "slice") else None
     s_ins = [torch.cuda.Stream(device=dev) for _ in range(2)]     # chunks alternate between two copy-in streams
@@ -1187,18 +1489,20 @@ def main():
     e1.record(last)
     torch.cuda.synchronize(dev)
     e2e_ms = e0.elapsed_time(e1)
+    e2e_b = torch.tensor([float(wl.e2e_bytes() if hasattr(wl, "e2e_bytes") else wl.total_bytes())],
+                         dtype=torch.float64, device=dev)
     if world > 1:
         t = torch.tensor([e2e_ms], device=dev, dtype=torch.float64)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.all_reduce(e2e_b, op=dist.ReduceOp.SUM)
         e2e_ms = float(t.item())
         barrier()
+    e2e_all_bytes = float(e2e_b.item())
 
     # ---- report ---------------------------------------------------------------
     if rank == 0:
-        step_bytes = wl.total_bytes()
-        e2e_bytes = wl.e2e_bytes() if hasattr(wl, "e2e_bytes") else step_bytes
         ms_per_step = total_ms / args.steps
-        gbs = world * step_bytes * args.steps / (total_ms / 1e3) / 1e9
+        gbs = all_bytes * args.steps / (total_ms / 1e3) / 1e9
         kern = {}
         for k, (name, b) in enumerate(wl.kernels()):
             avg = statistics.mean(per_kernel[k])
@@ -1207,14 +1511,23 @@ def main():
         dom_name, dom_bytes = max(wl.kernels(), key=lambda kb: kb[1])
         dom_avg_s = statistics.mean(per_kernel[[n for n, _ in wl.kernels()].index(dom_name)]) / 1e3
         achieved = dom_bytes / dom_avg_s / 1e9
+        scaling = "strong" if strong else "weak"
+        par = (f"token rows split over {world} GPUs (strong: the configuration's total is fixed)" if strong else
+               f"token rows x{world} (weak: the same batch on every GPU)")
         line = {
             "metric": METRIC, "value": round(gbs, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
-            "config": dict(wl.config(), parallelism=f"token rows x{world} (weak)",
+            "scaling": scaling, "vs_baseline": None, "dtype": wl.dtype, "data": "synthetic",
+            "config": dict(wl.config(), parallelism=par,
+                           total_tokens=int(all_tokens),
                            l2="flushed between timed steps (256 MiB write + 256 MiB read of another buffer, outside the events); "
-                              f"step working set {step_bytes / 1e6:.0f} MB vs 126 MB L2"),
-            "tokens_per_s": round(world * wl.tokens * args.steps / (total_ms / 1e3), 1),
+                              f"step working set {wl.total_bytes() / 1e6:.0f} MB per GPU vs 126 MB L2"),
+            "timing": ("per step: host barrier, a fixed device sleep while the step is enqueued, then CUDA events "
+                       "around the step on the launching stream; step time = max over ranks; value = all ranks' "
+                       "algorithmic bytes / sum of step times"),
+            "kernel_sum_ms_per_step": round(kernel_ms / args.steps, 5),
+            "rank_ms_per_step": [round(x, 5) for x in rank_ms],
+            "tokens_per_s": round(all_tokens * args.steps / (total_ms / 1e3), 1),
             "hbm_frac": round(gbs / world / peak, 4),
             "kernels": kern,
             "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": peak,
@@ -1222,7 +1535,7 @@ def main():
                          else "fallback 6650 GB/s", "unit": "GB/s", "frac": round(achieved / peak, 4),
                          "traffic": profiled_traffic(wl.name, dom_name, dom_bytes),
                          "algorithmic_bytes_per_launch": dom_bytes},
-            "e2e": {"value": round(world * e2e_bytes * args.e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
+            "e2e": {"value": round(e2e_all_bytes * args.e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
                     "path": ("pinned host inputs -> cudaMemcpyAsync H2D -> q3cu C ABI kernels -> D2H, per step"
@@ -1233,6 +1546,13 @@ def main():
         }
         if graph is not None:
             line["graph"] = graph
+        if hasattr(wl, "parity"):
+            # the checker: a sample of the last timed step against the oracle
+            from oracle.oracle import Oracle
+            line["parity"] = {"checked": "last timed step (sampled rows) vs the oracle on the same inputs; "
+                                         "counts of mismatching values (bit-exact ops) or of values outside "
+                                         "the tolerance (RoPE, softmax)",
+                              **wl.parity(Oracle(), snap or {}, d)}
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(wl, args.cpu_seconds)
         print(json.dumps(line), flush=True)

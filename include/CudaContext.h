@@ -3,8 +3,9 @@
  * over the q3cu C ABI (q3cu.h).
  *
  * The engine's wrappers MetalQwen3::metal_rmsnorm / metal_softmax /
- * metal_swiglu / metal_rope (src/metal/MetalQwen3.cpp:479-633) call these
- * methods with the same host-pointer signatures; only the type name changes.
+ * metal_swiglu / metal_rope / metal_attention (src/metal/MetalQwen3.cpp:479-639)
+ * and its error handler (isBatching / endBatch, :56-57) call these methods with
+ * the same host-pointer signatures; only the type name changes.
  * Like MetalContext, each execute* call is synchronous (copy in, run, copy
  * out).  Failures throw std::runtime_error, the exception type MetalContext
  * throws on buffer and command-buffer errors (src/metal/MetalContext.cpp:438-442,
@@ -35,12 +36,24 @@ public:
     bool isInitialized() const { return ctx_ != nullptr; }
     const std::string &lastError() const { return last_error_; }
 
-    // MetalContext::execute* (MetalContext.h:79-85), host pointers, synchronous
+    // MetalContext::beginBatch / endBatch / isBatching (MetalContext.h:58-60).
+    // Every call here is already synchronous and complete on return, so there
+    // is never an open batch: the first two do nothing, isBatching() is false.
+    void beginBatch() {}
+    void endBatch() {}
+    bool isBatching() const { return false; }
+
+    // MetalContext::execute* (MetalContext.h:79-87), host pointers, synchronous
     void executeRMSNorm(float *output, const float *input, const float *weight, int size);
     void executeSoftmax(float *x, int size);
     void executeSwiGLU(float *hb, const float *hb2, int hidden_dim);
     void executeRoPE(float *q, float *k, int head_dim, int pos, int n_heads, int n_kv_heads,
                      const float *q_norm_weights, const float *k_norm_weights);
+    // MetalContext::executeAttention (MetalContext.h:86-87): one token's heads
+    // over the cache rows 0..pos at key_cache + loff / value_cache + loff.
+    void executeAttention(float *xb, const float *q, float *att, float *key_cache, float *value_cache, int pos,
+                          int head_dim, int n_heads, int n_kv_heads, int seq_len, int kv_dim, uint64_t loff,
+                          int kv_mul);
     // the engine's CPU quantize (MetalQwen3.cpp:308-329) and embedding copy (:228)
     void executeQuantize(int8_t *q, float *s, const float *x, int n);
     void executeEmbedding(float *out, const int8_t *q, const float *s, int token, int dim);
@@ -64,6 +77,8 @@ public:
     void quantizeQ8(const void *x, q3cu_dtype dt, int64_t rows, int n, int8_t *q, float *s, q3cu_stream stream);
     void embedGather(const int8_t *tq, const float *ts, int vocab, int dim, const int32_t *ids, int64_t n,
                      float *out_f32, int8_t *out_q, float *out_s, q3cu_stream stream);
+    void attention(const float *q, const float *key_cache, const float *value_cache, int pos, int n_heads,
+                   int kv_dim, int kv_mul, float *att, int att_stride, float *xb, q3cu_stream stream);
     // synchronises `stream` and throws if a kernel flagged a device-side error
     void checkDeviceStatus(q3cu_stream stream);
 

@@ -166,6 +166,20 @@ q3cu_status q3cu_matmul_q8(q3cu_ctx *ctx, const int8_t *xq, const float *xs, int
                            const int8_t *wq, const float *ws, int n, int d, float *out,
                            q3cu_stream stream);
 
+/* Multi-head attention of one token over positions 0..pos
+ * (qwen3_original.c:395-428; MetalContext::executeAttention,
+ * src/metal/MetalContext.h:86-87, shaders/attention.metal): per query head h,
+ * scores q_h . k_t / sqrtf(128) in index order, the reference's softmax (max
+ * from 0), then xb_h = sum over t in order of att[t] * v_t; kv head h / kv_mul.
+ * Device pointers: q [n_heads][128] (after QK-norm + RoPE); key_cache,
+ * value_cache [pos + 1 or more][kv_dim] (this layer's rows); att
+ * [n_heads][att_stride] receives the probabilities (att_stride > pos); xb
+ * [n_heads][128].  head_dim is 128; kv_dim % 4 == 0.  Same bits as the
+ * reference. */
+q3cu_status q3cu_attention(q3cu_ctx *ctx, const float *q, const float *key_cache, const float *value_cache,
+                           int pos, int n_heads, int kv_dim, int kv_mul, float *att, int att_stride, float *xb,
+                           q3cu_stream stream);
+
 /* ---- a checkpoint on the device and its decode step --------------------- */
 typedef struct q3cu_model q3cu_model;
 
@@ -204,6 +218,15 @@ q3cu_status q3cu_execute_swiglu(q3cu_ctx *ctx, float *hb, const float *hb2, int 
 q3cu_status q3cu_execute_rope(q3cu_ctx *ctx, float *q, float *k, int head_dim, int pos,
                               int n_heads, int n_kv_heads, const float *q_norm_weights,
                               const float *k_norm_weights);
+/* MetalContext::executeAttention (src/metal/MetalContext.h:86-87; called from
+ * MetalQwen3::metal_attention, src/metal/MetalQwen3.cpp:639): one token's
+ * attention over the layer's cache rows 0..pos at key_cache + loff and
+ * value_cache + loff (row stride kv_dim), host pointers.  Writes xb
+ * [n_heads][head_dim] and, as the reference's CPU loop does, the probabilities
+ * into att [n_heads][seq_len] (columns 0..pos).  head_dim must be 128. */
+q3cu_status q3cu_execute_attention(q3cu_ctx *ctx, float *xb, const float *q, float *att, float *key_cache,
+                                   float *value_cache, int pos, int head_dim, int n_heads, int n_kv_heads,
+                                   int seq_len, int kv_dim, uint64_t loff, int kv_mul);
 /* The engine's CPU quantize (src/metal/MetalQwen3.cpp:308-329). */
 q3cu_status q3cu_execute_quantize(q3cu_ctx *ctx, int8_t *q, float *s, const float *x, int n);
 /* MetalContext::executeQuantizedMatMul (src/metal/MetalContext.h:81-82): one

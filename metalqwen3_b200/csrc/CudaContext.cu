@@ -42,6 +42,13 @@ void CudaContext::executeRoPE(float *q, float *k, int head_dim, int pos, int n_h
     check(q3cu_execute_rope(ctx_, q, k, head_dim, pos, n_heads, n_kv_heads, q_norm_weights, k_norm_weights),
           "executeRoPE");
 }
+void CudaContext::executeAttention(float *xb, const float *q, float *att, float *key_cache, float *value_cache,
+                                   int pos, int head_dim, int n_heads, int n_kv_heads, int seq_len, int kv_dim,
+                                   uint64_t loff, int kv_mul) {
+    check(q3cu_execute_attention(ctx_, xb, q, att, key_cache, value_cache, pos, head_dim, n_heads, n_kv_heads, seq_len,
+                                 kv_dim, loff, kv_mul),
+          "executeAttention");
+}
 void CudaContext::executeQuantize(int8_t *q, float *s, const float *x, int n) {
     check(q3cu_execute_quantize(ctx_, q, s, x, n), "executeQuantize");
 }
@@ -86,6 +93,11 @@ void CudaContext::quantizeQ8(const void *x, q3cu_dtype dt, int64_t rows, int n, 
 void CudaContext::embedGather(const int8_t *tq, const float *ts, int vocab, int dim, const int32_t *ids, int64_t n,
                               float *out_f32, int8_t *out_q, float *out_s, q3cu_stream stream) {
     check(q3cu_embed_gather(ctx_, tq, ts, vocab, dim, ids, n, out_f32, out_q, out_s, stream), "embedGather");
+}
+void CudaContext::attention(const float *q, const float *key_cache, const float *value_cache, int pos, int n_heads,
+                            int kv_dim, int kv_mul, float *att, int att_stride, float *xb, q3cu_stream stream) {
+    check(q3cu_attention(ctx_, q, key_cache, value_cache, pos, n_heads, kv_dim, kv_mul, att, att_stride, xb, stream),
+          "attention");
 }
 void CudaContext::checkDeviceStatus(q3cu_stream stream) {
     check(q3cu_device_status(ctx_, stream, nullptr), "checkDeviceStatus");

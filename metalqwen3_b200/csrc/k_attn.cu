@@ -42,10 +42,14 @@ __device__ __forceinline__ void attn_stage(uint8_t *buf, const float *cache, int
     cp_async_commit();
 }
 
+// Outputs: the Q8_0 codes and scales of the head outputs (xq, xs; the decode
+// step), and/or the float head outputs xb [n_heads][128] (executeAttention);
+// either may be NULL.  The position is read from device memory (*pos_p; a
+// captured decode step serves every position) or, with pos_p NULL, is pos_v.
 __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__restrict__ q, const float *kc,
                                                                const float *vc, float *att, int8_t *xq, float *xs,
-                                                               const StepParams *__restrict__ sp, int kv_dim,
-                                                               int kv_mul, int seq_len) {
+                                                               float *xb, const int32_t *__restrict__ pos_p,
+                                                               int pos_v, int kv_dim, int kv_mul, int seq_len) {
     extern __shared__ __align__(16) uint8_t tiles[];        // [2][AT_BUF]
     __shared__ __align__(16) float qs[AT_HD];
     __shared__ ExpTab tab;
@@ -54,7 +58,7 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__re
     __shared__ float gmax[2];
     const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int kvh = h / kv_mul;
-    const int pos = sp->pos;                                // this step's position (device memory)
+    const int pos = pos_p ? *pos_p : pos_v;                 // this step's position
     const int npos = pos + 1, nch = (npos + AT_CH - 1) / AT_CH;
     griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
     qs[tid] = q[int64_t(h) * AT_HD + tid];
@@ -129,6 +133,8 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__re
         for (int t = 0; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(at[t], vt[t * AT_HD]));
         __syncthreads();
     }
+    if (xb) xb[int64_t(h) * AT_HD + tid] = acc;
+    if (!xq) return;                                         // (uniform over the CTA)
     // the quantize that follows (:431): the head's 128 outputs are Q8_0 groups
     // 2h and 2h+1 -- group absmax (strict >, from 0), scale = wmax / 127,
     // code = (int8) round(x / scale), the reference's operations exactly
@@ -445,7 +451,17 @@ cudaError_t launch_attention_step(float *qkv, float *kc, float *vc, float *att, 
     cudaError_t e = launch_qk_norm_rope_step(qkv, kc, vc, n_heads, n_kv, qn, kn, sp, eps, stream);
     if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void *>(attn_decode_kernel), AT_SMEM, 24);
     if (e != cudaSuccess) return e;
-    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(qkv, kc, vc, att, xq, xs, sp, kv_dim, kv_mul, seq_len);
+    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(qkv, kc, vc, att, xq, xs, nullptr, &sp->pos, 0, kv_dim,
+                                                            kv_mul, seq_len);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_attention_rows(const float *q, const float *kc, const float *vc, float *att, float *xb, int pos,
+                                  int n_heads, int kv_dim, int kv_mul, int att_stride, cudaStream_t stream) {
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_decode_kernel), AT_SMEM, 24);
+    if (e != cudaSuccess) return e;
+    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(q, kc, vc, att, nullptr, nullptr, xb, nullptr, pos, kv_dim,
+                                                            kv_mul, att_stride);
     return cudaGetLastError();
 }
 

@@ -434,6 +434,31 @@ q3cu_status q3cu_matmul_q8(q3cu_ctx *ctx, const int8_t *xq, const float *xs, int
                     "matmul_q8 launch");
 }
 
+static q3cu_status check_attention(const float *q, const float *kc, const float *vc, int pos, int n_heads,
+                                   int kv_dim, int kv_mul, const float *att, int att_stride, const float *xb) {
+    if (!q || !kc || !vc || !att || !xb || pos < 0 || n_heads <= 0 || kv_mul <= 0 || att_stride <= pos)
+        return fail(Q3CU_ERR_INVALID, "attention: bad argument (pos=%d n_heads=%d kv_mul=%d att_stride=%d)", pos,
+                    n_heads, kv_mul, att_stride);
+    if (int64_t(kv_dim) < int64_t((n_heads - 1) / kv_mul + 1) * 128)
+        return fail(Q3CU_ERR_INVALID, "attention: kv_dim %d holds fewer than the %d kv heads of 128 used", kv_dim,
+                    (n_heads - 1) / kv_mul + 1);
+    if (kv_dim % 4 || !aligned(kc, 16) || !aligned(vc, 16) || !aligned(q, 4) || !aligned(att, 4) || !aligned(xb, 4))
+        return fail(Q3CU_ERR_ALIGN, "attention: caches 16-byte aligned with kv_dim %% 4 == 0");
+    return Q3CU_OK;
+}
+
+q3cu_status q3cu_attention(q3cu_ctx *ctx, const float *q, const float *key_cache, const float *value_cache, int pos,
+                           int n_heads, int kv_dim, int kv_mul, float *att, int att_stride, float *xb,
+                           q3cu_stream stream) {
+    CHECK_CTX(ctx);
+    if (q3cu_status st = check_attention(q, key_cache, value_cache, pos, n_heads, kv_dim, kv_mul, att, att_stride, xb))
+        return st;
+    if (q3cu_status st = use_device(ctx)) return st;
+    return launched(q3::launch_attention_rows(q, key_cache, value_cache, att, xb, pos, n_heads, kv_dim, kv_mul,
+                                              att_stride, static_cast<cudaStream_t>(stream)),
+                    "attention launch");
+}
+
 // ---------------------------------------------------------------------------
 // host-pointer drop-in wrappers (synchronous)
 // ---------------------------------------------------------------------------
@@ -531,6 +556,42 @@ q3cu_status q3cu_execute_rope(q3cu_ctx *ctx, float *q, float *k, int head_dim, i
                                      ctx->d_status, ctx->stream, ctx->sms), "qk_norm_rope");
     TRY_CUDA(cudaMemcpyAsync(q, dq, size_t(n_heads) * head_dim * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
     TRY_CUDA(cudaMemcpyAsync(k, dk, size_t(n_kv_heads) * head_dim * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
+    return finish(ctx);
+}
+
+q3cu_status q3cu_execute_attention(q3cu_ctx *ctx, float *xb, const float *q, float *att, float *key_cache,
+                                   float *value_cache, int pos, int head_dim, int n_heads, int n_kv_heads,
+                                   int seq_len, int kv_dim, uint64_t loff, int kv_mul) {
+    CHECK_CTX(ctx);
+    if (head_dim != 128) return fail(Q3CU_ERR_INVALID, "executeAttention: head_dim %d, only 128 is supported", head_dim);
+    if (n_kv_heads <= 0 || seq_len <= pos || kv_mul <= 0 || (n_heads - 1) / kv_mul >= n_kv_heads)
+        return fail(Q3CU_ERR_INVALID, "executeAttention: bad argument (pos=%d seq_len=%d n_heads=%d n_kv=%d kv_mul=%d)",
+                    pos, seq_len, n_heads, n_kv_heads, kv_mul);
+    // The layer's rows 0..pos are staged on the device as they lie in the host
+    // cache (row stride kv_dim, padded to a multiple of 4 floats for 16-byte
+    // rows); the probabilities come back into att's columns 0..pos.
+    const int npos = pos + 1, kvp = (kv_dim + 3) & ~3;
+    const size_t qb = up16(size_t(n_heads) * 128 * 4), cb = up16(size_t(npos) * kvp * 4),
+                 ab = up16(size_t(n_heads) * npos * 4);
+    if (!xb || !q || !att || !key_cache || !value_cache || n_heads <= 0 || int64_t(kv_dim) < int64_t(n_kv_heads) * 128)
+        return fail(Q3CU_ERR_INVALID, "executeAttention: bad argument (n_heads=%d kv_dim=%d n_kv=%d)", n_heads, kv_dim,
+                    n_kv_heads);
+    if (q3cu_status st = use_device(ctx)) return st;
+    if (q3cu_status st = grow_scratch(ctx, qb + 2 * cb + ab + qb)) return st;
+    auto *d = static_cast<uint8_t *>(ctx->d_scratch);
+    float *dq = reinterpret_cast<float *>(d), *dk = reinterpret_cast<float *>(d + qb),
+          *dv = reinterpret_cast<float *>(d + qb + cb), *da = reinterpret_cast<float *>(d + qb + 2 * cb),
+          *dx = reinterpret_cast<float *>(d + qb + 2 * cb + ab);
+    TRY_CUDA(cudaMemcpyAsync(dq, q, size_t(n_heads) * 128 * 4, cudaMemcpyHostToDevice, ctx->stream), "H2D");
+    TRY_CUDA(cudaMemcpy2DAsync(dk, size_t(kvp) * 4, key_cache + loff, size_t(kv_dim) * 4, size_t(kv_dim) * 4, npos,
+                               cudaMemcpyHostToDevice, ctx->stream), "H2D");
+    TRY_CUDA(cudaMemcpy2DAsync(dv, size_t(kvp) * 4, value_cache + loff, size_t(kv_dim) * 4, size_t(kv_dim) * 4, npos,
+                               cudaMemcpyHostToDevice, ctx->stream), "H2D");
+    TRY_CUDA(q3::launch_attention_rows(dq, dk, dv, da, dx, pos, n_heads, kvp, kv_mul, npos, ctx->stream),
+             "attention");
+    TRY_CUDA(cudaMemcpyAsync(xb, dx, size_t(n_heads) * 128 * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
+    TRY_CUDA(cudaMemcpy2DAsync(att, size_t(seq_len) * 4, da, size_t(npos) * 4, size_t(npos) * 4, n_heads,
+                               cudaMemcpyDeviceToHost, ctx->stream), "D2H");
     return finish(ctx);
 }
 

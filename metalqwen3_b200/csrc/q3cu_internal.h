@@ -111,6 +111,12 @@ cudaError_t launch_attention_step(float *qkv, float *kc, float *vc, float *att, 
                                   const StepParams *sp, int n_heads, int n_kv, const float *qn, const float *kn,
                                   float eps, int seq_len, cudaStream_t stream, int sms);
 
+// The attention of one token alone (qwen3_original.c:395-428, q already
+// normalised and rotated, K/V rows 0..pos in the caches [..][kv_dim]): the
+// probabilities into att [n_heads][att_stride] (att_stride > pos) and the head
+// outputs into xb [n_heads][128].  One CTA per query head; head_dim 128.
+cudaError_t launch_attention_rows(const float *q, const float *kc, const float *vc, float *att, float *xb, int pos,
+                                  int n_heads, int kv_dim, int kv_mul, int att_stride, cudaStream_t stream);
 
 cudaError_t launch_swiglu(const void *hb, const void *hb2, q3cu_dtype dt, int64_t elems, void *out, int8_t *q,
                           float *s, cudaStream_t stream, int sms);

@@ -44,9 +44,10 @@ def reference_path() -> str:
 
 def build_reference() -> str | None:
     """Compile the reference CPU engine if its sources are reachable."""
-    src = os.path.join(os.environ.get("Q3_REFERENCE", "/root/reference"), "src", "cpu", "qwen3_original.c")
+    root = os.environ.get("Q3_REFERENCE", os.path.join(HERE, "..", "..", "reference"))   # default: beside the repo
+    src = os.path.join(root, "src", "cpu", "qwen3_original.c")
     if os.path.exists(src):
-        subprocess.run(["make", "-s", "-C", HERE, "ref"], check=True)
+        subprocess.run(["make", "-s", "-C", HERE, "ref", f"REFERENCE={os.path.abspath(root)}"], check=True)
     return reference_path() if os.path.exists(reference_path()) else None
 
 
@@ -66,6 +67,7 @@ class Oracle:
             "q3o_qk_norm_rope_head_theta": (None, [vp, vp, i32, i32, f32]),
             "q3o_swiglu": (None, [vp, vp, i32]),
             "q3o_matmul": (None, [vp, vp, vp, vp, vp, i32, i32]),
+            "q3o_attention": (None, [vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, C.c_uint64, i32]),
             "q3o_rows_rmsnorm": (None, [vp, i32, vp, i64, i32, vp, i32]),
             "q3o_rows_rmsnorm_q8": (None, [vp, i32, vp, i64, i32, vp, vp, i32]),
             "q3o_rows_quantize": (None, [vp, i32, i64, i32, vp, vp, i32]),
@@ -127,6 +129,20 @@ class Oracle:
         for b in range(B):
             self.lib.q3o_matmul(_p(out[b]), _p(xq[b]), _p(xs[b]), _p(wq), _p(ws), n, d)
         return out
+
+    def attention(self, q, key_cache, value_cache, pos, n_heads, n_kv_heads, seq_len, loff=0, kv_mul=None):
+        """qwen3_original.c:395-428 (q3o_attention): q [n_heads * 128]; the caches
+        [.., kv_dim] flat; returns (xb [n_heads * hd], att [n_heads][seq_len])."""
+        q = np.ascontiguousarray(q, np.float32).ravel()
+        hd = q.size // n_heads
+        kv_mul = kv_mul or n_heads // n_kv_heads
+        kc = np.ascontiguousarray(key_cache, np.float32).ravel()
+        vc = np.ascontiguousarray(value_cache, np.float32).ravel()
+        xb = np.empty(n_heads * hd, np.float32)
+        att = np.zeros((n_heads, seq_len), np.float32)
+        self.lib.q3o_attention(_p(xb), _p(q), _p(att), _p(kc), _p(vc), int(pos), hd, n_heads, n_kv_heads,
+                               seq_len, n_kv_heads * hd, C.c_uint64(loff), kv_mul)
+        return xb, att
 
     # ---- row-batched forms ------------------------------------------------
     @staticmethod

@@ -121,6 +121,36 @@ void q3o_matmul(float *xout, const int8_t *xq, const float *xs,
     }
 }
 
+/* qwen3_original.c:395-428, the multi-head attention loop of one decode step,
+ * with MetalContext::executeAttention's arguments (src/metal/MetalContext.h:86-87):
+ * per query head h, kv head h / kv_mul, over positions 0..pos of the layer's
+ * cache rows at key_cache + loff / value_cache + loff. */
+void q3o_attention(float *xb, const float *q, float *att, const float *key_cache, const float *value_cache,
+                   int pos, int head_dim, int n_heads, int n_kv_heads, int seq_len, int kv_dim, uint64_t loff,
+                   int kv_mul) {
+    (void)n_kv_heads;
+    for (int h = 0; h < n_heads; h++) {
+        const float *qh = q + h * head_dim;
+        float *a = att + (int64_t)h * seq_len;
+        for (int t = 0; t <= pos; t++) {
+            const float *k = key_cache + loff + (int64_t)t * kv_dim + (h / kv_mul) * head_dim;
+            float score = 0;
+            for (int i = 0; i < head_dim; i++)
+                score += qh[i] * k[i];
+            a[t] = score / sqrtf(head_dim);
+        }
+        q3o_softmax(a, pos + 1);
+        float *xh = xb + h * head_dim;
+        memset(xh, 0, (size_t)head_dim * sizeof(float));
+        for (int t = 0; t <= pos; t++) {
+            const float *v = value_cache + loff + (int64_t)t * kv_dim + (h / kv_mul) * head_dim;
+            float w = a[t];
+            for (int i = 0; i < head_dim; i++)
+                xh[i] += w * v[i];
+        }
+    }
+}
+
 /* ------------------------------------------------------------------------ */
 /* bf16                                                                      */
 /* ------------------------------------------------------------------------ */

@@ -73,6 +73,15 @@ void q3o_swiglu(float *hb, const float *hb2, int n);
 void q3o_matmul(float *xout, const int8_t *xq, const float *xs,
                 const int8_t *wq, const float *ws, int n, int d);
 
+/* qwen3_original.c:395-428: scores q.k / sqrtf(head_dim) over positions
+ * 0..pos, softmax, weighted sum of the values, for every query head (kv head
+ * h / kv_mul); arguments as MetalContext::executeAttention
+ * (src/metal/MetalContext.h:86-87).  att: [n_heads][seq_len] scratch (rows hold
+ * the probabilities afterwards); xb: [n_heads][head_dim]. */
+void q3o_attention(float *xb, const float *q, float *att, const float *key_cache, const float *value_cache,
+                   int pos, int head_dim, int n_heads, int n_kv_heads, int seq_len, int kv_dim, uint64_t loff,
+                   int kv_mul);
+
 /* ---- bf16 helpers (inputs of the bf16 configurations) ------------------- */
 
 /* bf16 -> f32 is exact (a 16-bit shift).  f32 -> bf16 rounds to nearest even,

@@ -75,6 +75,60 @@ def test_cpp_boundary_compiles_and_links(tmp_path):
     assert (tmp_path / "engine").exists()
 
 
+ENGINE_CALL_SITES = r'''
+#include "CudaContext.h"
+#include <memory>
+#include <stdexcept>
+// The calls the reference engine makes on its backend object, with its member
+// and argument names (src/metal/MetalQwen3.cpp: the error handler :56-57 and
+// metal_rmsnorm / metal_softmax / metal_swiglu / metal_rope / metal_attention
+// :479-639), compiled against CudaContext in place of MetalContext.
+struct Engine {
+    std::unique_ptr<CudaContext> metalContext;
+    void on_error() {
+        if (metalContext->isBatching()) {
+            metalContext->endBatch();
+        }
+    }
+    void rmsnorm(float *o, float *x, float *weight, int size) { metalContext->executeRMSNorm(o, x, weight, size); }
+    void softmax(float *x, int size) { metalContext->executeSoftmax(x, size); }
+    void swiglu(float *hb, float *hb2, int hidden_dim) { metalContext->executeSwiGLU(hb, hb2, hidden_dim); }
+    void rope(float *q, float *k, int head_dim, int pos, int n_heads, int n_kv_heads, float *q_norm, float *k_norm) {
+        metalContext->executeRoPE(q, k, head_dim, pos, n_heads, n_kv_heads, q_norm, k_norm);
+    }
+    void attention(float *xb, float *q, float *att, float *key_cache, float *value_cache, int pos, int head_dim,
+                   int n_heads, int n_kv_heads, int seq_len, int kv_dim, uint64_t loff, int kv_mul) {
+        metalContext->executeAttention(xb, q, att, key_cache, value_cache, pos, head_dim, n_heads, n_kv_heads,
+                                       seq_len, kv_dim, loff, kv_mul);
+    }
+    void matmul(float *xout, int8_t *xq, float *xs, int8_t *wq, float *ws, int n, int d) {
+        metalContext->executeQuantizedMatMul(xout, xq, xs, wq, ws, n, d, 64);
+    }
+};
+int main() {
+    Engine e;
+    e.metalContext = std::make_unique<CudaContext>(0);
+    e.metalContext->beginBatch();
+    e.on_error();
+    return e.metalContext->isInitialized() ? 1 : 0;
+}
+'''
+
+
+def test_engine_call_sites_compile(tmp_path):
+    """Every backend call of the reference engine compiles against CudaContext
+    unchanged apart from the type name (the drop-in claim of INTEGRATION.md)."""
+    import subprocess
+    from metalqwen3_b200.build import library_path
+    src = tmp_path / "engine_calls.cpp"
+    src.write_text(ENGINE_CALL_SITES)
+    libdir = os.path.dirname(library_path())
+    subprocess.run(["g++", "-std=c++17", "-O1", "-Wall", "-Werror", "-I", os.path.join(ROOT, "include"), str(src),
+                    "-o", str(tmp_path / "engine_calls"), "-L", libdir, "-lq3cu", f"-Wl,-rpath,{libdir}"], check=True)
+    syms = subprocess.run(["nm", "-D", "-C", library_path()], capture_output=True, text=True).stdout
+    assert "CudaContext::executeAttention" in syms
+
+
 def test_status_strings(lib):
     for s in range(11):
         assert lib.q3cu_status_string(s)

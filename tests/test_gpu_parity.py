@@ -525,6 +525,56 @@ def test_execute_dropin(q3, oracle):
     assert np.array_equal(bits(out), bits(oracle.dequantize(tq[17], ts[17])))
 
 
+@pytest.mark.parametrize("pos,n_heads,n_kv,seq_len,layer", [(0, 16, 8, 64, 0), (37, 16, 8, 64, 1), (700, 32, 8, 1024, 2),
+                                                          (5000, 4, 4, 5001, 0)])
+def test_execute_attention(q3, oracle, pos, n_heads, n_kv, seq_len, layer):
+    """MetalContext::executeAttention (the engine's metal_attention call,
+    MetalQwen3.cpp:639): one token's heads over a layer's cache rows at loff,
+    host pointers; head outputs and the probabilities left in att bit for bit
+    against the reference's loop (qwen3_original.c:395-428).  Also the
+    device-pointer q3cu_attention on the same rows."""
+    import torch
+    rng = np.random.default_rng(pos + n_heads)
+    hd, kv_dim = 128, n_kv * 128
+    kv_mul = n_heads // n_kv
+    layers = layer + 1
+    kc = rng.standard_normal(layers * seq_len * kv_dim).astype(np.float32)
+    vc = rng.standard_normal(layers * seq_len * kv_dim).astype(np.float32)
+    q = (0.3 * rng.standard_normal(n_heads * hd)).astype(np.float32)
+    loff = layer * seq_len * kv_dim
+    xb_o, att_o = oracle.attention(q, kc, vc, pos, n_heads, n_kv, seq_len, loff=loff)
+    xb = np.full(n_heads * hd, np.nan, np.float32)
+    att = np.full(n_heads * seq_len, -7.0, np.float32)
+    q3.execute_attention(xb, q, att, kc, vc, pos, hd, n_heads, n_kv, seq_len, kv_dim, loff, kv_mul)
+    assert np.array_equal(bits(xb), bits(xb_o))
+    att = att.reshape(n_heads, seq_len)
+    assert np.array_equal(bits(att[:, :pos + 1]), bits(att_o[:, :pos + 1]))
+    assert (att[:, pos + 1:] == -7.0).all()                         # columns past pos untouched
+    rows = slice(loff, loff + (pos + 1) * kv_dim)
+    xg, ag = q3.attention(dev(q), dev(kc[rows].reshape(pos + 1, kv_dim)), dev(vc[rows].reshape(pos + 1, kv_dim)),
+                          pos, kv_mul)
+    torch.cuda.synchronize()
+    assert np.array_equal(bits(host(xg).ravel()), bits(xb_o))
+    assert np.array_equal(bits(host(ag)), bits(att_o[:, :pos + 1]))
+
+
+def test_attention_rejects_bad_arguments(q3):
+    import torch
+    from metalqwen3_b200.q3cu import Q3Error
+    q = torch.zeros(4 * 128, device="cuda")
+    kc = torch.zeros(10, 256, device="cuda")
+    with pytest.raises(Q3Error) as e:                                 # att narrower than pos + 1
+        q3.attention(q, kc, kc, 9, 2, att=torch.zeros(4, 9, device="cuda"))
+    assert e.value.status == 1
+    with pytest.raises(Q3Error) as e:                                 # 4 heads / kv_mul 1 need 4 kv heads of 128
+        q3.attention(q, kc, kc, 3, 1)
+    assert e.value.status == 1
+    with pytest.raises(Q3Error) as e:
+        q3.execute_attention(np.zeros(512, np.float32), np.zeros(512, np.float32), np.zeros(40, np.float32),
+                             np.zeros(2560, np.float32), np.zeros(2560, np.float32), 3, 64, 4, 2, 10, 256, 0, 2)
+    assert e.value.status == 1                                         # head_dim 64
+
+
 # --------------------------------------------------------------------------- Q8_0 matmul
 def same_bits(a, b):
     a, b = np.asarray(a, np.float32), np.asarray(b, np.float32)

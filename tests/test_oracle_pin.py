@@ -128,6 +128,12 @@ def test_forward_vs_reference(oracle, reference, shape):
                 assert np.array_equal(u32(st["x"]), u32(taps[(L, "final_rms_out")]))
                 for layer in range(L):
                     assert np.array_equal(u32(st["key_cache"][layer, pos]), u32(taps[(layer, "k_post")]))
+                # the attention loop alone (q3o_attention, executeAttention's arguments) on the
+                # reference's own last-layer q and caches: its probabilities and head outputs
+                xb, att = oracle.attention(st["q"], st["key_cache"][L - 1], st["value_cache"][L - 1], pos,
+                                           shape["n_heads"], shape["n_kv"], shape["seq_len"])
+                assert np.array_equal(u32(att[:, :pos + 1]), u32(st["att"]))
+                assert np.array_equal(u32(xb), u32(taps[(L - 1, "att_out")]))
         finally:
             reference.free(t)
             om.close()
