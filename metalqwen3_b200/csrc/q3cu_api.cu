@@ -355,7 +355,7 @@ static q3cu_status swiglu_common(q3cu_ctx *ctx, const void *hb, const void *hb2,
 q3cu_status q3cu_swiglu(q3cu_ctx *ctx, void *hb, const void *hb2, q3cu_dtype dtype, int64_t rows, int hidden,
                         q3cu_stream stream) {
     if (q3cu_status st = swiglu_common(ctx, hb, hb2, dtype, rows, hidden, false, nullptr, nullptr)) return st;
-    return launched(q3::launch_swiglu(hb, hb2, dtype, rows * int64_t(hidden), hb, nullptr, nullptr,
+    return launched(q3::launch_swiglu(hb, hb2, dtype, rows * int64_t(hidden), hb, nullptr, nullptr, ctx->d_status,
                                       static_cast<cudaStream_t>(stream), ctx->sms),
                     "swiglu launch");
 }
@@ -363,7 +363,7 @@ q3cu_status q3cu_swiglu(q3cu_ctx *ctx, void *hb, const void *hb2, q3cu_dtype dty
 q3cu_status q3cu_swiglu_q8(q3cu_ctx *ctx, const void *hb, const void *hb2, q3cu_dtype dtype, int64_t rows, int hidden,
                            int8_t *q, float *s, q3cu_stream stream) {
     if (q3cu_status st = swiglu_common(ctx, hb, hb2, dtype, rows, hidden, true, q, s)) return st;
-    return launched(q3::launch_swiglu(hb, hb2, dtype, rows * int64_t(hidden), nullptr, q, s,
+    return launched(q3::launch_swiglu(hb, hb2, dtype, rows * int64_t(hidden), nullptr, q, s, ctx->d_status,
                                       static_cast<cudaStream_t>(stream), ctx->sms),
                     "swiglu_q8 launch");
 }
@@ -526,7 +526,8 @@ q3cu_status q3cu_execute_swiglu(q3cu_ctx *ctx, float *hb, const float *hb2, int 
     if (padded != hidden_dim) TRY_CUDA(cudaMemsetAsync(d, 0, 2 * rb, ctx->stream), "memset");
     TRY_CUDA(cudaMemcpyAsync(da, hb, size_t(hidden_dim) * 4, cudaMemcpyHostToDevice, ctx->stream), "H2D");
     TRY_CUDA(cudaMemcpyAsync(db, hb2, size_t(hidden_dim) * 4, cudaMemcpyHostToDevice, ctx->stream), "H2D");
-    TRY_CUDA(q3::launch_swiglu(da, db, Q3CU_F32, padded, da, nullptr, nullptr, ctx->stream, ctx->sms), "swiglu");
+    TRY_CUDA(q3::launch_swiglu(da, db, Q3CU_F32, padded, da, nullptr, nullptr, ctx->d_status, ctx->stream, ctx->sms),
+             "swiglu");
     TRY_CUDA(cudaMemcpyAsync(hb, da, size_t(hidden_dim) * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
     return finish(ctx);
 }

@@ -546,6 +546,20 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, uint32
     return false;
 }
 
+// The same bounded wait for warps that expect a long wait (microseconds) and
+// share their SM with a latency-bound warp: between polls the warp sleeps
+// (nanosleep), so it takes no issue slots from the warps that do the work.
+__device__ __forceinline__ bool mbar_wait_idle(uint64_t *bar, uint32_t parity, uint32_t *status) {
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0; i < WAIT_POLLS; ++i) {
+        if (mbar_test_wait(bar, parity)) return true;
+        __nanosleep(200);
+        if ((i & 15u) == 15u && global_ns() - t0 > WAIT_NS) break;
+    }
+    if (status) atomicOr(status, Q3CU_DEV_TIMEOUT);
+    return false;
+}
+
 // ---------------------------------------------------------------------------
 // reductions
 // ---------------------------------------------------------------------------

@@ -119,7 +119,7 @@ cudaError_t launch_attention_rows(const float *q, const float *kc, const float *
                                   int n_heads, int kv_dim, int kv_mul, int att_stride, cudaStream_t stream);
 
 cudaError_t launch_swiglu(const void *hb, const void *hb2, q3cu_dtype dt, int64_t elems, void *out, int8_t *q,
-                          float *s, cudaStream_t stream, int sms);
+                          float *s, uint32_t *status, cudaStream_t stream, int sms);
 
 // `sched` is a pair of device counters, zero before the launch and zero
 // again after it (the last CTA resets them); no two launches that may run at

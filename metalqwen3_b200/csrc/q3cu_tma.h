@@ -1,0 +1,47 @@
+// q3cu_tma.h -- tensor maps (TMA descriptors) for the kernels that stage rows
+// through shared memory with cp.async.bulk.tensor, and the device-side copy.
+//
+// Host: the driver's cuTensorMapEncodeTiled is looked up once through the
+// runtime (cudaGetDriverEntryPoint), so the library does not link libcuda.
+// Device: one tiled 3-D load per call, completing on an mbarrier; no multicast
+// (the maps only ever describe this GPU's own memory).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace q3 {
+
+// A row-major [rows][row_bytes] byte array viewed as 3-D for TMA: dim 0 = the
+// 128 bytes of one line, dim 1 = the line within a row (stride 128 B), dim 2 =
+// the row (stride row_bytes).  Box = {128, L, R}: L consecutive lines of R
+// consecutive rows, landing in shared memory as [R][L][128 B] with the 128-byte
+// swizzle (16-byte chunk c of smem line i is stored at chunk c ^ (i % 8); the
+// destination must be 1024-byte aligned).  Out-of-range lines and rows are
+// filled with zeros.  Requires base 16-byte aligned and row_bytes % 128 == 0.
+// Returns false (and leaves *map undefined) if the driver rejects it.
+// The map depends only on the arguments, so the last few are kept per host
+// thread and reused (encode_row_lines_map_uncached always encodes).
+bool encode_row_lines_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t row_bytes, uint32_t L,
+                          uint32_t R);
+bool encode_row_lines_map_uncached(CUtensorMap *map, const void *base, uint64_t rows, uint64_t row_bytes,
+                                   uint32_t L, uint32_t R);
+
+#if defined(__CUDACC__)
+// Tiled 3-D tensor load of the box at (x, y, z) into shared memory at dst,
+// completing on `bar` (the caller has armed it with the box's bytes).  x is
+// the byte offset within the line and is always 0 here (16-byte aligned).
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, int x, int y, int z, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];"
+        :: "r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(reinterpret_cast<uint64_t>(map)), "r"(x),
+           "r"(y), "r"(z), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+        : "memory");
+}
+__device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
+    asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+#endif
+
+}  // namespace q3

@@ -136,6 +136,32 @@ def test_rmsnorm_q8_f32(q3, oracle, rows, dim):
     assert_q8_equal(qg, sg, qo, so)
 
 
+@pytest.mark.parametrize("rows,dim,bf16", [
+    (8192, 2560, False),      # TMA-fed kernel: blocks of 56 rows, two chain warps
+    (20011, 1024, False),     # TMA-fed: 2-3 blocks per SM (double-buffered row scales), a 1-row last block
+    (1000, 2560, False),      # persistent ring kernel: 7 rows per SM
+    (5000, 4096, True),       # TMA-fed, bf16, blocks of 34 rows
+    (16384, 5120, True),      # TMA-fed, the Qwen3-14B prefill rows: 2 blocks of 56 per SM
+])
+def test_rmsnorm_many_rows(q3, oracle, rows, dim, bf16):
+    """The prefill kernels (more rows than 4 per SM): codes, scales and floats
+    bit for bit, also in place."""
+    rng = np.random.default_rng(rows + dim)
+    x = activations(rng, rows, dim)
+    if bf16:
+        x = to_bf16(x, oracle)
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    qg, sg = q3.rmsnorm_q8(dev(x), dev(w))
+    qo, so = oracle.rows_rmsnorm_q8(x, w, threads=8)
+    assert_q8_equal(qg, sg, qo, so)
+    o = oracle.rows_rmsnorm(x, w, threads=8)
+    t = dev(x)
+    assert np.array_equal(host(q3.rmsnorm(t, dev(w))), o)
+    q3.rmsnorm(t, dev(w), out=t)                                     # in place
+    assert np.array_equal(host(t), o)
+    assert q3.device_status() == 0
+
+
 @pytest.mark.parametrize("rows,dim", [(3, 512), (256, 4096), (2048, 5120)])
 def test_rmsnorm_bf16(q3, oracle, rows, dim):
     rng = np.random.default_rng(dim)
@@ -248,6 +274,47 @@ def test_swiglu_expf_sweep(q3, oracle):
     g, o = host(t), oracle.rows_swiglu(hb, hb2, threads=8)
     same = (bits(g) == bits(o)) | (np.isnan(g) & np.isnan(o))
     assert same.all(), f"{int((~same).sum())} mismatches"
+
+
+@pytest.mark.parametrize("rows,hidden,bf16", [
+    (2000, 1024, False),      # 2,048,000 elements: the last chunk of the streaming kernel is partial
+    (512, 17408, True),       # the Qwen3-14B FFN rows, bf16
+    (4096, 9728, True),
+])
+def test_swiglu_streaming(q3, oracle, rows, hidden, bf16):
+    """The streaming (per-warp bulk-copy ring) kernel: Q8_0 codes/scales and the
+    float output, in place, bit for bit."""
+    rng = np.random.default_rng(rows + hidden)
+    hb, hb2 = activations(rng, rows, hidden), activations(rng, rows, hidden)
+    if bf16:
+        hb, hb2 = to_bf16(hb, oracle), to_bf16(hb2, oracle)
+    qg, sg = q3.swiglu_q8(dev(hb), dev(hb2))
+    qo, so = oracle.rows_swiglu_q8(hb, hb2, threads=8)
+    assert_q8_equal(qg, sg, qo, so)
+    t = dev(hb)
+    q3.swiglu(t, dev(hb2))
+    g, o = host(t), oracle.rows_swiglu(hb, hb2, threads=8)
+    assert np.array_equal(bits(g) if not bf16 else g, bits(o) if not bf16 else o)
+    assert q3.device_status() == 0
+
+
+def test_swiglu_bf16_every_input(q3, oracle):
+    """Every one of the 65,536 bf16 bit patterns as hb (zeros, subnormals, the
+    gate table's window and beyond, +-inf, NaN), 64 copies against random hb2,
+    through the streaming kernel: the float output bit for bit (NaN where the
+    reference gives NaN), and the Q8_0 codes of the finite part."""
+    rng = np.random.default_rng(17)
+    hb = np.tile(np.arange(65536, dtype=np.uint32).astype(np.uint16), 64).reshape(-1, 4096)
+    hb2 = to_bf16(rng.standard_normal(hb.shape, dtype=np.float32), oracle)
+    t = dev(hb)
+    q3.swiglu(t, dev(hb2))
+    g, o = bf16_to_f32(host(t)), bf16_to_f32(oracle.rows_swiglu(hb, hb2, threads=8))
+    same = (g.view(np.uint32) == o.view(np.uint32)) | (np.isnan(g) & np.isnan(o))
+    assert same.all(), f"{int((~same).sum())} mismatches"
+    fin = np.isfinite(bf16_to_f32(hb)).all(axis=1)
+    qg, sg = q3.swiglu_q8(dev(hb[fin]), dev(hb2[fin]))
+    qo, so = oracle.rows_swiglu_q8(hb[fin], hb2[fin], threads=8)
+    assert_q8_equal(qg, sg, qo, so)
 
 
 @pytest.mark.parametrize("rows,hidden", [(3, 512), (256, 12288)])
