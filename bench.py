@@ -485,7 +485,7 @@ class Embed(Workload):
 
     def make(self, torch, dev, seed):
         g = torch.Generator(device=dev)
-        g.manual_seed(seed)
+        g.manual_seed(1234)                            # the same (replicated) table on every rank
         V, D, N = self.vocab, self.dim, self.tokens
         d = {
             "tq": torch.randint(-127, 128, (V, D), device=dev, dtype=torch.int8, generator=g),
@@ -1320,10 +1320,26 @@ def main():
                     help="time each kernel of the workload on the reference's CPU code (1 core and all cores) and exit")
     ap.add_argument("--h2d-probe", action="store_true",
                     help="measure pinned host<->device copy bandwidth on every rank at once and exit")
-    args = ap.parse_args()
+    ap.set_defaults(workload_list=None)
+    argv = sys.argv[1:]
+    wi = argv.index("--workload") if "--workload" in argv else -1
+    names = argv[wi + 1].split(",") if wi >= 0 else ["prefill4b"]
+    if wi >= 0:
+        argv = argv[:wi + 1] + [names[0]] + argv[wi + 2:]
+    args = ap.parse_args(argv)
     args.warmup = max(args.warmup, 3)
     if args.h2d_probe:
         return h2d_probe(args)
+    rc = 0
+    for name in names:                   # several workloads in one launch: one JSON line each
+        if name not in WORKLOADS:
+            raise SystemExit(f"unknown workload {name}")
+        args.workload = name
+        rc = rc or run_one(args)
+    return rc
+
+
+def run_one(args):
     cls = WORKLOADS[args.workload]
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
     rank_env = int(os.environ.get("RANK", "0"))

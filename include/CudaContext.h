@@ -78,7 +78,7 @@ public:
     void embedGather(const int8_t *tq, const float *ts, int vocab, int dim, const int32_t *ids, int64_t n,
                      float *out_f32, int8_t *out_q, float *out_s, q3cu_stream stream);
     void attention(const float *q, const float *key_cache, const float *value_cache, int pos, int n_heads,
-                   int kv_dim, int kv_mul, float *att, int att_stride, float *xb, q3cu_stream stream);
+                   int kv_dim, int kv_mul, float *att, int att_stride, float *probs, float *xb, q3cu_stream stream);
     // synchronises `stream` and throws if a kernel flagged a device-side error
     void checkDeviceStatus(q3cu_stream stream);
 

@@ -173,12 +173,13 @@ q3cu_status q3cu_matmul_q8(q3cu_ctx *ctx, const int8_t *xq, const float *xs, int
  * from 0), then xb_h = sum over t in order of att[t] * v_t; kv head h / kv_mul.
  * Device pointers: q [n_heads][128] (after QK-norm + RoPE); key_cache,
  * value_cache [pos + 1 or more][kv_dim] (this layer's rows); att
- * [n_heads][att_stride] receives the probabilities (att_stride > pos); xb
- * [n_heads][128].  head_dim is 128; kv_dim % 4 == 0.  Same bits as the
- * reference. */
+ * [n_heads][att_stride] is scratch for the scores (att_stride > pos); probs
+ * (NULL, or a different buffer of the same shape) receives the probabilities,
+ * the reference's att after its softmax; xb [n_heads][128].  head_dim is 128;
+ * kv_dim % 4 == 0.  Any number of positions.  Same bits as the reference. */
 q3cu_status q3cu_attention(q3cu_ctx *ctx, const float *q, const float *key_cache, const float *value_cache,
-                           int pos, int n_heads, int kv_dim, int kv_mul, float *att, int att_stride, float *xb,
-                           q3cu_stream stream);
+                           int pos, int n_heads, int kv_dim, int kv_mul, float *att, int att_stride, float *probs,
+                           float *xb, q3cu_stream stream);
 
 /* ---- a checkpoint on the device and its decode step --------------------- */
 typedef struct q3cu_model q3cu_model;

@@ -95,8 +95,10 @@ void CudaContext::embedGather(const int8_t *tq, const float *ts, int vocab, int 
     check(q3cu_embed_gather(ctx_, tq, ts, vocab, dim, ids, n, out_f32, out_q, out_s, stream), "embedGather");
 }
 void CudaContext::attention(const float *q, const float *key_cache, const float *value_cache, int pos, int n_heads,
-                            int kv_dim, int kv_mul, float *att, int att_stride, float *xb, q3cu_stream stream) {
-    check(q3cu_attention(ctx_, q, key_cache, value_cache, pos, n_heads, kv_dim, kv_mul, att, att_stride, xb, stream),
+                            int kv_dim, int kv_mul, float *att, int att_stride, float *probs, float *xb,
+                            q3cu_stream stream) {
+    check(q3cu_attention(ctx_, q, key_cache, value_cache, pos, n_heads, kv_dim, kv_mul, att, att_stride, probs, xb,
+                         stream),
           "attention");
 }
 void CudaContext::checkDeviceStatus(q3cu_stream stream) {

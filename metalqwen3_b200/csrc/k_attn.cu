@@ -16,11 +16,10 @@
 // probabilities live in the caller's att buffer ([n_heads][seq_len], like the
 // reference's RunState att), so any position up to seq_len is supported.
 //
-// One CTA per query head, 128 threads (one per element of the head).  K and V
-// reach shared memory in chunks of 128 positions by cp.async, double-buffered
-// (64 KB per chunk in flight, the next chunk loading while this one is used);
-// K rows are padded to 528 B so a thread per position reads its row without
-// bank conflicts.  The position-order probability sum is the serial part.
+// Two launches that spread over the GPU (below).  K and V reach shared memory
+// in chunks of 128 positions by cp.async; K rows are padded to 528 B so a
+// thread per position reads its row without bank conflicts.  The
+// position-order probability sum is the serial part.
 #include "q3cu_internal.h"
 
 namespace q3 {
@@ -29,7 +28,6 @@ constexpr int AT_HD = 128;
 constexpr int AT_CH = 128;                                  // positions per staged chunk
 constexpr int AT_KROW = AT_HD * 4 + 16;                     // padded K row: 33 x 16 B, conflict-free float4 reads
 constexpr size_t AT_BUF = size_t(AT_CH) * AT_KROW;          // 67,584 B per chunk buffer
-constexpr size_t AT_SMEM = 2 * AT_BUF;                      // double-buffered
 
 // Copies rows c0 .. c0+n-1 of a cache (this kv head's 128 floats of each) into
 // buf with 16-byte cp.async pieces, `rowb` bytes apart; one commit group.
@@ -42,115 +40,9 @@ __device__ __forceinline__ void attn_stage(uint8_t *buf, const float *cache, int
     cp_async_commit();
 }
 
-// Outputs: the Q8_0 codes and scales of the head outputs (xq, xs; the decode
-// step), and/or the float head outputs xb [n_heads][128] (executeAttention);
-// either may be NULL.  The position is read from device memory (*pos_p; a
-// captured decode step serves every position) or, with pos_p NULL, is pos_v.
-__global__ void __launch_bounds__(AT_HD, 1) attn_decode_kernel(const float *__restrict__ q, const float *kc,
-                                                               const float *vc, float *att, int8_t *xq, float *xs,
-                                                               float *xb, const int32_t *__restrict__ pos_p,
-                                                               int pos_v, int kv_dim, int kv_mul, int seq_len) {
-    extern __shared__ __align__(16) uint8_t tiles[];        // [2][AT_BUF]
-    __shared__ __align__(16) float qs[AT_HD];
-    __shared__ ExpTab tab;
-    __shared__ float red[AT_HD / 32];
-    __shared__ float sum_sh;
-    __shared__ float gmax[2];
-    const int h = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int kvh = h / kv_mul;
-    const int pos = pos_p ? *pos_p : pos_v;                 // this step's position
-    const int npos = pos + 1, nch = (npos + AT_CH - 1) / AT_CH;
-    griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
-    qs[tid] = q[int64_t(h) * AT_HD + tid];
-    load_exp_table(tab);
-    float *a = att + int64_t(h) * seq_len;
-    const float scale = __fsqrt_rn(float(AT_HD));            // sqrtf((float) head_dim)
-
-    // scores, chunk by chunk (the next chunk's K rows in flight): thread t
-    // runs position c0 + t's dot product in index order from shared memory
-    float m = 0.0f;                                         // softmax's max starts at 0
-    attn_stage(tiles, kc, 0, npos < AT_CH ? npos : AT_CH, kv_dim, kvh, AT_KROW, tid);
-    for (int c = 0; c < nch; ++c) {
-        const int c0 = c * AT_CH, n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
-        if (c + 1 < nch) {
-            const int n1 = npos - c0 - AT_CH < AT_CH ? npos - c0 - AT_CH : AT_CH;
-            attn_stage(tiles + ((c + 1) & 1) * AT_BUF, kc, c0 + AT_CH, n1, kv_dim, kvh, AT_KROW, tid);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();                                     // chunk c landed (every thread's pieces)
-        if (tid < n) {
-            const float4 *kr = reinterpret_cast<const float4 *>(tiles + (c & 1) * AT_BUF + tid * AT_KROW);
-            float s = 0.0f;
-#pragma unroll 8
-            for (int i4 = 0; i4 < AT_HD / 4; ++i4) {
-                const float4 kv = kr[i4];
-                s = __fadd_rn(s, __fmul_rn(qs[4 * i4], kv.x));
-                s = __fadd_rn(s, __fmul_rn(qs[4 * i4 + 1], kv.y));
-                s = __fadd_rn(s, __fmul_rn(qs[4 * i4 + 2], kv.z));
-                s = __fadd_rn(s, __fmul_rn(qs[4 * i4 + 3], kv.w));
-            }
-            const float sc = __fdiv_rn(s, scale);
-            a[c0 + tid] = sc;
-            m = fmaxf(m, sc);                                // a NaN never replaces the max
-        }
-        __syncthreads();                                     // before the buffer is refilled
-    }
-    // the first V chunk streams in while the softmax runs
-    attn_stage(tiles, vc, 0, npos < AT_CH ? npos : AT_CH, kv_dim, kvh, AT_HD * 4, tid);
-    m = warp_max(m);
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    m = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    // exp (the host libm's bits), then the sum in position order
-    for (int t = tid; t < npos; t += AT_HD) a[t] = expf_host(__fsub_rn(a[t], m), tab);
-    __syncthreads();
-    if (tid == 0) {
-        float sum = 0.0f;
-        for (int t = 0; t < npos; ++t) sum = __fadd_rn(sum, a[t]);
-        sum_sh = sum;
-    }
-    __syncthreads();
-    const float sum = sum_sh;
-    for (int t = tid; t < npos; t += AT_HD) a[t] = __fdiv_rn(a[t], sum);
-    __syncthreads();
-    // weighted values: thread i runs element i's chain over the positions in order
-    float acc = 0.0f;
-    for (int c = 0; c < nch; ++c) {
-        const int c0 = c * AT_CH, n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
-        if (c + 1 < nch) {
-            const int n1 = npos - c0 - AT_CH < AT_CH ? npos - c0 - AT_CH : AT_CH;
-            attn_stage(tiles + ((c + 1) & 1) * AT_BUF, vc, c0 + AT_CH, n1, kv_dim, kvh, AT_HD * 4, tid);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-        }
-        __syncthreads();
-        const float *vt = reinterpret_cast<const float *>(tiles + (c & 1) * AT_BUF) + tid;
-        const float *at = a + c0;
-#pragma unroll 8
-        for (int t = 0; t < n; ++t) acc = __fadd_rn(acc, __fmul_rn(at[t], vt[t * AT_HD]));
-        __syncthreads();
-    }
-    if (xb) xb[int64_t(h) * AT_HD + tid] = acc;
-    if (!xq) return;                                         // (uniform over the CTA)
-    // the quantize that follows (:431): the head's 128 outputs are Q8_0 groups
-    // 2h and 2h+1 -- group absmax (strict >, from 0), scale = wmax / 127,
-    // code = (int8) round(x / scale), the reference's operations exactly
-    float gm = warp_max(fmaxf(0.0f, fabsf(acc)));           // from 0; a NaN never wins
-    if (lane == 0) red[warp] = gm;
-    __syncthreads();
-    if (tid < 2) gmax[tid] = fmaxf(red[2 * tid], red[2 * tid + 1]);
-    __syncthreads();
-    const float qscale = q8_scale(gmax[tid >> 6]);
-    xq[int64_t(h) * AT_HD + tid] = int8_t(q8_code(acc, qscale));
-    if ((tid & 63) == 0) xs[int64_t(h) * 2 + (tid >> 6)] = qscale;
-}
-
-// The same attention in two launches that spread over the GPU (the fused
-// kernel above runs on only n_heads SMs and streams 512 B per cached position
-// through each):
+// The attention in two launches that spread over the GPU (one CTA per head
+// would run on only n_heads SMs and stream 512 B per cached position through
+// each):
 //   attn_scores_kernel: a CTA per (head, chunk of 128 positions) work item,
 //     grid-stride over the items of this position -- the chunk's K rows staged
 //     by cp.async (padded, as above), a thread per position runs its score
@@ -205,16 +97,20 @@ __device__ __forceinline__ void norm_rope_row(const float *v, const float *__res
     __syncwarp();                                            // out written, scratch free
 }
 
-// Scores with the step's QK-norm + RoPE folded in: qkv holds this token's raw
-// [q | k | v] rows.  Each work item normalizes and rotates its head's q into
-// shared memory (warp 0).  The item holding position pos also rotates the kv
-// head's k straight into its tile row (warp 1) and, once per kv head (the
-// first of its query heads), writes that k row and the v row into the caches
-// for the values kernel and later steps (warps 1 and 2).
+// Scores with the step's QK-norm + RoPE folded in (ROT): qkv holds this
+// token's raw [q | k | v] rows.  Each work item normalizes and rotates its
+// head's q into shared memory (warp 0).  The item holding position pos also
+// rotates the kv head's k straight into its tile row (warp 1) and, once per kv
+// head (the first of its query heads), writes that k row and the v row into the
+// caches for the values kernel and later steps (warps 1 and 2).  Without ROT,
+// qkv is the already rotated q [n_heads][128] and the caches already hold row
+// pos (MetalContext::executeAttention's inputs).  The position is *pos_p (the
+// step's parameters) or, with pos_p NULL, pos_v.
+template <bool ROT>
 __global__ void __launch_bounds__(AT_HD) attn_scores_kernel(const float *qkv, float *kc, float *vc, float *att,
                                                             const float *__restrict__ qn,
                                                             const float *__restrict__ kn,
-                                                            const StepParams *__restrict__ sp, float eps,
+                                                            const StepParams *__restrict__ sp, int pos_v, float eps,
                                                             int n_heads, int kv_dim, int kv_mul, int seq_len) {
     extern __shared__ __align__(16) uint8_t tile[];          // [AT_CH][AT_KROW]
     __shared__ __align__(16) float qs[AT_HD];
@@ -222,15 +118,18 @@ __global__ void __launch_bounds__(AT_HD) attn_scores_kernel(const float *qkv, fl
     griddep_launch_dependents();
     griddep_wait();                                          // qkv from the matmul before
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int pos = sp->pos, npos = pos + 1, items = (npos + AT_CH - 1) / AT_CH * n_heads;
+    const int pos = sp ? sp->pos : pos_v, npos = pos + 1, items = (npos + AT_CH - 1) / AT_CH * n_heads;
     const int qdim = n_heads * AT_HD;
     for (int w = blockIdx.x; w < items; w += gridDim.x) {
         const int h = w % n_heads, c0 = (w / n_heads) * AT_CH, kvh = h / kv_mul;
         const int n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
-        const bool last = c0 + n == npos;                    // this chunk holds position pos
+        const bool last = ROT && c0 + n == npos;             // this chunk holds position pos (rotated here)
         __syncthreads();                                     // the previous item's reads of tile / qs are done
-        attn_stage(tile, kc, c0, last ? n - 1 : n, kv_dim, kvh, AT_KROW, tid);   // cached rows below pos
-        if (warp == 0) {
+        attn_stage(tile, kc, c0, last ? n - 1 : n, kv_dim, kvh, AT_KROW, tid);   // cached rows (below pos)
+        if (!ROT) {
+            if (warp == 0)
+                reinterpret_cast<float4 *>(qs)[lane] = reinterpret_cast<const float4 *>(qkv + int64_t(h) * AT_HD)[lane];
+        } else if (warp == 0) {
             norm_rope_row(qkv + int64_t(h) * AT_HD, qn, sp, eps, scr[0][0], scr[0][1], qs, lane);
         } else if (warp == 1 && last) {
             float *kr = reinterpret_cast<float *>(tile + (n - 1) * AT_KROW);
@@ -316,10 +215,25 @@ __device__ __forceinline__ void attn_stage_half(uint8_t *buf, const float *vc, i
     cp_async_commit();
 }
 
-__global__ void __launch_bounds__(AT_HD, 1) attn_values_kernel(const float *att, const float *vc, int8_t *xq,
-                                                               float *xs, const StepParams *__restrict__ sp,
-                                                               int kv_dim, int kv_mul, int seq_len) {
-    extern __shared__ __align__(16) uint8_t dyn[];          // [AV_NST][AV_BUF] V ring, then [seq_len] probabilities
+// Above AV_MAXPOS positions the probabilities do not fit next to the V ring:
+// the kernel then keeps none of them.  It takes the row max from the scores in
+// global memory, adds the exponentials in position order chunk by chunk (each
+// chunk's exponentials computed in parallel into a buffer, then summed by one
+// thread), and recomputes each V chunk's probabilities, with the same
+// operations and therefore the same bits, just before that chunk's value
+// chains.  Any context length; one more exponential per position.
+constexpr int AV_ECH = 4096;                                 // exponentials per sum chunk (long mode)
+
+// Outputs: Q8_0 codes/scales of the head (xq, xs; the decode step) and/or the
+// float head outputs xb [n_heads][128] and the probabilities into probs (the
+// first half's CTA only; executeAttention).  probs must not be att: the other
+// half's CTA may still be reading the scores.  Position from *sp or, with sp
+// NULL, pos_v.
+__global__ void __launch_bounds__(AT_HD, 1) attn_values_kernel(float *att, const float *vc, int8_t *xq, float *xs,
+                                                               float *xb, float *probs,
+                                                               const StepParams *__restrict__ sp, int pos_v,
+                                                               int kv_dim, int kv_mul, int seq_len, int res_cap) {
+    extern __shared__ __align__(16) uint8_t dyn[];          // [AV_NST][AV_BUF] V ring, then the probabilities
     float *pr = reinterpret_cast<float *>(dyn + AV_NST * AV_BUF);
     __shared__ ExpTab tab;
     __shared__ float red[AT_HD / 32];
@@ -334,7 +248,11 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_values_kernel(const float *att,
     const int pt = tid - AV_COLS;
     load_exp_table(tab);
     griddep_wait();                                          // att (and the caches, written two kernels back)
-    const int npos = sp->pos + 1, nch = (npos + AT_CH - 1) / AT_CH;
+    const int npos = (sp ? sp->pos : pos_v) + 1, nch = (npos + AT_CH - 1) / AT_CH;
+    // every probability kept in shared memory, if the launch's allocation holds them (res_cap floats)
+    const bool resident = npos <= res_cap;
+    float *a = att + int64_t(h) * seq_len;
+    float *ech = pr + AT_CH;                                 // long mode: pr = one chunk, ech = AV_ECH exponentials
     auto stage = [&](int c) {                                // chunk c into slot c % AV_NST, or an empty group
         if (c < nch) {
             const int c0 = c * AT_CH;
@@ -344,40 +262,63 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_values_kernel(const float *att,
             cp_async_commit();
         }
     };
+    float m = 0.0f;
     if (producer) {                                          // the first chunks stream in during the softmax
         for (int c = 0; c < AV_NST - 1; ++c) stage(c);
     } else {                                                 // the softmax by the chain warps (named barrier 1)
-        const float *a = att + int64_t(h) * seq_len;
-        float m = 0.0f;                                       // softmax's max starts at 0
-        for (int t = tid; t < npos; t += AV_COLS) m = fmaxf(m, a[t]);   // a NaN never replaces the max
+        for (int t = tid; t < npos; t += AV_COLS) m = fmaxf(m, a[t]);   // max from 0; a NaN never replaces it
         m = warp_max(m);
         if (lane == 0) red[warp] = m;
         named_sync(1, AV_COLS);                               // (also: the exp table is loaded)
         m = fmaxf(red[0], red[1]);
-        for (int t = tid; t < npos; t += AV_COLS) pr[t] = expf_host(__fsub_rn(a[t], m), tab);
-        named_sync(1, AV_COLS);
-        if (tid == 0) sum_sh = ordered_sum_smem(0.0f, pr, npos);
-        named_sync(1, AV_COLS);
-        const float sum = sum_sh;
-        for (int t = tid; t < npos; t += AV_COLS) pr[t] = __fdiv_rn(pr[t], sum);
+        if (resident) {
+            for (int t = tid; t < npos; t += AV_COLS) pr[t] = expf_host(__fsub_rn(a[t], m), tab);
+            named_sync(1, AV_COLS);
+            if (tid == 0) sum_sh = ordered_sum_smem(0.0f, pr, npos);
+            named_sync(1, AV_COLS);
+            const float sum = sum_sh;
+            for (int t = tid; t < npos; t += AV_COLS) pr[t] = __fdiv_rn(pr[t], sum);
+        } else {
+            float sum = 0.0f;                                 // thread 0's running sum, in position order
+            for (int e0 = 0; e0 < npos; e0 += AV_ECH) {
+                const int ne = npos - e0 < AV_ECH ? npos - e0 : AV_ECH;
+                for (int t = tid; t < ne; t += AV_COLS) ech[t] = expf_host(__fsub_rn(a[e0 + t], m), tab);
+                named_sync(1, AV_COLS);
+                if (tid == 0) sum = ordered_sum_smem(sum, ech, ne);
+                named_sync(1, AV_COLS);                       // ech is free again
+            }
+            if (tid == 0) sum_sh = sum;
+        }
     }
     // value chains: thread j < 64 runs element col0 + j over the positions in
     // order.  Iteration c: chunk c has landed (the copiers' wait, then the
     // barrier), the copiers refill slot (c + AV_NST - 1) % AV_NST -- chunk
     // c - 1's, which every chain finished before this barrier -- while the
-    // chains run c.
+    // chains run c.  (Long mode: the chunk's probabilities first, into pr.)
     float acc = 0.0f;
     for (int c = 0; c < nch; ++c) {
         if (producer) cp_async_wait<AV_NST - 2>();            // chunks c .. c + AV_NST - 2 were pending
-        __syncthreads();                                      // chunk c visible; (c == 0) the probabilities are final
+        __syncthreads();                                      // chunk c visible; (c == 0) the softmax is done
+        const int c0 = c * AT_CH, n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
         if (producer) {
             stage(c + AV_NST - 1);
         } else {
-            const int c0 = c * AT_CH, n = npos - c0 < AT_CH ? npos - c0 : AT_CH;
-            acc = value_chain(acc, pr + c0, reinterpret_cast<const float *>(dyn + (c % AV_NST) * AV_BUF) + tid, n);
+            const float *pc = pr + c0;
+            if (!resident) {                                  // this chunk's probabilities, recomputed
+                const float sum = sum_sh;
+                for (int t = tid; t < n; t += AV_COLS) pr[t] = __fdiv_rn(expf_host(__fsub_rn(a[c0 + t], m), tab), sum);
+                named_sync(1, AV_COLS);
+                pc = pr;
+            }
+            if (probs && part == 0)
+                for (int t = tid; t < n; t += AV_COLS) probs[int64_t(h) * seq_len + c0 + t] = pc[t];
+            acc = value_chain(acc, pc, reinterpret_cast<const float *>(dyn + (c % AV_NST) * AV_BUF) + tid, n);
+            if (!resident) named_sync(1, AV_COLS);            // every chain is done with pr before it is refilled
         }
     }
     if (producer) cp_async_wait<0>();                         // nothing in flight at exit
+    if (xb && tid < AV_COLS) xb[int64_t(h) * AT_HD + col0 + tid] = acc;
+    if (!xq) return;                                          // (uniform over the CTA)
     // the quantize of this group (:431): absmax from 0, scale = wmax / 127, codes
     const float gm = warp_max(tid < AV_COLS ? fmaxf(0.0f, fabsf(acc)) : 0.0f);
     if (lane == 0) red[warp] = gm;
@@ -387,82 +328,48 @@ __global__ void __launch_bounds__(AT_HD, 1) attn_values_kernel(const float *att,
     if (tid == 0) xs[int64_t(h) * 2 + part] = qscale;
 }
 
-// Q/K RMSNorm + RoPE of one token (qwen3_original.c:361-393) with the
-// rotation's cos/sin given by the host: the reference takes them from the C
-// library (cosf/sinf of pos*freq, :367-368), so the host computing them with
-// the same calls makes the rotation bit-exact; they reach the device in the
-// step's parameters, with the position.  The Q|K|V matmul left this token's
-// rows in qkv = [q | k | v]: one warp per head row normalises and rotates the
-// n_heads query rows in place and the n_kv key rows into their cache row at
-// pos (:349-350, keys rotated in the cache as the reference does), and n_kv
-// more warps copy the value rows into theirs.  Lane 0 runs a row's sum of
-// squares in index order (rmsnorm, :278-289); then every lane normalises and
-// rotates four elements: x' = w*(ss*x), (x, y) -> (x c - y s, x s + y c), each
-// product and sum rounded once.
-__global__ void __launch_bounds__(128) qk_norm_rope_step_kernel(float *qkv, float *kc, float *vc, int n_heads, int n_kv,
-                                                                const float *__restrict__ qn,
-                                                                const float *__restrict__ kn,
-                                                                const StepParams *__restrict__ sp, float eps) {
-    __shared__ __align__(16) float rows[4][AT_HD], sq[4][AT_HD];
-    griddep_launch_dependents();                  // the attention launches wait for this kernel before reading
-    griddep_wait();                               // qkv from the matmul before
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int row = blockIdx.x * 4 + warp;
-    if (row >= n_heads + 2 * n_kv) return;                  // whole warps
-    const int kv_dim = n_kv * AT_HD, pos = sp->pos;
-    if (row >= n_heads + n_kv) {                              // value row: copy into the cache
-        const int r = row - n_heads - n_kv;
-        const float *src = qkv + int64_t(n_heads) * AT_HD + kv_dim + r * AT_HD;
-        float *dst = vc + int64_t(pos) * kv_dim + r * AT_HD;
-        reinterpret_cast<float4 *>(dst)[lane] = reinterpret_cast<const float4 *>(src)[lane];
-        return;
-    }
-    const bool isq = row < n_heads;
-    const float *v = isq ? qkv + int64_t(row) * AT_HD : qkv + int64_t(n_heads) * AT_HD + (row - n_heads) * AT_HD;
-    float *o = isq ? qkv + int64_t(row) * AT_HD : kc + int64_t(pos) * kv_dim + (row - n_heads) * AT_HD;
-    norm_rope_row(v, isq ? qn : kn, sp, eps, rows[warp], sq[warp], o, lane);
-}
-
-static cudaError_t launch_qk_norm_rope_step(float *qkv, float *kc, float *vc, int n_heads, int n_kv, const float *qn,
-                                     const float *kn, const StepParams *sp, float eps, cudaStream_t stream) {
-    return launch_dependent(qk_norm_rope_step_kernel, dim3((n_heads + 2 * n_kv + 3) / 4), dim3(128), 0, stream, qkv,
-                            kc, vc, n_heads, n_kv, qn, kn, sp, eps);
-}
-
 cudaError_t launch_attention_step(float *qkv, float *kc, float *vc, float *att, int8_t *xq, float *xs,
                                   const StepParams *sp, int n_heads, int n_kv, const float *qn, const float *kn,
                                   float eps, int seq_len, cudaStream_t stream, int sms) {
     const int kv_dim = n_kv * AT_HD, kv_mul = n_heads / n_kv;
-    if (seq_len <= AV_MAXPOS) {                               // two launches, (head, chunk) / (head, half)
-        const size_t vsm = AV_NST * AV_BUF + size_t(seq_len) * 4;
-        cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_scores_kernel), AT_BUF, 25);
-        if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void *>(attn_values_kernel),
-                                                   AV_NST * AV_BUF + size_t(AV_MAXPOS) * 4, 26);
-        if (e != cudaSuccess) return e;
-        const int64_t items = int64_t(n_heads) * ((seq_len + AT_CH - 1) / AT_CH);
-        const int grid = int(items < int64_t(AS_PER_SM) * sms ? items : int64_t(AS_PER_SM) * sms);
-        e = launch_dependent(attn_scores_kernel, dim3(grid), dim3(AT_HD), AT_BUF, stream, qkv, kc, vc, att, qn, kn, sp,
-                             eps, n_heads, kv_dim, kv_mul, seq_len);
-        if (e != cudaSuccess) return e;
-        return launch_dependent(attn_values_kernel, dim3(n_heads, 2), dim3(AT_HD), vsm, stream, att, vc, xq, xs, sp,
-                                kv_dim, kv_mul, seq_len);
-    }
-    // long contexts: the rotations into q and the caches first, then one kernel
-    cudaError_t e = launch_qk_norm_rope_step(qkv, kc, vc, n_heads, n_kv, qn, kn, sp, eps, stream);
-    if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void *>(attn_decode_kernel), AT_SMEM, 24);
+    // two launches, (head, chunk) / (head, half), any context length; the values
+    // launch keeps all probabilities in shared memory while they fit (res_cap)
+    const int res_cap = seq_len <= AV_MAXPOS ? seq_len : AT_CH + AV_ECH;
+    const size_t vsm = AV_NST * AV_BUF + size_t(res_cap) * 4;
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_scores_kernel<true>), AT_BUF, 25);
+    if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void *>(attn_values_kernel),
+                                               AV_NST * AV_BUF + size_t(AV_MAXPOS) * 4, 26);
     if (e != cudaSuccess) return e;
-    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(qkv, kc, vc, att, xq, xs, nullptr, &sp->pos, 0, kv_dim,
-                                                            kv_mul, seq_len);
-    return cudaGetLastError();
+    const int64_t items = int64_t(n_heads) * ((seq_len + AT_CH - 1) / AT_CH);
+    const int grid = int(items < int64_t(AS_PER_SM) * sms ? items : int64_t(AS_PER_SM) * sms);
+    e = launch_dependent(attn_scores_kernel<true>, dim3(grid), dim3(AT_HD), AT_BUF, stream, qkv, kc, vc, att, qn, kn,
+                         sp, 0, eps, n_heads, kv_dim, kv_mul, seq_len);
+    if (e != cudaSuccess) return e;
+    return launch_dependent(attn_values_kernel, dim3(n_heads, 2), dim3(AT_HD), vsm, stream, att, vc, xq, xs,
+                            static_cast<float *>(nullptr), static_cast<float *>(nullptr), sp, 0, kv_dim, kv_mul,
+                            seq_len, res_cap);
 }
 
-cudaError_t launch_attention_rows(const float *q, const float *kc, const float *vc, float *att, float *xb, int pos,
-                                  int n_heads, int kv_dim, int kv_mul, int att_stride, cudaStream_t stream) {
-    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_decode_kernel), AT_SMEM, 24);
+cudaError_t launch_attention_rows(const float *q, const float *kc, const float *vc, float *att, float *probs, float *xb,
+                                  int pos, int n_heads, int kv_dim, int kv_mul, int att_stride, cudaStream_t stream,
+                                  int sms) {
+    const int npos = pos + 1;
+    const int res_cap = npos <= AV_MAXPOS ? npos : AT_CH + AV_ECH;
+    const size_t vsm = AV_NST * AV_BUF + size_t(res_cap) * 4;
+    cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(attn_scores_kernel<false>), AT_BUF, 24);
+    if (e == cudaSuccess) e = ensure_smem_attr(reinterpret_cast<const void *>(attn_values_kernel),
+                                               AV_NST * AV_BUF + size_t(AV_MAXPOS) * 4, 26);
     if (e != cudaSuccess) return e;
-    attn_decode_kernel<<<n_heads, AT_HD, AT_SMEM, stream>>>(q, kc, vc, att, nullptr, nullptr, xb, nullptr, pos, kv_dim,
-                                                            kv_mul, att_stride);
-    return cudaGetLastError();
+    const int64_t items = int64_t(n_heads) * ((npos + AT_CH - 1) / AT_CH);
+    const int grid = int(items < int64_t(AS_PER_SM) * sms ? items : int64_t(AS_PER_SM) * sms);
+    e = launch_dependent(attn_scores_kernel<false>, dim3(grid), dim3(AT_HD), AT_BUF, stream, q,
+                         const_cast<float *>(kc), const_cast<float *>(vc), att, static_cast<const float *>(nullptr),
+                         static_cast<const float *>(nullptr), static_cast<const StepParams *>(nullptr), pos, 0.0f,
+                         n_heads, kv_dim, kv_mul, att_stride);
+    if (e != cudaSuccess) return e;
+    return launch_dependent(attn_values_kernel, dim3(n_heads, 2), dim3(AT_HD), vsm, stream, att, vc,
+                            static_cast<int8_t *>(nullptr), static_cast<float *>(nullptr), xb, probs,
+                            static_cast<const StepParams *>(nullptr), pos, kv_dim, kv_mul, att_stride, res_cap);
 }
 
 __global__ void set_step_kernel(StepParams *sp, StepParams v) {

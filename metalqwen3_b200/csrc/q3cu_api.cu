@@ -430,6 +430,10 @@ q3cu_status q3cu_matmul_q8(q3cu_ctx *ctx, const int8_t *xq, const float *xs, int
     if (!aligned(xq, 32) || !aligned(wq, 32) || !aligned(xs, 4) || !aligned(ws, 4) || !aligned(out, 4))
         return fail(Q3CU_ERR_ALIGN, "xq and wq must be 32-byte aligned, xs, ws and out 4-byte aligned");
     if (q3cu_status st = use_device(ctx)) return st;
+    if (q3::matmul_q8_tc_supported(B, n, d))               // prefill batches: the tensor-core kernel
+        return launched(q3::launch_matmul_q8_tc(xq, xs, B, wq, ws, n, d, out, ctx->d_status,
+                                                static_cast<cudaStream_t>(stream), ctx->sms),
+                        "matmul_q8 (tensor cores) launch");
     return launched(q3::launch_matmul_q8(xq, xs, B, wq, ws, n, d, out, static_cast<cudaStream_t>(stream), ctx->sms),
                     "matmul_q8 launch");
 }
@@ -448,14 +452,16 @@ static q3cu_status check_attention(const float *q, const float *kc, const float 
 }
 
 q3cu_status q3cu_attention(q3cu_ctx *ctx, const float *q, const float *key_cache, const float *value_cache, int pos,
-                           int n_heads, int kv_dim, int kv_mul, float *att, int att_stride, float *xb,
+                           int n_heads, int kv_dim, int kv_mul, float *att, int att_stride, float *probs, float *xb,
                            q3cu_stream stream) {
     CHECK_CTX(ctx);
     if (q3cu_status st = check_attention(q, key_cache, value_cache, pos, n_heads, kv_dim, kv_mul, att, att_stride, xb))
         return st;
+    if (probs == att || (probs && !aligned(probs, 4)))
+        return fail(Q3CU_ERR_INVALID, "attention: probs must be NULL or a 4-byte aligned buffer other than att");
     if (q3cu_status st = use_device(ctx)) return st;
-    return launched(q3::launch_attention_rows(q, key_cache, value_cache, att, xb, pos, n_heads, kv_dim, kv_mul,
-                                              att_stride, static_cast<cudaStream_t>(stream)),
+    return launched(q3::launch_attention_rows(q, key_cache, value_cache, att, probs, xb, pos, n_heads, kv_dim, kv_mul,
+                                              att_stride, static_cast<cudaStream_t>(stream), ctx->sms),
                     "attention launch");
 }
 
@@ -573,25 +579,26 @@ q3cu_status q3cu_execute_attention(q3cu_ctx *ctx, float *xb, const float *q, flo
     // rows); the probabilities come back into att's columns 0..pos.
     const int npos = pos + 1, kvp = (kv_dim + 3) & ~3;
     const size_t qb = up16(size_t(n_heads) * 128 * 4), cb = up16(size_t(npos) * kvp * 4),
-                 ab = up16(size_t(n_heads) * npos * 4);
+                 ab = up16(size_t(n_heads) * npos * 4);          // scores, then the probabilities
     if (!xb || !q || !att || !key_cache || !value_cache || n_heads <= 0 || int64_t(kv_dim) < int64_t(n_kv_heads) * 128)
         return fail(Q3CU_ERR_INVALID, "executeAttention: bad argument (n_heads=%d kv_dim=%d n_kv=%d)", n_heads, kv_dim,
                     n_kv_heads);
     if (q3cu_status st = use_device(ctx)) return st;
-    if (q3cu_status st = grow_scratch(ctx, qb + 2 * cb + ab + qb)) return st;
+    if (q3cu_status st = grow_scratch(ctx, qb + 2 * cb + 2 * ab + qb)) return st;
     auto *d = static_cast<uint8_t *>(ctx->d_scratch);
     float *dq = reinterpret_cast<float *>(d), *dk = reinterpret_cast<float *>(d + qb),
           *dv = reinterpret_cast<float *>(d + qb + cb), *da = reinterpret_cast<float *>(d + qb + 2 * cb),
-          *dx = reinterpret_cast<float *>(d + qb + 2 * cb + ab);
+          *dp = reinterpret_cast<float *>(d + qb + 2 * cb + ab), *dx = reinterpret_cast<float *>(d + qb + 2 * cb + 2 * ab);
     TRY_CUDA(cudaMemcpyAsync(dq, q, size_t(n_heads) * 128 * 4, cudaMemcpyHostToDevice, ctx->stream), "H2D");
     TRY_CUDA(cudaMemcpy2DAsync(dk, size_t(kvp) * 4, key_cache + loff, size_t(kv_dim) * 4, size_t(kv_dim) * 4, npos,
                                cudaMemcpyHostToDevice, ctx->stream), "H2D");
     TRY_CUDA(cudaMemcpy2DAsync(dv, size_t(kvp) * 4, value_cache + loff, size_t(kv_dim) * 4, size_t(kv_dim) * 4, npos,
                                cudaMemcpyHostToDevice, ctx->stream), "H2D");
-    TRY_CUDA(q3::launch_attention_rows(dq, dk, dv, da, dx, pos, n_heads, kvp, kv_mul, npos, ctx->stream),
+    TRY_CUDA(q3::launch_attention_rows(dq, dk, dv, da, dp, dx, pos, n_heads, kvp, kv_mul, npos, ctx->stream,
+                                       ctx->sms),
              "attention");
     TRY_CUDA(cudaMemcpyAsync(xb, dx, size_t(n_heads) * 128 * 4, cudaMemcpyDeviceToHost, ctx->stream), "D2H");
-    TRY_CUDA(cudaMemcpy2DAsync(att, size_t(seq_len) * 4, da, size_t(npos) * 4, size_t(npos) * 4, n_heads,
+    TRY_CUDA(cudaMemcpy2DAsync(att, size_t(seq_len) * 4, dp, size_t(npos) * 4, size_t(npos) * 4, n_heads,
                                cudaMemcpyDeviceToHost, ctx->stream), "D2H");
     return finish(ctx);
 }

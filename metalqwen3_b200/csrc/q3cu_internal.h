@@ -91,6 +91,12 @@ cudaError_t launch_matmul_q8_seg(const int8_t *xq, const float *xs, int B, const
 cudaError_t launch_matmul_q8(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
                              int d, float *out, cudaStream_t stream, int sms, const float *add = nullptr);
 
+// The same matmul for prefill-sized batches on the tcgen05 tensor cores
+// (k_gemm.cu): B >= 128 token rows, n a multiple of 128.  Same bits.
+bool matmul_q8_tc_supported(int B, int n, int d);
+cudaError_t launch_matmul_q8_tc(const int8_t *xq, const float *xs, int B, const int8_t *wq, const float *ws, int n,
+                                int d, float *out, uint32_t *status, cudaStream_t stream, int sms);
+
 // One decode step's parameters, in device memory: the token, its position and
 // RoPE's cos/sin(pos * freq_j) for j < 64 (head_dim 128), computed on the host.
 struct StepParams {
@@ -104,19 +110,22 @@ cudaError_t launch_set_step(StepParams *sp, const StepParams &v, cudaStream_t st
 // (:361-393), k and v into the layer's cache rows at pos (kc / vc
 // [seq_len][n_kv * 128]), scores, softmax and weighted values (:395-428;
 // att [n_heads][seq_len] scratch), the output [n_heads][128] as Q8_0 codes xq
-// and scales xs [n_heads * 2] (:431).  Up to 16,384 positions: two launches
-// with the rotations inside the first; beyond: a rotation launch, then one
-// fused attention kernel.
+// and scales xs [n_heads * 2] (:431).  Two launches, the rotations inside the
+// first, at every context length (above 16,384 positions the values launch
+// recomputes each chunk's probabilities instead of keeping them all).
 cudaError_t launch_attention_step(float *qkv, float *kc, float *vc, float *att, int8_t *xq, float *xs,
                                   const StepParams *sp, int n_heads, int n_kv, const float *qn, const float *kn,
                                   float eps, int seq_len, cudaStream_t stream, int sms);
 
 // The attention of one token alone (qwen3_original.c:395-428, q already
 // normalised and rotated, K/V rows 0..pos in the caches [..][kv_dim]): the
-// probabilities into att [n_heads][att_stride] (att_stride > pos) and the head
-// outputs into xb [n_heads][128].  One CTA per query head; head_dim 128.
-cudaError_t launch_attention_rows(const float *q, const float *kc, const float *vc, float *att, float *xb, int pos,
-                                  int n_heads, int kv_dim, int kv_mul, int att_stride, cudaStream_t stream);
+// scores into att [n_heads][att_stride] (att_stride > pos, scratch), the
+// probabilities into probs (same shape, a different buffer; may be NULL) and
+// the head outputs into xb [n_heads][128].  The decode step's two launches (scores over
+// (head, chunk), then values over (head, half)); head_dim 128, any length.
+cudaError_t launch_attention_rows(const float *q, const float *kc, const float *vc, float *att, float *probs, float *xb,
+                                  int pos, int n_heads, int kv_dim, int kv_mul, int att_stride, cudaStream_t stream,
+                                  int sms);
 
 cudaError_t launch_swiglu(const void *hb, const void *hb2, q3cu_dtype dt, int64_t elems, void *out, int8_t *q,
                           float *s, uint32_t *status, cudaStream_t stream, int sms);

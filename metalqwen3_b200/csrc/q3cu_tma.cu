@@ -30,7 +30,7 @@ namespace {
 struct MapKey {
     const void *base;
     uint64_t rows, row_bytes;
-    uint32_t L, R;
+    uint32_t L, R;                       // L == 0: the 2-D map of encode_rows_2d_map
     bool operator==(const MapKey &o) const {
         return base == o.base && rows == o.rows && row_bytes == o.row_bytes && L == o.L && R == o.R;
     }
@@ -41,19 +41,46 @@ thread_local CUtensorMap t_maps[kMapCache];
 thread_local int t_used = 0, t_next = 0;
 }  // namespace
 
-bool encode_row_lines_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t row_bytes, uint32_t L,
-                          uint32_t R) {
-    const MapKey key{base, rows, row_bytes, L, R};
+static bool cache_lookup(const MapKey &key, CUtensorMap *map) {
     for (int i = 0; i < t_used; ++i)
         if (t_keys[i] == key) {
             *map = t_maps[i];
             return true;
         }
-    if (!encode_row_lines_map_uncached(map, base, rows, row_bytes, L, R)) return false;
+    return false;
+}
+static void cache_store(const MapKey &key, const CUtensorMap &map) {
     t_keys[t_next] = key;
-    t_maps[t_next] = *map;
+    t_maps[t_next] = map;
     t_next = (t_next + 1) % kMapCache;
     if (t_used < kMapCache) ++t_used;
+}
+
+bool encode_row_lines_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t row_bytes, uint32_t L,
+                          uint32_t R) {
+    const MapKey key{base, rows, row_bytes, L, R};
+    if (cache_lookup(key, map)) return true;
+    if (!encode_row_lines_map_uncached(map, base, rows, row_bytes, L, R)) return false;
+    cache_store(key, *map);
+    return true;
+}
+
+bool encode_rows_2d_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows) {
+    const MapKey key{base, rows, row_bytes, 0, box_rows};
+    if (cache_lookup(key, map)) return true;
+    EncodeTiled enc = encoder();
+    if (!enc || rows == 0 || row_bytes % 128 || (reinterpret_cast<uintptr_t>(base) % 16) || box_rows == 0 ||
+        box_rows > 256)
+        return false;
+    const cuuint64_t dims[2] = {row_bytes, rows};
+    const cuuint64_t strides[1] = {row_bytes};
+    const cuuint32_t box[2] = {128, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    cache_store(key, *map);
     return true;
 }
 

@@ -28,7 +28,19 @@ bool encode_row_lines_map(CUtensorMap *map, const void *base, uint64_t rows, uin
 bool encode_row_lines_map_uncached(CUtensorMap *map, const void *base, uint64_t rows, uint64_t row_bytes,
                                    uint32_t L, uint32_t R);
 
+// A row-major [rows][row_bytes] byte array as 2-D for TMA: box = {128 bytes,
+// box_rows rows}, landing as box_rows x 128 B with the 128-byte swizzle (the
+// K-major operand layout of the tensor-core MMA).  Cached like the above.
+bool encode_rows_2d_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows);
+
 #if defined(__CUDACC__)
+__device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+        :: "r"(static_cast<uint32_t>(__cvta_generic_to_shared(dst))), "l"(reinterpret_cast<uint64_t>(map)), "r"(x),
+           "r"(y), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
+        : "memory");
+}
 // Tiled 3-D tensor load of the box at (x, y, z) into shared memory at dst,
 // completing on `bar` (the caller has armed it with the box's bytes).  x is
 // the byte offset within the line and is always 0 here (16-byte aligned).

@@ -66,7 +66,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
                 "q3cu_embed_gather": (st, [vp, vp, vp, i32, i32, vp, i64, vp, vp, vp, vp]),
                 "q3cu_matmul_q8": (st, [vp, vp, vp, i32, vp, vp, i32, i32, vp, vp]),
                 "q3cu_execute_quantized_matmul": (st, [vp, vp, vp, vp, vp, vp, i32, i32, i32]),
-                "q3cu_attention": (st, [vp, vp, vp, vp, i32, i32, i32, i32, vp, i32, vp, vp]),
+                "q3cu_attention": (st, [vp, vp, vp, vp, i32, i32, i32, i32, vp, i32, vp, vp, vp]),
                 "q3cu_execute_attention": (st, [vp, vp, vp, vp, vp, vp, i32, i32, i32, i32, i32, i32, C.c_uint64,
                                                 i32]),
                 "q3cu_model_load": (st, [vp, vp, C.c_size_t, i32, C.POINTER(vp)]),
@@ -231,19 +231,21 @@ class Q3CU:
                                             self._stream(stream)), "q3cu_matmul_q8")
         return out
 
-    def attention(self, q, key_cache, value_cache, pos, kv_mul, att=None, xb=None, stream=None):
+    def attention(self, q, key_cache, value_cache, pos, kv_mul, att=None, probs=None, xb=None, stream=None):
         """One token's attention over cache rows 0..pos: q [n_heads][128];
-        key_cache / value_cache [rows][kv_dim]; returns (xb [n_heads][128],
-        att [n_heads][att_stride] with the probabilities in columns 0..pos)."""
+        key_cache / value_cache [rows][kv_dim]; att: scratch for the scores;
+        returns (xb [n_heads][128], probs [n_heads][att_stride] with the
+        probabilities in columns 0..pos)."""
         T = self.torch
         n_heads = q.numel() // 128
         kv_dim = key_cache.shape[-1]
         att = T.zeros((n_heads, pos + 1), dtype=T.float32, device=q.device) if att is None else att
+        probs = T.zeros_like(att) if probs is None else probs
         xb = T.empty((n_heads, 128), dtype=T.float32, device=q.device) if xb is None else xb
         self._check(self.lib.q3cu_attention(self.ctx, _ptr(q), _ptr(key_cache), _ptr(value_cache), pos, n_heads,
-                                            kv_dim, kv_mul, _ptr(att), att.shape[-1], _ptr(xb), self._stream(stream)),
-                    "q3cu_attention")
-        return xb, att
+                                            kv_dim, kv_mul, _ptr(att), att.shape[-1], _ptr(probs), _ptr(xb),
+                                            self._stream(stream)), "q3cu_attention")
+        return xb, probs
 
     # -- host-pointer drop-in (numpy arrays, synchronous) -----------------------
     def execute_attention(self, xb, q, att, key_cache, value_cache, pos, head_dim, n_heads, n_kv_heads, seq_len,

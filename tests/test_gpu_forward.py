@@ -89,10 +89,15 @@ LONG = {
     # chunks wraps several times
     "split_1800": (dict(dim=128, hidden=384, n_layers=2, n_heads=32, n_kv=8, vocab=200, seq_len=1800,
                         head_dim=128), range(1800)),
-    # seq_len above the two-launch limit of 16384 positions: the single fused
-    # attention kernel, over its first 300 positions (3 chunks)
-    "fused_16400": (dict(dim=256, hidden=768, n_layers=2, n_heads=4, n_kv=2, vocab=300, seq_len=16400,
-                         head_dim=128), range(300)),
+    # a context above 16,384 positions: the values launch keeps the
+    # probabilities in shared memory while they fit its long-context
+    # allocation (4,224 positions), over the first 300 positions here
+    "long_16400": (dict(dim=256, hidden=768, n_layers=2, n_heads=4, n_kv=2, vocab=300, seq_len=16400,
+                        head_dim=128), range(300)),
+    # a 33,000-position context, 4,400 positions: past 4,224 the values
+    # launch recomputes each chunk's probabilities instead of keeping them
+    "long_33000_chunked": (dict(dim=256, hidden=768, n_layers=2, n_heads=4, n_kv=2, vocab=300, seq_len=33000,
+                                head_dim=128), range(4400)),
 }
 
 

@@ -593,7 +593,8 @@ def test_execute_dropin(q3, oracle):
 
 
 @pytest.mark.parametrize("pos,n_heads,n_kv,seq_len,layer", [(0, 16, 8, 64, 0), (37, 16, 8, 64, 1), (700, 32, 8, 1024, 2),
-                                                          (5000, 4, 4, 5001, 0)])
+                                                          (5000, 4, 4, 5001, 0),
+                                                          (40959, 8, 4, 40960, 0)])   # 40,960 positions: chunked
 def test_execute_attention(q3, oracle, pos, n_heads, n_kv, seq_len, layer):
     """MetalContext::executeAttention (the engine's metal_attention call,
     MetalQwen3.cpp:639): one token's heads over a layer's cache rows at loff,
@@ -635,6 +636,10 @@ def test_attention_rejects_bad_arguments(q3):
     assert e.value.status == 1
     with pytest.raises(Q3Error) as e:                                 # 4 heads / kv_mul 1 need 4 kv heads of 128
         q3.attention(q, kc, kc, 3, 1)
+    assert e.value.status == 1
+    a = torch.zeros(4, 10, device="cuda")
+    with pytest.raises(Q3Error) as e:                                 # the probabilities may not overwrite the scores
+        q3.attention(q, kc, kc, 3, 2, att=a, probs=a)
     assert e.value.status == 1
     with pytest.raises(Q3Error) as e:
         q3.execute_attention(np.zeros(512, np.float32), np.zeros(512, np.float32), np.zeros(40, np.float32),
@@ -703,3 +708,43 @@ def test_execute_quantized_matmul(q3, oracle):
     with pytest.raises(Q3Error) as e:
         q3.execute_quantized_matmul(out, xq[0], xs[0], wq, ws, 2048, 1024, group_size=32)
     assert e.value.status == 3                       # ERR_GROUP
+
+
+# --------------------------------------------------------------------------- tensor-core Q8_0 matmul
+@pytest.mark.parametrize("B,n,d", [
+    (128, 128, 128),          # one tile, one K-stage (two groups)
+    (300, 2560, 1000),        # ragged token and output tiles, 40 groups (10 passes over the 4 accumulators)
+    (1024, 1024, 3072),       # Qwen3-0.6B W1-shaped, several tiles per SM
+])
+def test_matmul_q8_tensor_cores(q3, oracle, B, n, d):
+    """Prefill-sized batches (>= 128 token rows) go through the tcgen05 kernel:
+    every output bit-identical to the reference's matmul (qwen3_original.c:310-331)."""
+    rng = np.random.default_rng(B + n + d)
+    xq, xs, wq, wsc = q8_operands(rng, B, n, d)
+    g = host(q3.matmul_q8(*(dev(a) for a in (xq, xs, wq, wsc))))
+    o = oracle.matmul(xq, xs, wq, wsc)
+    assert same_bits(g, o), f"{int((bits(g) != bits(o)).sum())} of {g.size} differ"
+    assert q3.device_status() == 0
+
+
+def test_matmul_q8_tensor_cores_extremes(q3, oracle):
+    """The tensor-core path with -128 codes, zero, huge and infinite scales
+    (inf * 0 = NaN in the reference's chain): the same bits or the same NaNs."""
+    xq, xs, wq, ws = q8_operands(np.random.default_rng(5), 128, 640, 40, extremes=True)
+    with np.errstate(all="ignore"):
+        assert same_bits(host(q3.matmul_q8(dev(xq), dev(xs), dev(wq), dev(ws))), oracle.matmul(xq, xs, wq, ws))
+
+
+def test_matmul_q8_tensor_cores_prefill_4b(q3, oracle):
+    """The Qwen3-4B prefill W1 product (4096 tokens, 2560 -> 9728), with
+    extreme codes (+-127 and -128) in some groups: 96 sampled token rows
+    against the oracle, all 9728 outputs each, bit for bit."""
+    rng = np.random.default_rng(7)
+    B, n, d = 4096, 2560, 9728
+    xq, xs, wq, wsc = q8_operands(rng, B, n, d)
+    xq[5, :64] = 127; wq[:, :64] = 127; xq[6, 64:128] = -128; wq[:, 64:128] = -128
+    g = host(q3.matmul_q8(*(dev(a) for a in (xq, xs, wq, wsc))))
+    rows = np.unique(np.concatenate([[0, 5, 6, B - 1], rng.integers(0, B, 92)]))
+    o = oracle.matmul(xq[rows], xs[rows], wq, wsc)
+    assert same_bits(g[rows], o), f"{int((bits(g[rows]) != bits(o)).sum())} of {o.size} differ"
+    assert q3.device_status() == 0
