@@ -858,6 +858,85 @@ class Matmul06B(Workload):
         return out
 
 
+class Matmul4B(Workload):
+    """The prefill form of the Q8_0 matmul (qwen3_original.c:310-331 applied to
+    every token row) on the tensor cores: the Qwen3-4B FFN up-projection of a
+    4096-token batch, x codes/scales [4096][2560] (the rmsnorm_q8 output) times
+    W1 [9728][2560] into f32 [4096][9728].  tcgen05 int8 MMA, the float chain
+    per group in the reference's order (bit-exact).  Compute-bound: the
+    roofline is int8 tensor throughput (2 ops per multiply-add)."""
+    name = "matmul4b"
+    dtype = "int8 codes (tcgen05 int8 MMA, exact int32) -> f32"
+    bound = "tensor"
+
+    def __init__(self, tokens=4096, n=2560, d=9728):
+        self.tokens, self.n, self.d = tokens, n, d
+
+    def kernels(self):
+        T, n, d = self.tokens, self.n, self.d
+        return [("matmul_q8_tc", T * n + T * (n // GS) * 4 + d * n + d * (n // GS) * 4 + 4 * T * d)]
+
+    def flops(self):
+        return 2 * self.tokens * self.n * self.d
+
+    def config(self):
+        return {"workload": "Qwen3-4B prefill FFN up-projection, Q8_0 x Q8_0 on the tcgen05 tensor cores",
+                "tokens_per_gpu": self.tokens, "n": self.n, "d": self.d,
+                "weights": "codes uniform [-127,127], scales |N(0,0.01)|; x scales |N(0,0.05)|"}
+
+    def make(self, torch, dev, seed):
+        g = torch.Generator(device=dev)
+        g.manual_seed(seed)
+        T, n, d = self.tokens, self.n, self.d
+        return {"xq": torch.randint(-127, 128, (T, n), dtype=torch.int8, device=dev, generator=g),
+                "xs": (0.05 * torch.randn(T, n // GS, device=dev, generator=g)).abs(),
+                "wq": torch.randint(-127, 128, (d, n), dtype=torch.int8, device=dev, generator=g),
+                "ws": (0.01 * torch.randn(d, n // GS, device=dev, generator=g)).abs(),
+                "out": torch.empty(T, d, device=dev)}
+
+    def launch(self, q3, d, stream, events=None):
+        if events is not None:
+            events[0][0].record(stream)
+        q3.matmul_q8(d["xq"], d["xs"], d["wq"], d["ws"], out=d["out"], stream=stream)
+        if events is not None:
+            events[0][1].record(stream)
+        return 1
+
+    h2d_keys = ("xq", "xs")
+    d2h_keys = ("out",)
+
+    def cpu_step(self, oracle, np, sample, threads, rng):
+        """The reference's own matmul (OpenMP over output rows) on a few token rows."""
+        if not hasattr(self, "_cpu"):
+            from oracle.oracle import Oracle, Reference
+            try:
+                self._mm = Reference().matmul
+            except Exception:
+                self._mm = Oracle().matmul
+            n, d = self.n, self.d
+            self._cpu = (rng.integers(-127, 128, (4, n), dtype=np.int8),
+                         np.abs(0.05 * rng.standard_normal((4, n // GS))).astype(np.float32),
+                         rng.integers(-127, 128, (d, n), dtype=np.int8),
+                         np.abs(0.01 * rng.standard_normal((d, n // GS))).astype(np.float32))
+        self._mm(*self._cpu)
+
+    cpu_tokens = 4
+    cpu_note = ("the reference's own matmul (src/cpu/qwen3_original.c:310-331, compiled unmodified, OpenMP over "
+                "output rows), 4 token rows per pass")
+
+    def bytes_for_tokens(self, n):
+        return self.total_bytes() * n / self.tokens
+
+    def parity_snapshot(self, d):
+        return {"rows": _sample_rows(self.tokens, 16)}
+
+    def parity(self, oracle, snap, d, q3=None):
+        import numpy as np
+        S = snap["rows"]
+        o = oracle.matmul(_host(d["xq"][S]), _host(d["xs"][S]), _host(d["wq"]), _host(d["ws"]))
+        return {"token_rows": int(S.size), "outputs": int((_host(d["out"][S]).view(np.uint32) != o.view(np.uint32)).sum())}
+
+
 class Forward06B(Workload):
     """One Qwen3-0.6B decode token through the whole model on the device
     (q3cu_model_load + q3cu_model_forward: qwen3_original.c:333-468), at
@@ -1016,7 +1095,7 @@ class Forward06B(Workload):
 
 
 WORKLOADS = {"prefill4b": Prefill4B, "decode8b": Decode8B, "embed": Embed, "prefill14b": Prefill14B,
-             "decode06b": Decode06B, "matmul06b": Matmul06B, "forward06b": Forward06B}
+             "decode06b": Decode06B, "matmul06b": Matmul06B, "matmul4b": Matmul4B, "forward06b": Forward06B}
 
 
 # ---------------------------------------------------------------------------- clocks
@@ -1081,6 +1160,19 @@ def measured_hbm_peak():
             return float(json.load(f)["hbm_gbs"]), "measured"
     except Exception:
         return 6650.0, "fallback"
+
+
+def measured_tensor_peak():
+    """Dense int8 tensor throughput for the roofline: twice the measured dense
+    bf16 burst figure (MEASURED_PEAKS.json bf16_tflops; B200's dense int8 rate
+    is twice its bf16 rate), else twice the fallback 1.59 PFLOP/s."""
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            v = float(json.load(f)["bf16_tflops"])
+        return 2 * v, "2 x measured dense bf16 burst (MEASURED_PEAKS.json bf16_tflops): int8 rate"
+    except Exception:
+        return 2 * 1590.0, "2 x fallback 1590 TFLOP/s bf16: int8 rate"
 
 
 def profiled_traffic(workload, kernel, alg_bytes=None):
@@ -1544,6 +1636,9 @@ def run_one(args):
         dom_name, dom_bytes = max(wl.kernels(), key=lambda kb: kb[1])
         dom_avg_s = statistics.mean(per_kernel[[n for n, _ in wl.kernels()].index(dom_name)]) / 1e3
         achieved = dom_bytes / dom_avg_s / 1e9
+        tensor = getattr(wl, "bound", "hbm") == "tensor"
+        if tensor:
+            tpeak, tkind = measured_tensor_peak()
         scaling = "strong" if strong else "weak"
         par = (f"token rows split over {world} GPUs (strong: the configuration's total is fixed)" if strong else
                f"token rows x{world} (weak: the same batch on every GPU)")
@@ -1564,11 +1659,17 @@ def run_one(args):
             "tokens_per_s": round(all_tokens * args.steps / (total_ms / 1e3), 1),
             "hbm_frac": round(gbs / world / peak, 4),
             "kernels": kern,
-            "roofline": {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": peak,
-                         "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
-                         else "fallback 6650 GB/s", "unit": "GB/s", "frac": round(achieved / peak, 4),
-                         "traffic": profiled_traffic(wl.name, dom_name, dom_bytes),
-                         "algorithmic_bytes_per_launch": dom_bytes},
+            "roofline": ({"bound": "tensor", "kernel": dom_name,
+                          "achieved": round(wl.flops() / dom_avg_s / 1e12, 1), "peak": tpeak, "peak_source": tkind,
+                          "unit": "TFLOP/s", "frac": round(wl.flops() / dom_avg_s / 1e12 / tpeak, 4),
+                          "traffic": profiled_traffic(wl.name, dom_name, dom_bytes),
+                          "hbm_gbs": round(achieved, 1), "algorithmic_flops_per_launch": wl.flops(),
+                          "algorithmic_bytes_per_launch": dom_bytes} if tensor else
+                         {"bound": "hbm", "kernel": dom_name, "achieved": round(achieved, 1), "peak": peak,
+                          "peak_source": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)" if peak_kind == "measured"
+                          else "fallback 6650 GB/s", "unit": "GB/s", "frac": round(achieved / peak, 4),
+                          "traffic": profiled_traffic(wl.name, dom_name, dom_bytes),
+                          "algorithmic_bytes_per_launch": dom_bytes}),
             "e2e": {"value": round(e2e_all_bytes * args.e2e_steps / (e2e_ms / 1e3) / 1e9, 3), "unit": "GB/s",
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                     "ms_per_step": round(e2e_ms / args.e2e_steps, 3),

@@ -84,6 +84,28 @@ bool encode_rows_2d_map(CUtensorMap *map, const void *base, uint64_t rows, uint6
     return true;
 }
 
+bool encode_f32_2d_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                       uint32_t box_rows, bool swizzle128) {
+    // keyed apart from the byte maps: L = box_cols | 1 << 31 (| 1 << 30 swizzled) never occurs there
+    const MapKey key{base, rows, cols, box_cols | 0x80000000u | (swizzle128 ? 0x40000000u : 0u), box_rows};
+    if (cache_lookup(key, map)) return true;
+    EncodeTiled enc = encoder();
+    if (!enc || rows == 0 || cols % 4 || (reinterpret_cast<uintptr_t>(base) % 16) || box_cols == 0 ||
+        (box_cols * 4) % 16 || box_cols > 256 || box_rows == 0 || box_rows > 256 || (swizzle128 && box_cols != 32))
+        return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 4};
+    const cuuint32_t box[2] = {box_cols, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    if (enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<void *>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_NONE,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+        return false;
+    cache_store(key, *map);
+    return true;
+}
+
 bool encode_row_lines_map_uncached(CUtensorMap *map, const void *base, uint64_t rows, uint64_t row_bytes,
                                    uint32_t L, uint32_t R) {
     EncodeTiled enc = encoder();

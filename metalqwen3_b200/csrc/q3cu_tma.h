@@ -33,6 +33,14 @@ bool encode_row_lines_map_uncached(CUtensorMap *map, const void *base, uint64_t 
 // K-major operand layout of the tensor-core MMA).  Cached like the above.
 bool encode_rows_2d_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t row_bytes, uint32_t box_rows);
 
+// A row-major [rows][cols] fp32 matrix as 2-D for TMA stores: box = {box_cols,
+// box_rows}; shared memory holds the box row-major, with the 128-byte swizzle
+// when swizzle128 (box_cols == 32; 16-byte chunk c of box row r at c ^ (r % 8),
+// 1024-byte aligned).  Requires base 16-byte aligned, cols % 4 == 0 and
+// box_cols * 4 a multiple of 16.  Cached.
+bool encode_f32_2d_map(CUtensorMap *map, const void *base, uint64_t rows, uint64_t cols, uint32_t box_cols,
+                       uint32_t box_rows, bool swizzle128);
+
 #if defined(__CUDACC__)
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, int x, int y, uint64_t *bar) {
     asm volatile(
@@ -51,6 +59,22 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, i
            "r"(y), "r"(z), "r"(static_cast<uint32_t>(__cvta_generic_to_shared(bar)))
         : "memory");
 }
+// Tiled 2-D tensor store of the box at (x, y) from shared memory at src, in the
+// thread's bulk async-group (the caller commits it).  Out-of-range parts of the
+// box are not written.
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap *map, int x, int y, const void *src) {
+    asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];"
+                 :: "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y),
+                    "r"(static_cast<uint32_t>(__cvta_generic_to_shared(src)))
+                 : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until the thread's bulk stores have finished reading shared memory.
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// Waits until the thread's bulk stores are complete.
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later async-proxy (TMA) reads.
+__device__ __forceinline__ void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" :: "l"(reinterpret_cast<uint64_t>(map)) : "memory");
 }

@@ -715,6 +715,9 @@ def test_execute_quantized_matmul(q3, oracle):
     (128, 128, 128),          # one tile, one K-stage (two groups)
     (300, 2560, 1000),        # ragged token and output tiles, 40 groups (10 passes over the 4 accumulators)
     (1024, 1024, 3072),       # Qwen3-0.6B W1-shaped, several tiles per SM
+    (256, 4224, 136),         # 66 groups: the last staged chunk holds 2 groups
+    (200, 9728, 384),         # Qwen3-4B W2-shaped K (152 groups: ten staged chunks)
+    (256, 256, 130),          # d % 4 != 0: outputs by plain stores instead of tensor stores
 ])
 def test_matmul_q8_tensor_cores(q3, oracle, B, n, d):
     """Prefill-sized batches (>= 128 token rows) go through the tcgen05 kernel:
