@@ -104,7 +104,12 @@ def test_config3_softmax_full_size(q3, oracle):
 @pytest.mark.parametrize("dim,hidden,nh,posmax", [(4096, 12288, 32, 32768), (5120, 17408, 40, 4096)])
 def test_bf16_layer_shapes(q3, oracle, dim, hidden, nh, posmax):
     """Configs 3 (dim 4096, hidden 12288, 32 + 8 heads) and 5 (dim 5120, hidden
-    17408, 40 + 8 heads, 1% outlier channels) on bf16 rows."""
+    17408, 40 + 8 heads, 1% outlier channels) on bf16 rows.  RMSNorm, SwiGLU
+    and their Q8_0 codes are bit-exact; RoPE is held to 1e-2 relative plus
+    BF16_ATOL = 1e-6 absolute: the device's sincosf is within a few ulps of the
+    host's cosf/sinf, and a rotated pair that cancels to near zero (|o| below
+    1e-4 on these unit-variance rows) has no meaningful relative error, so the
+    absolute term, 1e-6 of the data's scale, bounds those outputs instead."""
     rng = np.random.default_rng(dim)
     rows = 96
     outl = 0.01 if dim == 5120 else 0.0
