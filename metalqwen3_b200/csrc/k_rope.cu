@@ -12,13 +12,15 @@
 // rows.  A warp owns a tile of 32 consecutive head rows of one tensor, one row
 // per lane:
 //   * a copy warp per CTA copies every compute warp's tiles (one contiguous
-//     16 KB / 8 KB range each) into 32 padded shared-memory row slots with
-//     16-byte cp.async copies, 512 bytes per instruction; two buffers per
-//     compute warp with full/empty mbarriers (bounded waits), so the next tile
-//     streams in while this one is processed and the issue stalls of cp.async
-//     (an SM keeps only ~50 KB in flight) fall on the copy warp.  (A bulk copy
-//     per 512-byte row costs ~30 ns of copy-engine time per row per SM, more
-//     than the HBM time of the row.)
+//     16 KB / 8 KB range each) with one bulk copy per tile (cp.async.bulk,
+//     completing on the buffer's mbarrier); two buffers per compute warp with
+//     full/empty mbarriers (bounded waits), so the next tile streams in while
+//     this one is processed.  Bulk copies are not held to the ~50 KB of
+//     16-byte cp.async an SM keeps in flight, which capped the earlier
+//     per-piece copies near 25 GB/s per SM.  The tile lands dense; the compute
+//     warp then moves it in place into 32 padded row slots (coalesced 16-byte
+//     reads, conflict-free 16-byte writes; the back half of the rows first,
+//     so no row is overwritten before it is read);
 //   * lane i runs row i's sum of squares in index order (the reference's
 //     rounding sequence, so the normalised values are bit-exact);
 //   * the warp fills a table with cos/sin of every token the tile touches
@@ -126,14 +128,16 @@ __global__ void __launch_bounds__((rope_warps<T>() + 1) * 32, 1) qk_norm_rope_ke
     };
     // Compute warp w's tiles are t = blockIdx.x * RW + w + kk * GW, kk = 0, 1, ...,
     // in buffer kk & 1.  The copy warp (wid == RW) copies them all, in kk order,
-    // with 16-byte cp.async pieces: an SM keeps only ~50 KB of cp.async in
-    // flight and issuing beyond that stalls the issuing warp, so the stalls
-    // fall on a warp with nothing else to do.  Each piece is attached to the
-    // buffer's `full` barrier (balanced arrival) and one plain arrival follows;
-    // the compute warp releases the buffer on `empty` after its write-back.
+    // one bulk copy per tile into the start of the buffer (the expect-tx
+    // arrival is the buffer's one arrival); the compute warp releases the
+    // buffer on `empty` after its write-back.
     if (wid == RW) {
-        for (int64_t kk = 0;; ++kk) {
-            bool any = false, ok = true;
+        int64_t last[RW];                       // the last round whose tile was copied, per compute warp
+#pragma unroll
+        for (int w = 0; w < RW; ++w) last[w] = -1;
+        bool ok = true;
+        for (int64_t kk = 0; ok; ++kk) {
+            bool any = false;
             for (int w = 0; w < RW && ok; ++w) {
                 const int64_t t = int64_t(blockIdx.x) * RW + w + kk * GW;
                 if (t >= ntiles) continue;
@@ -146,17 +150,25 @@ __global__ void __launch_bounds__((rope_warps<T>() + 1) * 32, 1) qk_norm_rope_ke
                 }
                 T *base; int64_t row0; int nvalid, heads;
                 tile_info(t, base, row0, nvalid, heads);
-                const uint8_t *src = reinterpret_cast<const uint8_t *>(base + row0 * HD);
-                uint8_t *dst = smem + size_t(w) * rope_warp_bytes<T>() + size_t(b) * ROPE_TILE * ROWB;
-                for (int c = lane; c < nvalid * CPR; c += 32)
-                    cp_async16(dst + (c / CPR) * ROWB + (c % CPR) * 16, src + size_t(c) * 16);
-                cp_async_track(&full[w][b]);
+                if (lane == 0) {
+                    const uint32_t bytes = uint32_t(nvalid) * ROWBYTES;
+                    mbar_arrive_expect_tx(&full[w][b], bytes);
+                    bulk_g2s(smem + size_t(w) * rope_warp_bytes<T>() + size_t(b) * ROPE_TILE * ROWB,
+                             base + row0 * HD, bytes, &full[w][b]);
+                }
                 __syncwarp();
-                if (lane == 0) mbar_arrive(&full[w][b]);
+                last[w] = kk;
             }
             if (!any || !ok || __any_sync(FULL, fail_sh != 0)) break;
         }
-        cp_async_wait<0>();    // no copy may still be landing when the CTA exits
+        // No copy may still be landing when the CTA exits.  Normally every compute
+        // warp has waited for all of its tiles; after a failure, wait (bounded) for
+        // the latest copy into each buffer.
+        if (lane == 0)
+#pragma unroll
+            for (int w = 0; w < RW; ++w)
+                for (int64_t kk = last[w] > 0 ? last[w] - 1 : 0; kk <= last[w]; ++kk)
+                    mbar_wait(&full[w][int(kk & 1)], uint32_t((kk >> 1) & 1), nullptr);
         return;
     }
 
@@ -189,6 +201,24 @@ __global__ void __launch_bounds__((rope_warps<T>() + 1) * 32, 1) qk_norm_rope_ke
         const float *w = wsh[t < q_tiles ? 0 : 1];
         uint8_t *tb = buf0 + size_t(b) * ROPE_TILE * ROWB;
         uint8_t *row = tb + size_t(lane) * ROWB;
+        // dense [32][ROWBYTES] -> padded [32][ROWB], in place: rows 16..31, then 0..15
+        // (a half's padded range overlaps only dense bytes of that half or of rows
+        // already moved); rows past nvalid move garbage that is never used
+#pragma unroll
+        for (int h = 1; h >= 0; --h) {
+            constexpr int NC = ROPE_TILE / 2 * CPR / 32;         // 16-byte chunks per lane per half
+            uint4 v[NC];
+#pragma unroll
+            for (int i = 0; i < NC; ++i)
+                v[i] = *reinterpret_cast<const uint4 *>(tb + size_t(h * (ROPE_TILE / 2) * CPR + i * 32 + lane) * 16);
+            __syncwarp();
+#pragma unroll
+            for (int i = 0; i < NC; ++i) {
+                const int c = i * 32 + lane, r = h * (ROPE_TILE / 2) + c / CPR;
+                *reinterpret_cast<uint4 *>(tb + size_t(r) * ROWB + (c % CPR) * 16) = v[i];
+            }
+            __syncwarp();
+        }
 
         // ordered sum of squares of head row `lane`
         float acc = 0.0f;
@@ -229,7 +259,10 @@ __global__ void __launch_bounds__((rope_warps<T>() + 1) * 32, 1) qk_norm_rope_ke
         uint8_t *dst = reinterpret_cast<uint8_t *>(base + row0 * HD);
         for (int c = lane; c < nvalid * CPR; c += 32)
             st_cs_v4(dst + size_t(c) * 16, *reinterpret_cast<const uint4 *>(tb + (c / CPR) * ROWB + (c % CPR) * 16));
-        __syncwarp();          // all reads of buffer b done before it is refilled
+        // this warp's shared-memory writes to buffer b are ordered before the bulk copy
+        // (async proxy) that refills it; all reads of it are done
+        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+        __syncwarp();
         if (lane == 0) mbar_arrive(&empty[wid][b]);
     }
 }
