@@ -1383,7 +1383,8 @@ def _dist_init(torch, dist):
     local = int(os.environ.get("LOCAL_RANK", "0"))
     torch.cuda.set_device(local)
     dev = torch.device("cuda", local)
-    if world > 1:
+    if world > 1 and not dist.is_initialized():
+        # once per process: every workload of a multi-workload launch shares the group
         import datetime
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=dev)
     return world, rank, local, dev
@@ -1428,6 +1429,9 @@ def main():
             raise SystemExit(f"unknown workload {name}")
         args.workload = name
         rc = rc or run_one(args)
+    import torch.distributed as dist
+    if dist.is_available() and dist.is_initialized():
+        dist.destroy_process_group()
     return rc
 
 
@@ -1688,8 +1692,6 @@ def run_one(args):
         print(json.dumps(line), flush=True)
 
     q3.close()
-    if world > 1:
-        dist.destroy_process_group()
     return 0
 
 
