@@ -86,6 +86,13 @@ int         q3cu_version(void);
 /* Synchronises `stream`, returns the device status bits in *flags and clears
  * them.  Returns Q3CU_ERR_INDEX / Q3CU_ERR_TIMEOUT when the matching bit is set. */
 q3cu_status q3cu_device_status(q3cu_ctx *ctx, q3cu_stream stream, uint32_t *flags);
+/* Failure-path self-test (no counterpart in the reference): enqueues one CTA
+ * whose threads wait on a shared-memory barrier that nothing completes, with
+ * the same bounded wait the kernels use (about 2 s).  The wait gives up, sets
+ * Q3CU_DEV_TIMEOUT in the status word and the kernel returns; nothing faults
+ * and the context stays usable.  For testing a caller's handling of a
+ * device-side timeout (read it with q3cu_device_status). */
+q3cu_status q3cu_selftest_wait_timeout(q3cu_ctx *ctx, q3cu_stream stream);
 
 /* Validates a checkpoint header (src/cpu/qwen3_original.c:236-244 exits on a bad
  * magic or version; this returns Q3CU_ERR_FORMAT instead). */

@@ -248,6 +248,13 @@ q3cu_status q3cu_destroy(q3cu_ctx *ctx) {
 
 int q3cu_is_initialized(const q3cu_ctx *ctx) { return ctx && ctx->alive ? 1 : 0; }
 
+q3cu_status q3cu_selftest_wait_timeout(q3cu_ctx *ctx, q3cu_stream stream) {
+    CHECK_CTX(ctx);
+    if (q3cu_status st = use_device(ctx)) return st;
+    return launched(q3::launch_selftest_wait(ctx->d_status, static_cast<cudaStream_t>(stream)),
+                    "wait-timeout self-test launch");
+}
+
 q3cu_status q3cu_device_status(q3cu_ctx *ctx, q3cu_stream stream, uint32_t *flags) {
     CHECK_CTX(ctx);
     q3cu_status st = use_device(ctx);

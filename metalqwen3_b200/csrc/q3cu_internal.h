@@ -42,6 +42,10 @@ cudaError_t launch_dependent(void (*kernel)(KArgs...), dim3 grid, dim3 block, si
     return cudaLaunchKernelEx(&cfg, kernel, static_cast<KArgs>(args)...);
 }
 
+// The failure-path self-test: one CTA whose bounded wait on a barrier that
+// nothing completes gives up and sets Q3CU_DEV_TIMEOUT in `status`.
+cudaError_t launch_selftest_wait(uint32_t *status, cudaStream_t stream);
+
 // Every launcher enqueues on `stream`, allocates nothing and returns the
 // launch error.  `sms` is the device's multiprocessor count (grid sizing).
 cudaError_t launch_quantize_q8(const void *x, q3cu_dtype dt, int64_t elems, int8_t *q, float *s,

@@ -54,6 +54,7 @@ def load_library(path: str = LIB_PATH) -> C.CDLL:
                 "q3cu_status_string": (C.c_char_p, [st]),
                 "q3cu_version": (i32, []),
                 "q3cu_device_status": (st, [vp, vp, C.POINTER(C.c_uint32)]),
+                "q3cu_selftest_wait_timeout": (st, [vp, vp]),
                 "q3cu_check_header": (st, [vp, C.c_size_t, vp]),
                 "q3cu_rmsnorm": (st, [vp, vp, i32, vp, i64, i32, f32, vp, vp]),
                 "q3cu_rmsnorm_q8": (st, [vp, vp, i32, vp, i64, i32, f32, vp, vp, vp]),
@@ -138,6 +139,11 @@ class Q3CU:
             self.close()
         except Exception:
             pass
+
+    def selftest_wait_timeout(self, stream=None) -> None:
+        """Enqueue the failure-path self-test: a kernel whose bounded wait gives
+        up (about 2 s) and sets the timeout bit; read it with device_status()."""
+        self._check(self.lib.q3cu_selftest_wait_timeout(self.ctx, self._stream(stream)), "q3cu_selftest_wait_timeout")
 
     def device_status(self, stream=None) -> int:
         flags = C.c_uint32(0)
