@@ -1,7 +1,7 @@
 /*
  * ref_rows.c -- row-batched, multi-threaded driver of the reference CPU engine.
  *
- * TEST/BASELINE INFRASTRUCTURE ONLY: used by the CPU-baseline and reference
+ * TEST AND CPU-BASELINE INFRASTRUCTURE ONLY: used by the CPU-baseline and reference
  * legs of bench.py to time the reference's own code on the host cores.
  *
  * Linked against oracle/_ref/libqwen3_ref.so, i.e. src/cpu/qwen3_original.c

@@ -117,7 +117,8 @@ int main() {
 
 def test_engine_call_sites_compile(tmp_path):
     """Every backend call of the reference engine compiles against CudaContext
-    unchanged apart from the type name (the drop-in claim of INTEGRATION.md)."""
+    unchanged apart from the type name (the drop-in claim: only the member's
+    type and the header change on the engine side)."""
     import subprocess
     from metalqwen3_b200.build import library_path
     src = tmp_path / "engine_calls.cpp"
