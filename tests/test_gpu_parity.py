@@ -225,6 +225,9 @@ def test_qk_norm_only_is_bitexact_at_pos0(q3, oracle):
 
 @pytest.mark.parametrize("rows,nh", [(7, 32), (256, 32)])
 def test_qk_norm_rope_bf16(q3, oracle, rows, nh):
+    """bf16 head rows at positions up to 32767: 1e-2 relative, plus 1e-6
+    absolute for outputs that cancel to near zero (the device sincosf is a few
+    ulps from the host's cosf/sinf, which is no relative bound at |o| ~ 0)."""
     rng = np.random.default_rng(rows)
     qh = to_bf16(rng.standard_normal((rows, nh, 128), dtype=np.float32), oracle)
     kh = to_bf16(rng.standard_normal((rows, 8, 128), dtype=np.float32), oracle)
@@ -234,8 +237,8 @@ def test_qk_norm_rope_bf16(q3, oracle, rows, nh):
     tq, tk = dev(qh), dev(kh)
     q3.qk_norm_rope(tq, tk, dev(pos), dev(qn), dev(kn))
     qo, ko = oracle.rows_qk_norm_rope(qh, kh, pos, qn, kn)
-    np.testing.assert_allclose(bf16_to_f32(host(tq)), bf16_to_f32(qo), rtol=BF16_RTOL, atol=1e-2)
-    np.testing.assert_allclose(bf16_to_f32(host(tk)), bf16_to_f32(ko), rtol=BF16_RTOL, atol=1e-2)
+    np.testing.assert_allclose(bf16_to_f32(host(tq)), bf16_to_f32(qo), rtol=BF16_RTOL, atol=1e-6)
+    np.testing.assert_allclose(bf16_to_f32(host(tk)), bf16_to_f32(ko), rtol=BF16_RTOL, atol=1e-6)
 
 
 # --------------------------------------------------------------------------- swiglu
