@@ -35,9 +35,9 @@
 //            memory as two tensor stores (plain stores when d % 4 != 0).
 // Measured on the 4096 x 2560 -> 9728 product (Qwen3-4B W1 of a 4096-token
 // prefill): ~480 us.  The fold issues ~190 instructions per warp and group
-// (issue ~70% busy), and each group's accumulator makes a round trip fold ->
-// MMA -> fold through four tensor-memory buffers, which with the ~4 us latency
-// of a 32 KB TMA stage under this load leaves the tensor pipe ~12% busy.
+// (issue ~70% busy), each group's accumulator makes a round trip fold -> MMA
+// -> fold through four tensor-memory buffers, and the MMA thread still waits
+// ~500-650 cycles per stage for its operands: the tensor pipe is ~12% busy.
 // Each group's first MMA overwrites its accumulator (the second adds to it),
 // so no accumulator needs clearing; the fold converts the int32 dot to float
 // exactly (|dot| <= 64 * 128 * 128 < 2^24).
