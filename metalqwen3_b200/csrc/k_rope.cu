@@ -220,16 +220,31 @@ __global__ void __launch_bounds__((rope_warps<T>() + 1) * 32, 1) qk_norm_rope_ke
             __syncwarp();
         }
 
-        // ordered sum of squares of head row `lane`
+        // ordered sum of squares of head row `lane`: batches of 8 16-byte vectors,
+        // the next batch loaded while this one is added (two register sets
+        // alternate), so the chain runs at the add latency
         float acc = 0.0f;
         if (lane < nvalid) {
+            constexpr int NV = HD / V, BT = 8, NBT = NV / BT;
             const uint4 *p4 = reinterpret_cast<const uint4 *>(row);
+            uint4 buf[2][BT];
 #pragma unroll
-            for (int c = 0; c < HD / V; ++c) {
-                float v[V];
-                Vec<T>::widen(p4[c], v);
+            for (int j = 0; j < BT; ++j) buf[0][j] = p4[j];
 #pragma unroll
-                for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, __fmul_rn(v[i], v[i]));
+            for (int bt = 0; bt < NBT; ++bt) {
+                if (bt + 1 < NBT) {
+#pragma unroll
+                    for (int j = 0; j < BT; ++j) buf[(bt + 1) & 1][j] = p4[(bt + 1) * BT + j];
+                }
+#pragma unroll
+                for (int j = 0; j < BT; ++j) {
+                    float v[V], sq[V];
+                    Vec<T>::widen(buf[bt & 1][j], v);
+#pragma unroll
+                    for (int i = 0; i < V; i += 2) up2(mul2(pk2(v[i], v[i + 1]), pk2(v[i], v[i + 1])), sq[i], sq[i + 1]);
+#pragma unroll
+                    for (int i = 0; i < V; ++i) acc = __fadd_rn(acc, sq[i]);     // in index order
+                }
             }
         }
         const float ss = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, float(HD)), eps)));
