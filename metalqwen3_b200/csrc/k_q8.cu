@@ -107,44 +107,57 @@ __global__ void __launch_bounds__(256) embed_gather_kernel(const int8_t *__restr
         }
         const int8_t *row = tq + int64_t(t) * dim;
         const float *srow = ts + int64_t(t) * (dim / GS);
-        for (int st = 0; st <= steps; ++st) {
-            const bool full = st < steps;
-            if (!full && rem16 == 0) break;
-            const bool act = full || lane < rem16;
-            const int e = st * 512 + lane * 16;        // element index of this lane
-            uint4 c = make_uint4(0, 0, 0, 0);
-            float sc = 0.0f;
-            if (act) {
-                c = ld_nc_v4(row + e);
-                sc = __ldg(srow + e / GS);
-            }
-            const uint32_t w[4] = {c.x, c.y, c.z, c.w};
-            float v[16];
+        const int nst = steps + (rem16 > 0 ? 1 : 0);    // warp steps of the row, the tail included
+        // The codes and scales of EB steps are requested together, so the row's
+        // loads wait out one latency per EB steps, not one per step.
+        constexpr int EB = 4;
+        for (int st0 = 0; st0 < nst; st0 += EB) {
+            uint4 cb[EB];
+            float sb[EB];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                v[4 * k + 0] = __fmul_rn((float)(int8_t)(w[k] & 0xff), sc);
-                v[4 * k + 1] = __fmul_rn((float)(int8_t)((w[k] >> 8) & 0xff), sc);
-                v[4 * k + 2] = __fmul_rn((float)(int8_t)((w[k] >> 16) & 0xff), sc);
-                v[4 * k + 3] = __fmul_rn((float)(int8_t)(w[k] >> 24), sc);
+            for (int u = 0; u < EB; ++u) {
+                const int st = st0 + u;
+                const bool act = st < steps || (st == steps && lane < rem16);
+                const int e = st * 512 + lane * 16;
+                cb[u] = act ? ld_nc_v4(row + e) : make_uint4(0, 0, 0, 0);
+                sb[u] = act ? __ldg(srow + e / GS) : 0.0f;
             }
-            if (F32 && act) {
-                float *op = out + i * dim + e;
 #pragma unroll
-                for (int k = 0; k < 4; ++k)
-                    st_cs_v4(op + 4 * k, make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
-                                                     __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3])));
-            }
-            if (Q8) {
-                float m = 0.0f;
+            for (int u = 0; u < EB; ++u) {
+                const int st = st0 + u;
+                if (st >= nst) break;                  // warp-uniform
+                const bool full = st < steps;
+                const bool act = full || lane < rem16;
+                const int e = st * 512 + lane * 16;    // element index of this lane
+                const uint32_t w[4] = {cb[u].x, cb[u].y, cb[u].z, cb[u].w};
+                const float sc = sb[u];
+                float v[16];
 #pragma unroll
-                for (int k = 0; k < 16; ++k) m = amax_fold(m, v[k]);
-                m = amax_merge(m, __shfl_xor_sync(FULL, m, 1));
-                m = amax_merge(m, __shfl_xor_sync(FULL, m, 2));
-                if (act) {
-                    const Q8Scale gs = q8_prepare(m);
-                    st_cs_v4(oq + i * dim + e,
-                             make_uint4(q8_pack4(v, gs), q8_pack4(v + 4, gs), q8_pack4(v + 8, gs), q8_pack4(v + 12, gs)));
-                    if ((lane & 3) == 0) st_cs_f32(os + i * (dim / GS) + e / GS, gs.scale);
+                for (int k = 0; k < 4; ++k) {
+                    v[4 * k + 0] = __fmul_rn((float)(int8_t)(w[k] & 0xff), sc);
+                    v[4 * k + 1] = __fmul_rn((float)(int8_t)((w[k] >> 8) & 0xff), sc);
+                    v[4 * k + 2] = __fmul_rn((float)(int8_t)((w[k] >> 16) & 0xff), sc);
+                    v[4 * k + 3] = __fmul_rn((float)(int8_t)(w[k] >> 24), sc);
+                }
+                if (F32 && act) {
+                    float *op = out + i * dim + e;
+#pragma unroll
+                    for (int k = 0; k < 4; ++k)
+                        st_cs_v4(op + 4 * k, make_uint4(__float_as_uint(v[4 * k]), __float_as_uint(v[4 * k + 1]),
+                                                         __float_as_uint(v[4 * k + 2]), __float_as_uint(v[4 * k + 3])));
+                }
+                if (Q8) {
+                    float m = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 16; ++k) m = amax_fold(m, v[k]);
+                    m = amax_merge(m, __shfl_xor_sync(FULL, m, 1));
+                    m = amax_merge(m, __shfl_xor_sync(FULL, m, 2));
+                    if (act) {
+                        const Q8Scale gs = q8_prepare(m);
+                        st_cs_v4(oq + i * dim + e, make_uint4(q8_pack4(v, gs), q8_pack4(v + 4, gs),
+                                                              q8_pack4(v + 8, gs), q8_pack4(v + 12, gs)));
+                        if ((lane & 3) == 0) st_cs_f32(os + i * (dim / GS) + e / GS, gs.scale);
+                    }
                 }
             }
         }
