@@ -809,8 +809,13 @@ static cudaError_t launch_rms_t(const T *x, const float *w, int64_t rows, int di
     // same number per SM), L odd lines per stage.  With one block per SM the
     // pass cannot overlap anything, and the persistent kernel below, which
     // normalises the block's last chunks straight from its ring, measured
-    // faster (4096 x 2560 f32: 28.9 against 36 us).
-    if (rows_per_sm > RMS_MAXR && row_bytes % 128 == 0 && reinterpret_cast<uintptr_t>(x) % 32 == 0 &&
+    // faster (4096 x 2560 f32: 28.9 against 36 us).  For f32 rows the ring
+    // kernel also wins up to two blocks per SM (8192 x 2560: 47.1 against
+    // 51.2 us; 20011 x 1024, 135 rows per SM: the same); bf16 rows stream at
+    // half the bytes per chain element and take the TMA kernel (16384 x 5120:
+    // 135 against 166 us).
+    if (rows_per_sm > RMS_MAXR && (sizeof(T) == 2 || rows_per_sm > 2 * RMS_MAXR) && row_bytes % 128 == 0 &&
+        reinterpret_cast<uintptr_t>(x) % 32 == 0 &&
         (Q8 ? reinterpret_cast<uintptr_t>(q) % 16 == 0 : reinterpret_cast<uintptr_t>(out) % 16 == 0)) {
         const int64_t bps2 = (rows_per_sm + RT_MAXR - 1) / RT_MAXR;
         const int R2 = int((rows_per_sm + bps2 - 1) / bps2);

@@ -137,7 +137,8 @@ def test_rmsnorm_q8_f32(q3, oracle, rows, dim):
 
 
 @pytest.mark.parametrize("rows,dim,bf16", [
-    (8192, 2560, False),      # TMA-fed kernel: blocks of 56 rows, two chain warps
+    (8192, 2560, False),      # persistent ring kernel: 2 blocks of 28 rows per SM (f32 below 65 rows per SM)
+    (12000, 2560, False),     # TMA-fed, f32: 82 rows per SM, blocks of 41 rows, two chain warps
     (20011, 1024, False),     # TMA-fed: 2-3 blocks per SM (double-buffered row scales), a 1-row last block
     (1000, 2560, False),      # persistent ring kernel: 7 rows per SM
     (5000, 4096, True),       # TMA-fed, bf16, blocks of 34 rows
