@@ -148,6 +148,8 @@ __global__ void __launch_bounds__(RMS_THREADS, 1) rmsnorm_kernel(const T *x, con
         fail_sh = 0;
     }
     __syncthreads();
+    griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
+    griddep_wait();                               // x from the kernel before (a dependent launch)
 
     auto block_rows = [&](int k, int64_t &r0, int &rv) {
         const int64_t b = blockIdx.x + int64_t(k) * gridDim.x;
@@ -627,6 +629,8 @@ __global__ void __launch_bounds__(RT_THREADS, 1) rmsnorm_tma_kernel(const __grid
         fail_sh = 0;
     }
     __syncthreads();
+    griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
+    griddep_wait();                               // x from the kernel before (a dependent launch)
 
     auto block_rows = [&](int k, int64_t &r0, int &rv) {
         const int64_t b = blockIdx.x + int64_t(k) * gridDim.x;
@@ -831,16 +835,15 @@ static cudaError_t launch_rms_t(const T *x, const float *w, int64_t rows, int di
             cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(rmsnorm_tma_kernel<T, Q8>), RT_SMEM, tslot);
             if (e != cudaSuccess) return e;
             const unsigned g2 = unsigned(nb2 < sms ? nb2 : sms);
-            rmsnorm_tma_kernel<T, Q8><<<g2, RT_THREADS, RT_SMEM, stream>>>(map, x, w, rows, dim, n_div, eps, R2, L,
-                                                                          stage_b, out, q, s, status);
-            return cudaGetLastError();
+            return launch_dependent(rmsnorm_tma_kernel<T, Q8>, dim3(g2), dim3(RT_THREADS), RT_SMEM, stream, map, x, w,
+                                    rows, dim, n_div, eps, R2, L, stage_b, out, q, s, status);
         }
     }
     const int slot = 2 + (sizeof(T) == 4 ? 0 : 2) + (Q8 ? 1 : 0);
     cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(rmsnorm_kernel<T, Q8>), RMS_SMEM, slot);
     if (e != cudaSuccess) return e;
-    rmsnorm_kernel<T, Q8><<<grid, RMS_THREADS, RMS_SMEM, stream>>>(x, w, rows, dim, n_div, eps, R, out, q, s, status);
-    return cudaGetLastError();
+    return launch_dependent(rmsnorm_kernel<T, Q8>, dim3(grid), dim3(RMS_THREADS), RMS_SMEM, stream, x, w, rows, dim,
+                            n_div, eps, R, out, q, s, status);
 }
 
 cudaError_t launch_rmsnorm(const void *x, q3cu_dtype dt, const float *w, int64_t rows, int dim, float eps, void *out,

@@ -109,6 +109,8 @@ __global__ void __launch_bounds__((rope_warps<T>() + 1) * 32, 1) qk_norm_rope_ke
         mbar_init_fence();
     }
     __syncthreads();
+    griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
+    griddep_wait();                               // q / k from the kernel before (a dependent launch)
 
     const int64_t q_tiles = (q_rows + ROPE_TILE - 1) / ROPE_TILE;
     const int64_t k_tiles = (k_rows + ROPE_TILE - 1) / ROPE_TILE;
@@ -295,9 +297,8 @@ static cudaError_t launch_rope_t(T *q, T *k, const int32_t *pos, int64_t rows, i
     const int64_t tiles = (qr + ROPE_TILE - 1) / ROPE_TILE + (kr + ROPE_TILE - 1) / ROPE_TILE;
     int64_t blocks = (tiles + RW - 1) / RW;                      // one CTA per SM (shared memory)
     if (blocks > sms) blocks = sms;
-    qk_norm_rope_kernel<T><<<unsigned(blocks), (RW + 1) * 32, SMEM, stream>>>(q, k, pos, qr, kr, nh, nkv, qn, kn,
-                                                                            invf, eps, status);
-    return cudaGetLastError();
+    return launch_dependent(qk_norm_rope_kernel<T>, dim3(unsigned(blocks)), dim3((RW + 1) * 32), SMEM, stream, q, k,
+                            pos, qr, kr, nh, nkv, qn, kn, invf, eps, status);
 }
 
 cudaError_t launch_qk_norm_rope(void *q, void *k, q3cu_dtype dt, const int32_t *pos, int64_t rows, int n_heads,

@@ -223,6 +223,8 @@ __global__ void __launch_bounds__(SW_WARPS * 32, 1) swiglu_ring_kernel(const T *
         for (int k = 0; k < SW_K; ++k) mbar_init(&bar[warp][k], 1);
     mbar_init_fence();
     __syncthreads();                                         // (also: the exp table)
+    griddep_launch_dependents();                  // a dependent-launched successor may start its own prologue
+    griddep_wait();                               // hb / hb2 from the kernel before (a dependent launch)
 
     const int64_t nch = (elems + CE - 1) / CE;
     const int64_t gw = int64_t(blockIdx.x) * SW_WARPS + warp, nw = int64_t(gridDim.x) * SW_WARPS;
@@ -312,8 +314,8 @@ static cudaError_t launch_swiglu_t(const T *hb, const T *hb2, int64_t elems, T *
         const size_t smem = SW_RING + (sizeof(T) == 2 ? sizeof(GateTab) : 0);
         cudaError_t e = ensure_smem_attr(reinterpret_cast<const void *>(swiglu_ring_kernel<T, Q8>), smem, slot);
         if (e != cudaSuccess) return e;
-        swiglu_ring_kernel<T, Q8><<<sms, SW_WARPS * 32, smem, stream>>>(hb, hb2, elems, out, q, s, status);
-        return cudaGetLastError();
+        return launch_dependent(swiglu_ring_kernel<T, Q8>, dim3(sms), dim3(SW_WARPS * 32), smem, stream, hb, hb2,
+                                elems, out, q, s, status);
     }
     const bool v8 = (elems % Wide<T>::N) == 0 && (reinterpret_cast<uintptr_t>(hb) % 32) == 0 &&
                     (reinterpret_cast<uintptr_t>(hb2) % 32) == 0 &&
