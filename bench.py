@@ -48,7 +48,9 @@ E2E_CHUNKS = 8          # token-row chunks of the pipelined end-to-end step
 # outputs with the oracle (oracle/, the CPU restatement of the reference pinned
 # to it by the tests) applied to that step's inputs: mismatch counts go on the
 # JSON line.  Inputs that the step updates in place are snapshotted (a few rows)
-# between the last two timed steps, outside the timed events.
+# between the last two timed steps, outside the timed events.  For prefill4b and
+# matmul4b the same check also runs on the end-to-end path (`e2e.parity`): the
+# pinned host outputs of its last step against the pinned host inputs.
 RTOL, ATOL, BF16_RTOL = 1e-5, 1e-6, 1e-2
 
 
@@ -105,6 +107,10 @@ class Workload:
     dtype = "f32"
     e2e_note = ""
     scaling = "weak"
+    # True where the tensors copied in and out by the end-to-end step carry the
+    # names the parity check reads, so the checker also runs on the host
+    # outputs of the last end-to-end step.
+    e2e_parity = False
 
     def kernels(self):              # [(name, algorithmic bytes per launch)]
         raise NotImplementedError
@@ -116,6 +122,7 @@ class Workload:
 class Prefill4B(Workload):
     """Qwen3-4B-shaped prefill layer kernels, fp32, T tokens."""
     name = "prefill4b"
+    e2e_parity = True
 
     def __init__(self, tokens=4096, dim=2560, nh=32, nkv=8, hd=128, hidden=9728):
         self.tokens, self.dim, self.nh, self.nkv, self.hd, self.hidden = tokens, dim, nh, nkv, hd, hidden
@@ -868,6 +875,7 @@ class Matmul4B(Workload):
     name = "matmul4b"
     dtype = "int8 codes (tcgen05 int8 MMA, exact int32) -> f32"
     bound = "tensor"
+    e2e_parity = True
 
     def __init__(self, tokens=4096, n=2560, d=9728):
         self.tokens, self.n, self.d = tokens, n, d
@@ -1627,6 +1635,13 @@ def run_one(args):
         e2e_ms = float(t.item())
         barrier()
     e2e_all_bytes = float(e2e_b.item())
+    # The checker on the end-to-end path: the pinned host outputs of the last
+    # end-to-end step against the oracle applied to the pinned host inputs.
+    e2e_check = None
+    if rank == 0 and parity is not None and wl.e2e_parity:
+        from oracle.oracle import Oracle
+        d_in = dict(d, **hin)
+        e2e_check = wl.parity(Oracle(), wl.parity_snapshot(d_in), dict(d_in, **hout), q3)
 
     # ---- report ---------------------------------------------------------------
     if rank == 0:
@@ -1679,7 +1694,8 @@ def run_one(args):
                     "ms_per_step": round(e2e_ms / args.e2e_steps, 3),
                     "path": ("pinned host inputs -> cudaMemcpyAsync H2D -> q3cu C ABI kernels -> D2H, per step"
                              + (f", pipelined over {E2E_CHUNKS} token-row chunks on four streams (two copy-in, "
-                                "kernels, copy-out)" if chunks else "") + (f"; {wl.e2e_note}" if wl.e2e_note else ""))},
+                                "kernels, copy-out)" if chunks else "") + (f"; {wl.e2e_note}" if wl.e2e_note else "")),
+                    **({"parity": e2e_check} if e2e_check is not None else {})},
             "gpu_launches": launches,
             "clocks": clk,
         }

@@ -65,6 +65,30 @@ def test_parity_checker_counts_planted_mistakes(oracle):
     assert (r["rmsnorm_q8"], r["swiglu_q8"], r["qk_norm_rope"]) == (1, 1, 1)
 
 
+def test_end_to_end_checker_reads_the_host_buffers(oracle):
+    """The end-to-end check as bench.py composes it: inputs from the host
+    copies (q and k are rotated in place on the device, so the device tensors
+    no longer hold them), outputs from the host copies of the results."""
+    import torch
+    import bench
+    wl = bench.Prefill4B(tokens=40)
+    assert wl.e2e_parity and bench.Matmul4B.e2e_parity and not bench.Decode8B.e2e_parity
+    d = wl.make(torch, torch.device("cpu"), seed=2)
+    hin = {k: d[k].clone() for k in wl.h2d_keys}
+    qo, ko = _prefill_outputs(wl, d, oracle)
+    d["q"].copy_(torch.from_numpy(qo)); d["k"].copy_(torch.from_numpy(ko))
+    hout = {k: d[k].clone() for k in wl.d2h_keys}
+    d["q"].add_(1.0)                                      # the device tensors moved on after the last step
+    d["xq"].zero_()
+    d_in = dict(d, **hin)
+    r = wl.parity(oracle, wl.parity_snapshot(d_in), dict(d_in, **hout))
+    assert (r["rmsnorm_q8"], r["qk_norm_rope"], r["swiglu_q8"]) == (0, 0, 0)
+    row = int(wl.parity_snapshot(d_in)["rows"][2])
+    hout["hq"][row, 7] += 1                               # one wrong code in the host output
+    r = wl.parity(oracle, wl.parity_snapshot(d_in), dict(d_in, **hout))
+    assert r["swiglu_q8"] == 1
+
+
 def test_softmax_checker(oracle):
     import bench
     rng = np.random.default_rng(0)
