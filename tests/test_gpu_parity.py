@@ -191,6 +191,51 @@ def test_rmsnorm_rejects_bad_shapes(q3):
     assert e.value.status == 2                       # ERR_ALIGN (row bytes not a multiple of 16)
 
 
+@pytest.mark.parametrize("rows", [4096, 12000])
+def test_prefill_kernels_chained_on_one_stream(q3, oracle, rows):
+    """The prefill kernels are programmatic dependent launches: each may start
+    before the kernel ahead of it has finished, and must wait for it before
+    touching memory.  Each op here reads what the launch just before it wrote,
+    with no synchronisation in between (4096 rows: the RMSNorm ring kernel,
+    12000: the TMA-fed one)."""
+    import torch
+    rng = np.random.default_rng(rows + 7)
+    dim, hidden, nh, nkv = 2560, 9728, 32, 8
+    x = activations(rng, rows, dim)
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    w2 = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    qh = rng.standard_normal((rows, nh, 128), dtype=np.float32)
+    kh = rng.standard_normal((rows, nkv, 128), dtype=np.float32)
+    pos = (np.arange(rows) % 4096).astype(np.int32)
+    qn = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    kn = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    hb = activations(rng, 4096, hidden)
+    hb2 = rng.standard_normal((4096, hidden)).astype(np.float32)
+    tx, tw, tw2, tq, tk, tp, tqn, tkn = (dev(a) for a in (x, w, w2, qh, kh, pos, qn, kn))
+    thb, thb2 = dev(hb), dev(hb2)
+    torch.cuda.synchronize()
+    y = q3.rmsnorm(tx, tw)                        # RMSNorm -> y, then RMSNorm+Q8_0 of y
+    qg, sg = q3.rmsnorm_q8(y, tw2)
+    q3.qk_norm_rope(tq, tk, tp, tqn, tkn)         # twice in place
+    q3.qk_norm_rope(tq, tk, tp, tqn, tkn)
+    q3.swiglu(thb, thb2)                          # SwiGLU in place, then SwiGLU+Q8_0 of its output
+    hq, hs = q3.swiglu_q8(thb, thb2)
+    torch.cuda.synchronize()
+    yo = oracle.rows_rmsnorm(x, w, threads=8)
+    assert np.array_equal(bits(host(y)), bits(yo))
+    qo, so = oracle.rows_rmsnorm_q8(yo, w2, threads=8)
+    assert_q8_equal(qg, sg, qo, so)
+    q1, k1 = oracle.rows_qk_norm_rope(qh, kh, pos, qn, kn, threads=8)
+    q2, k2 = oracle.rows_qk_norm_rope(q1, k1, pos, qn, kn, threads=8)
+    np.testing.assert_allclose(host(tq), q2, rtol=RTOL, atol=ATOL)
+    np.testing.assert_allclose(host(tk), k2, rtol=RTOL, atol=ATOL)
+    ho = oracle.rows_swiglu(hb, hb2, threads=8)
+    assert np.array_equal(bits(host(thb)), bits(ho))
+    hqo, hso = oracle.rows_swiglu_q8(ho, hb2, threads=8)
+    assert_q8_equal(hq, hs, hqo, hso)
+    assert q3.device_status() == 0
+
+
 # --------------------------------------------------------------------------- qk-norm + rope
 @pytest.mark.parametrize("rows,nh,nkv,posmax", [(1, 16, 8, 37), (5, 32, 8, 4096), (4096, 32, 8, 4096), (64, 40, 8, 32768)])
 def test_qk_norm_rope_f32(q3, oracle, rows, nh, nkv, posmax):
