@@ -44,7 +44,7 @@ E2E_CHUNKS = 8          # token-row chunks of the pipelined end-to-end step
 
 
 # ---------------------------------------------------------------------------- parity helpers
-# After timing, the checker leg compares a sample of the last timed step's
+# After timing, the parity check compares a sample of the last timed step's
 # outputs with the oracle (oracle/, the CPU restatement of the reference pinned
 # to it by the tests) applied to that step's inputs: mismatch counts go on the
 # JSON line.  Inputs that the step updates in place are snapshotted (a few rows)
@@ -108,7 +108,7 @@ class Workload:
     e2e_note = ""
     scaling = "weak"
     # True where the tensors copied in and out by the end-to-end step carry the
-    # names the parity check reads, so the checker also runs on the host
+    # names the parity check reads, so the check also runs on the host
     # outputs of the last end-to-end step.
     e2e_parity = False
 
@@ -1537,7 +1537,7 @@ def run_one(args):
         raise RuntimeError("device status set during the timed region")
     parity = None
     if rank == 0 and hasattr(wl, "parity"):
-        # the checker: a sample of the last timed step against the oracle
+        # the parity check: a sample of the last timed step against the oracle
         from oracle.oracle import Oracle
         parity = {"checked": "last timed step (sampled rows) vs the oracle on the same inputs; counts of "
                              "mismatching values (bit-exact ops) or of values outside the tolerance (RoPE, softmax)",
@@ -1635,7 +1635,7 @@ def run_one(args):
         e2e_ms = float(t.item())
         barrier()
     e2e_all_bytes = float(e2e_b.item())
-    # The checker on the end-to-end path: the pinned host outputs of the last
+    # The parity check on the end-to-end path: the pinned host outputs of the last
     # end-to-end step against the oracle applied to the pinned host inputs.
     e2e_check = None
     if rank == 0 and parity is not None and wl.e2e_parity:

@@ -10,7 +10,7 @@ Two libraries are exposed:
   Present only where the reference sources were available at build time.
 
 Only tests/, ``__graft_entry__.smoke()`` and the CPU-baseline leg of
-``bench.py`` may import this module, and only as the checker.
+``bench.py`` may import this module, and only to check results against it.
 """
 from __future__ import annotations
 

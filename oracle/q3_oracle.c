@@ -1,7 +1,7 @@
 /*
  * q3_oracle.c -- CPU oracle for the fused Qwen3 layer kernels.
  *
- * TEST INFRASTRUCTURE ONLY: the checker for the CUDA library and the timed CPU
+ * TEST INFRASTRUCTURE ONLY: the reference results the CUDA library is tested against, and the timed CPU
  * baseline.  Never linked into, loaded by or called from the product.
  *
  * Plain-C restatement of src/cpu/qwen3_original.c (the reference's CPU engine).

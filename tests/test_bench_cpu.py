@@ -1,5 +1,5 @@
 """bench.py's host logic on CPU: the strong-scaling shards of the configurations
-that split over GPUs, the checker that compares a timed step's outputs with the
+that split over GPUs, the parity check that compares a timed step's outputs with the
 oracle (a mistake planted in the outputs must be counted), and the reference
 arm's JSON line."""
 import json
@@ -47,7 +47,7 @@ def _prefill_outputs(wl, d, oracle):
     return qo, ko
 
 
-def test_parity_checker_counts_planted_mistakes(oracle):
+def test_parity_check_counts_planted_mistakes(oracle):
     import torch
     import bench
     wl = bench.Prefill4B(tokens=40)
@@ -65,7 +65,7 @@ def test_parity_checker_counts_planted_mistakes(oracle):
     assert (r["rmsnorm_q8"], r["swiglu_q8"], r["qk_norm_rope"]) == (1, 1, 1)
 
 
-def test_end_to_end_checker_reads_the_host_buffers(oracle):
+def test_end_to_end_parity_check_reads_the_host_buffers(oracle):
     """The end-to-end check as bench.py composes it: inputs from the host
     copies (q and k are rotated in place on the device, so the device tensors
     no longer hold them), outputs from the host copies of the results."""
@@ -89,7 +89,7 @@ def test_end_to_end_checker_reads_the_host_buffers(oracle):
     assert r["swiglu_q8"] == 1
 
 
-def test_softmax_checker(oracle):
+def test_softmax_parity_check(oracle):
     import bench
     rng = np.random.default_rng(0)
     lens = [1, 38, 700, 4097]
@@ -101,7 +101,7 @@ def test_softmax_checker(oracle):
     assert bench._softmax_mismatch(g, x, lens) == 1
 
 
-def test_embed_checker(oracle):
+def test_embed_parity_check(oracle):
     import torch
     import bench
     wl = bench.Embed(tokens=200, vocab=500, dim=128)
