@@ -177,6 +177,42 @@ def test_rmsnorm_bf16(q3, oracle, rows, dim):
     assert np.array_equal(g, o)      # the float result is exact, so is its bf16 rounding
 
 
+@pytest.mark.parametrize("dim", [1024, 4096])
+def test_rmsnorm_bf16_tiny_values(q3, oracle, dim):
+    """bf16 rows of the few-row kernel fold each square with a fused
+    multiply-add, which equals the reference's square-then-add only while the
+    square is exact in binary32 (|v| >= 2^-63 or v == 0).  Rows holding
+    smaller values must be folded the reference's way: all-tiny rows (where
+    the two chains really differ), a few tiny values among normal ones, bf16
+    subnormals, values on both sides of 2^-63, and exact zeros."""
+    rng = np.random.default_rng(dim + 3)
+    rows = []
+    for scale in (2.0 ** -70, 2.0 ** -66, 2.0 ** -63):             # whole rows of tiny values
+        rows.append(rng.standard_normal(dim).astype(np.float32) * np.float32(scale))
+    r = rng.standard_normal(dim).astype(np.float32)                 # a few tiny values among normal ones
+    r[rng.choice(dim, 5, replace=False)] *= np.float32(2.0 ** -80)
+    rows.append(r)
+    r = rng.standard_normal(dim).astype(np.float32) * np.float32(2.0 ** -64)
+    r[: dim // 2] = rng.standard_normal(dim // 2).astype(np.float32)  # tiny tail after a normal head
+    rows.append(r)
+    r = rng.standard_normal(dim).astype(np.float32) * np.float32(2.0 ** -130)   # bf16 subnormals
+    rows.append(r)
+    r = np.where(rng.random(dim) < 0.5, np.float32(2.0 ** -63), np.float32(-(2.0 ** -63) * 0.99))
+    rows.append(r.astype(np.float32))                              # both sides of 2^-63
+    r = rng.standard_normal(dim).astype(np.float32)
+    r[rng.random(dim) < 0.3] = 0.0                                  # exact zeros only: no fallback needed
+    rows.append(r)
+    xb = to_bf16(np.stack(rows), oracle)
+    w = (1 + 0.1 * rng.standard_normal(dim)).astype(np.float32)
+    qg, sg = q3.rmsnorm_q8(dev(xb), dev(w))
+    qo, so = oracle.rows_rmsnorm_q8(xb, w)
+    assert_q8_equal(qg, sg, qo, so)
+    g = host(q3.rmsnorm(dev(xb), dev(w)))
+    o = oracle.rows_rmsnorm(xb, w)
+    assert np.array_equal(g, o)
+    assert q3.device_status() == 0
+
+
 def test_rmsnorm_rejects_bad_shapes(q3):
     import torch
     from metalqwen3_b200.q3cu import Q3Error
