@@ -1,7 +1,9 @@
-"""Checks of the fast arithmetic used by the Q8_0 epilogues and SwiGLU.
+"""Checks of the fast arithmetic used by the Q8_0 epilogues, SwiGLU and RMSNorm.
 
 * Q8_0 scale RN(wmax/127) by a Markstein correction step == IEEE division
   for every binary32 wmax in [2^-100, 2^100]  (CPU, exhaustive, fmaf);
+* the bf16 RMSNorm chain's fused square: every bf16 value whose square is
+  not exact in binary32 is caught by the kernel's guard (CPU, exhaustive);
 * on the GPU (tests/native/check_device_math.cu, built with nvcc):
   the Markstein reciprocal == __frcp_rn for every binary32 d >= 1 (two
   steps) and every d in [1, 2^120) (one step); softmax's binary32 exp within
@@ -49,6 +51,28 @@ def test_scale_div127_exhaustive():
         subprocess.run(["gcc", "-O2", "-fopenmp", "-ffp-contract=off", src, "-o", exe, "-lm"], check=True)
         bad = int(subprocess.run([exe], check=True, capture_output=True, text=True).stdout.split()[0])
     assert bad == 0
+
+
+def test_bf16_fused_square_guard_exhaustive():
+    """The few-row RMSNorm kernel folds a bf16 row's squares as fma(v, v, acc),
+    which rounds acc + v*v once where the reference rounds v*v and then the sum:
+    the same bits whenever v*v is exact in binary32.  Over all 65,536 bf16
+    values: every value whose square is not exact is caught by the kernel's
+    guard (0 < |bits| < 0x2000, i.e. 0 < |v| < 2^-63), and the guard catches
+    nothing else but values below 2^-63."""
+    import numpy as np
+    b = np.arange(1 << 16, dtype=np.uint32)
+    v = (b << 16).view(np.float32)
+    fin = np.isfinite(v)
+    with np.errstate(over="ignore"):
+        sq32 = (v[fin] * v[fin]).astype(np.float32)                   # RN(v*v) in binary32
+        sq64 = v[fin].astype(np.float64) ** 2                        # exact (16-bit significand)
+        exact = np.ones(b.size, bool)
+        exact[fin] = (sq32.astype(np.float64) == sq64) | np.isinf(sq32)   # overflow: inf either way
+    guard = ((b & 0x7FFF) - 1) < 0x1FFF                               # the kernel's predicate, per half word
+    assert not np.any(~exact & ~guard), "a square that is not exact escapes the guard"
+    assert np.all(np.abs(v[guard]) < 2.0 ** -63) and np.all(v[guard] != 0)
+    assert np.any(~exact)                                             # the guard is needed
 
 
 @pytest.mark.gpu
